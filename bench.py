@@ -1,0 +1,367 @@
+#!/usr/bin/env python
+"""Benchmark of the fused softplus MLP on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mlpk|reference]
+
+Headline workload (top of its batch sweep): the 3-layer
+D=H=OUT=128 softplus MLP forward on M = 4,194,304 rows per GPU, fp16 operands
+and fp32 accumulation, seeded synthetic inputs (x ~ N(0,1), W ~ U(+-1/sqrt(in))).
+A step is one forward over the whole batch.  With N > 1 (torchrun, one process
+per GPU) every rank runs its own M rows: the path shards by rows with no
+collective, so the scaling is weak and ``value`` = N*M*K / max-over-ranks time.
+
+Timing: W untimed warm-up steps, then K steps between CUDA events on the
+launching stream, bracketed by a barrier and a device synchronize; inputs
+(1 GiB x, 1 GiB out) are larger than L2, so no flush is needed.  SM clocks and
+throttle reasons are sampled through NVML during the timed region.
+
+``--impl reference`` times the reference's own PyTorch path (kernel.py:163-171,
+restated in oracle/cpu_baseline.py because the reference tree does not exist
+on the GPU box) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+BASELINE_METRIC = "fused MLP fwd rows/s & fwd+bwd rows/s vs roofline at M=1M-4M, 1-8 B200"
+DIMS = (128, 128, 128, 128)
+ROWS = 4 * 1024 * 1024
+BYTES_PER_ROW = 2 * (DIMS[0] + DIMS[-1])                     # x in + out out, fp16
+FLOP_PER_ROW = 2 * sum(a * b for a, b in zip(DIMS[:-1], DIMS[1:]))
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+FWD_KERNEL = "mlp_fwd_kernel"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="mlpk", choices=["mlpk", "reference"])
+    ap.add_argument("--rows", type=int, default=ROWS, help="rows per GPU")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", 0)) or None,
+                "source": "measured"}
+    except Exception:
+        return dict(FALLBACK_PEAKS)
+
+
+def load_traffic(name: str):
+    """dram bytes per launch recorded from an ncu capture in profiles/<name>.md
+    (a line `dram_bytes_per_launch: <int>`), or None."""
+    p = os.path.join(ROOT, "profiles", name + ".md")
+    try:
+        for line in open(p):
+            if line.strip().startswith("dram_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip()))
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------- clocks
+REASON_BITS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+    0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+}
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML in a thread."""
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples = []
+        self.period = period_s
+        self._stop = threading.Event()
+        self.ok = False
+        self.max_mhz = None
+        try:
+            import pynvml as nv
+
+            nv.nvmlInit()
+            self.nv = nv
+            import torch
+
+            props = torch.cuda.get_device_properties(device_index)
+            try:
+                bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+                self.h = nv.nvmlDeviceGetHandleByPciBusId_v2(bus)
+            except Exception:
+                self.h = nv.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.ok = False
+
+    def _reasons(self):
+        nv = self.nv
+        for fn in ("nvmlDeviceGetCurrentClocksEventReasons", "nvmlDeviceGetCurrentClocksThrottleReasons"):
+            if hasattr(nv, fn):
+                return getattr(nv, fn)(self.h)
+        return 0
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM), self._reasons()))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "note": "NVML unavailable" if not self.ok else "no samples"}
+        mhz = [s[0] for s in self.samples]
+        bits = 0
+        for _, r in self.samples:
+            bits |= int(r)
+        reasons = [n for b, n in REASON_BITS.items() if bits & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(mhz)}
+
+
+# ---------------------------------------------------------------------- CPU legs
+def cpu_forward_rows_per_s(rows: int, seconds: float):
+    """The reference's PyTorch forward (kernel.py:163-171) in fp32 on all host
+    threads, on a bounded sample of the workload (`rows` rows)."""
+    import torch
+
+    from oracle.cpu_baseline import model_forward, set_all_threads, time_rows_per_s
+    from mlp_megakernel_b200.synthetic import make_weights, make_x
+
+    cores = set_all_threads()
+    x = make_x(rows, DIMS[0], "normal", 0).float()
+    ws = [w.float() for w in make_weights(DIMS)]
+    with torch.no_grad():
+        rps, calls, dt = time_rows_per_s(lambda: model_forward(x, ws), rows, seconds)
+    return rps, cores, calls, dt
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # the CPU arm runs on rank 0 only
+    import torch
+
+    from oracle.cpu_baseline import model_forward, set_all_threads
+    from mlp_megakernel_b200.synthetic import make_weights, make_x
+
+    cores = set_all_threads()
+    sample = 65536
+    x = make_x(sample, DIMS[0], "normal", 0).float()
+    ws = [w.float() for w in make_weights(DIMS)]
+    with torch.no_grad():
+        for _ in range(max(args.warmup, 1)):
+            model_forward(x, ws)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            model_forward(x, ws)
+        dt = time.perf_counter() - t0
+    rps = sample * args.steps / dt
+    desc = (f"{sample} rows of the 3L128 forward per step (bounded sample of M={args.rows}), "
+            f"fp32 torch CPU, {cores} threads")
+    line = {
+        "impl": "reference", "metric": BASELINE_METRIC, "value": rps, "unit": "rows/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "3L128 fwd (kernel.py:163-171 Model on host CPU)",
+                   "dims": list(DIMS), "rows_per_step": sample, "device": "cpu"},
+        "cpu_baseline": {"value": rps, "unit": "rows/s", "cores": cores, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": rps, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------- GPU arm
+def run_mlpk(args):
+    import torch
+
+    from mlp_megakernel_b200 import _lib, fused_mlp_fwd
+    from mlp_megakernel_b200.synthetic import make_weights, make_x
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    M = args.rows
+    x = make_x(M, DIMS[0], "normal", rank, device="cuda")
+    ws = make_weights(DIMS, device="cuda")
+    _lib.device_status(clear=True)
+
+    step = lambda: fused_mlp_fwd(x, *ws)  # noqa: E731
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    status = _lib.device_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status} after the timed region")
+
+    # e2e through the public API: pinned host x -> device -> fused_mlp_fwd -> pinned host out
+    xh = x.cpu().pin_memory()
+    oh = torch.empty((M, DIMS[-1]), dtype=torch.float16, pin_memory=True)
+    xd = torch.empty_like(x)
+
+    def e2e_step():
+        xd.copy_(xh, non_blocking=True)
+        out = fused_mlp_fwd(xd, *ws)
+        oh.copy_(out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    clocks = clk.summary()
+    if dist is not None:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks = load_peaks()
+    per_launch_s = ms / 1e3 / args.steps
+    achieved_gbs = BYTES_PER_ROW * M / per_launch_s / 1e9
+    traffic = load_traffic("fwd_3L128_M4M")
+    value = world * M * args.steps / (ms / 1e3)
+    line = {
+        "metric": BASELINE_METRIC,
+        "value": value,
+        "unit": "rows/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": max(args.warmup, 3),
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 operands, f32 accumulate",
+        "data": "synthetic (seeded x~N(0,1), W~U(+-1/sqrt(in)))",
+        "config": {
+            "workload": "3L128 fwd: 3-layer softplus MLP D=H=OUT=128, M=4,194,304 rows per GPU "
+                        "(BASELINE config 2, top of the batch sweep)",
+            "dims": list(DIMS), "rows_per_gpu": M, "global_rows": world * M,
+            "parallelism": f"dp{world} (row-sharded, no collective)",
+            "l2": "inputs larger than L2 (x 1 GiB + out 1 GiB per GPU); no flush needed",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "achieved": achieved_gbs,
+            "peak": peaks["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": achieved_gbs / peaks["hbm_gbs"],
+            "traffic": traffic,
+            "peak_source": peaks["source"],
+            "algorithmic_bytes_per_row": BYTES_PER_ROW,
+            "kernel": FWD_KERNEL,
+            "tensor_tflops": FLOP_PER_ROW * M / per_launch_s / 1e12,
+            "tensor_frac_of_bf16_peak": FLOP_PER_ROW * M / per_launch_s / 1e12 / peaks["bf16_tflops"],
+        },
+        "e2e": {
+            "value": world * M * args.e2e_steps / (e2e_ms / 1e3),
+            "unit": "rows/s",
+            "h2d_bytes_per_step": M * DIMS[0] * 2,
+            "d2h_bytes_per_step": M * DIMS[-1] * 2,
+            "steps": args.e2e_steps,
+            "api": "mlp_megakernel_b200.fused_mlp_fwd with pinned host buffers",
+        },
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        rows = 65536
+        rps, cores, calls, dt = cpu_forward_rows_per_s(rows, args.cpu_seconds)
+        line["cpu_baseline"] = {
+            "value": rps, "unit": "rows/s", "cores": cores, "kind": "port",
+            "sample": f"{rows} rows of the 3L128 forward x {calls} calls ({dt:.1f} s), "
+                      f"reference PyTorch formula (kernel.py:163-171) in fp32 on {cores} threads",
+        }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_mlpk(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,70 @@
+/*
+ * mlpk -- B200 (sm_100a) fused softplus MLP, C ABI.
+ *
+ * The drop-in boundary for the reference's fused-MLP path
+ * (Marcelo5444/mlp-megakernel).  Every entry point takes plain device
+ * pointers, sizes and a CUDA stream; no torch types cross this boundary.  The
+ * Python package binds these symbols with ctypes (see INTEGRATION.md for the
+ * binding a maintainer of the reference would add).
+ *
+ * Conventions (mirroring the reference, kernel.py:130-156):
+ *   - weights are [in, out] row-major (out = x @ W), fp16;
+ *   - activations x / out / grad_out / dx are [M, d] row-major fp16;
+ *   - saved training activations and weight gradients are fp32;
+ *   - every pointer must be 16-byte aligned and tensors contiguous;
+ *   - all work is enqueued on `stream`; no entry point synchronises the host
+ *     (except mlpk_device_status, which reads a device word);
+ *   - return value: MLPK_OK or an MLPK_ERR_* code (mlpk_status_string).
+ */
+#ifndef MLPK_H_
+#define MLPK_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* mlpk_stream_t; /* a cudaStream_t */
+
+#define MLPK_MAX_LAYERS 8
+
+/* Network shape: num_layers GEMMs, dims[0] = in features, dims[num_layers] =
+ * out features, dims[1..num_layers-1] = hidden widths. */
+typedef struct mlpk_shape {
+  int32_t num_layers;
+  int32_t dims[MLPK_MAX_LAYERS + 1];
+} mlpk_shape;
+
+enum {
+  MLPK_OK = 0,
+  MLPK_ERR_SHAPE = 1,       /* dims/num_layers invalid or M < 0 */
+  MLPK_ERR_UNSUPPORTED = 2, /* no kernel built for this shape */
+  MLPK_ERR_ARCH = 3,        /* device is not sm_100 */
+  MLPK_ERR_CUDA = 4,        /* a CUDA runtime/driver call failed */
+  MLPK_ERR_ALIGN = 5,       /* a pointer is not 16-byte aligned */
+  MLPK_ERR_NULL = 6,        /* a required pointer is NULL */
+  MLPK_ERR_DEVICE = 7       /* a kernel recorded a device-side error */
+};
+
+/* Human-readable text for a status code. */
+const char* mlpk_status_string(int status);
+
+/* 1 if a kernel for this shape is compiled into the library, else 0. */
+int mlpk_shape_supported(const mlpk_shape* shape);
+
+/* Inference forward: out[M, dL] = MLP(x[M, d0]).
+ * Replaces _fused_mlp_fwd (kernel.py:130-156) / ModelNew.forward
+ * (kernel.py:174-180) and the 5-layer forward (README.md:9). */
+int mlpk_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W, void* out,
+             mlpk_stream_t stream);
+
+/* Reads (and optionally clears) the device-side status word of the current
+ * device: bit flags set by bounded waits that expired.  Synchronises. */
+int mlpk_device_status(int clear, int* status_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLPK_H_ */

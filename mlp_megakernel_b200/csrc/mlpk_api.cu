@@ -1,0 +1,211 @@
+// C-ABI entry points of libmlpk (declared in include/mlpk.h).
+//
+// Host responsibilities: validate shapes and pointers, encode the TMA tensor
+// maps (driver entry point fetched through the runtime, so the library does
+// not link libcuda), size the persistent grid from the SM count, and launch on
+// the caller's stream.  Nothing here allocates device memory or synchronises.
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/mlpk.h"
+#include "fwd_kernel.cuh"
+
+namespace {
+
+using mlpk::FwdCfg;
+using mlpk::FwdMaps;
+using mlpk::Net;
+
+// ------------------------------------------------------------------ device
+constexpr int kMaxDevices = 64;
+struct DevInfo {
+  int sm_count = 0;
+  int major = 0;
+  int minor = 0;
+  bool valid = false;
+};
+DevInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int current_device_info(DevInfo* out, int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MLPK_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DevInfo& d = g_dev[dev];
+  if (!d.valid) {
+    if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+      return MLPK_ERR_CUDA;
+    d.valid = true;
+  }
+  *out = d;
+  if (dev_out) *dev_out = dev;
+  return d.major == 10 ? MLPK_OK : MLPK_ERR_ARCH;
+}
+
+// ------------------------------------------------------------------ TMA maps
+using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
+EncodeFn get_encode() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  });
+  return fn;
+}
+
+// 2-D fp16 tensor [outer][inner] (inner contiguous), box {box_inner, box_outer},
+// swizzle chosen from the box's row pitch (box_inner * 2 bytes).
+int make_map_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer,
+                uint32_t box_inner, uint32_t box_outer) {
+  EncodeFn enc = get_encode();
+  if (!enc) return MLPK_ERR_CUDA;
+  const uint32_t pitch = box_inner * 2;
+  CUtensorMapSwizzle swz = pitch == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                           : pitch == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                         : CU_TENSOR_MAP_SWIZZLE_32B;
+  cuuint64_t gdim[2] = {inner, outer};
+  cuuint64_t gstride[1] = {inner * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), gdim, gstride,
+                   box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MLPK_OK : MLPK_ERR_CUDA;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------------ forward
+template <class NetT, int NS, int NEW>
+int launch_fwd(const void* x, const void* const* W, void* out, int64_t M, cudaStream_t st) {
+  using Cfg = FwdCfg<NetT, NS, NEW>;
+  constexpr int L = NetT::L;
+  DevInfo di;
+  int dev = 0;
+  int rc = current_device_info(&di, &dev);
+  if (rc != MLPK_OK) return rc;
+  if (M == 0) return MLPK_OK;
+  if (M > (int64_t(1) << 31) - 256) return MLPK_ERR_SHAPE;
+
+  FwdMaps<L> maps;
+  std::memset(&maps, 0, sizeof(maps));
+  rc = make_map_2d(&maps.x, x, Cfg::D0, M, mlpk::chunk_elems(Cfg::D0), mlpk::kTileM);
+  if (rc) return rc;
+  rc = make_map_2d(&maps.out, out, Cfg::DL, M, mlpk::chunk_elems(Cfg::DL), mlpk::kTileM);
+  if (rc) return rc;
+  int wrc = MLPK_OK;
+  mlpk::static_for<0, L>([&](auto lc) {
+    constexpr int l = decltype(lc)::value;
+    constexpr int K = NetT::template D<l>();
+    constexpr int N = NetT::template D<l + 1>();
+    if (wrc == MLPK_OK) wrc = make_map_2d(&maps.w[l], W[l], N, K, mlpk::chunk_elems(N), K);
+  });
+  if (wrc) return wrc;
+
+  auto kern = mlpk::mlp_fwd_kernel<NetT, NS, NEW>;
+  static bool attr_set[kMaxDevices] = {};
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg::SMEM_BYTES) != cudaSuccess)
+      return MLPK_ERR_CUDA;
+    attr_set[dev] = true;
+  }
+  const int num_tiles = static_cast<int>((M + mlpk::kTileM - 1) / mlpk::kTileM);
+  const int grid = num_tiles < di.sm_count ? num_tiles : di.sm_count;
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(maps, num_tiles);
+  return cudaGetLastError() == cudaSuccess ? MLPK_OK : MLPK_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------ dispatch
+template <int... Ds>
+bool shape_is(const mlpk_shape* s) {
+  constexpr int d[] = {Ds...};
+  constexpr int n = sizeof...(Ds);
+  if (s->num_layers != n - 1) return false;
+  for (int i = 0; i < n; ++i)
+    if (s->dims[i] != d[i]) return false;
+  return true;
+}
+
+using Fwd = int (*)(const void*, const void* const*, void*, int64_t, cudaStream_t);
+
+Fwd pick_fwd(const mlpk_shape* s) {
+  if (shape_is<128, 128, 128, 128>(s)) return &launch_fwd<Net<128, 128, 128, 128>, 2, 8>;
+  if (shape_is<32, 64, 64, 64, 64, 16>(s)) return &launch_fwd<Net<32, 64, 64, 64, 64, 16>, 2, 8>;
+  if (shape_is<64, 64, 64, 64>(s)) return &launch_fwd<Net<64, 64, 64, 64>, 2, 8>;
+  return nullptr;
+}
+
+int check_shape(const mlpk_shape* s) {
+  if (!s) return MLPK_ERR_NULL;
+  if (s->num_layers < 1 || s->num_layers > MLPK_MAX_LAYERS) return MLPK_ERR_SHAPE;
+  for (int i = 0; i <= s->num_layers; ++i)
+    if (s->dims[i] <= 0) return MLPK_ERR_SHAPE;
+  return MLPK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mlpk_status_string(int status) {
+  switch (status) {
+    case MLPK_OK: return "ok";
+    case MLPK_ERR_SHAPE: return "invalid shape";
+    case MLPK_ERR_UNSUPPORTED: return "no kernel compiled for this shape";
+    case MLPK_ERR_ARCH: return "device is not sm_100 (B200)";
+    case MLPK_ERR_CUDA: return "CUDA runtime/driver call failed";
+    case MLPK_ERR_ALIGN: return "pointer not 16-byte aligned";
+    case MLPK_ERR_NULL: return "required pointer is NULL";
+    case MLPK_ERR_DEVICE: return "kernel recorded a device-side error";
+    default: return "unknown status";
+  }
+}
+
+int mlpk_shape_supported(const mlpk_shape* shape) {
+  if (check_shape(shape) != MLPK_OK) return 0;
+  return pick_fwd(shape) != nullptr ? 1 : 0;
+}
+
+int mlpk_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W, void* out,
+             mlpk_stream_t stream) {
+  int rc = check_shape(shape);
+  if (rc) return rc;
+  if (M < 0) return MLPK_ERR_SHAPE;
+  if (!W) return MLPK_ERR_NULL;
+  if (M > 0 && (!x || !out)) return MLPK_ERR_NULL;
+  for (int l = 0; l < shape->num_layers; ++l) {
+    if (!W[l]) return MLPK_ERR_NULL;
+    if (!aligned16(W[l])) return MLPK_ERR_ALIGN;
+  }
+  if (!aligned16(x) || !aligned16(out)) return MLPK_ERR_ALIGN;
+  Fwd f = pick_fwd(shape);
+  if (!f) return MLPK_ERR_UNSUPPORTED;
+  return f(x, W, out, M, static_cast<cudaStream_t>(stream));
+}
+
+int mlpk_device_status(int clear, int* status_out) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, mlpk::g_device_status, sizeof(int)) != cudaSuccess)
+    return MLPK_ERR_CUDA;
+  if (status_out) *status_out = v;
+  if (clear) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(mlpk::g_device_status, &z, sizeof(int)) != cudaSuccess)
+      return MLPK_ERR_CUDA;
+  }
+  return MLPK_OK;
+}
+
+}  // extern "C"

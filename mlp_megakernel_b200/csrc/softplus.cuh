@@ -1,0 +1,50 @@
+// softplus(z) = log(1 + e^z) with beta = 1, threshold = 20 -- the activation of
+// the reference (F.softplus at kernel.py:169-170, written in the fused kernel
+// as where(z > 20, z, log(exp(z) + 1)) at kernel.py:108).
+//
+// Evaluated as max(z, 0) + log1p(e^{-|z|}), which equals the reference form
+// for every z (for z > 20 the log1p term is below 2.1e-9, under fp32's
+// resolution of z).  One MUFU op (ex2) per element; log1p(t) on t in (0, 1] is
+// t*q(t) with q a degree-5 polynomial on the FMA pipe.  The coefficients are
+// this project's own minimax fit (Remez exchange on the RELATIVE error) of
+// q(t) = log1p(t)/t on [0, 1]: max relative error 8.5e-6 in float32 Horner
+// form, 1/28 of fp16's half-ulp, so the fp16 value fed to the next GEMM
+// matches an exact softplus in > 99% of cases (the rest differ by one ulp).
+// Relative (not absolute) error matters because h = log1p(e^-|z|) is tiny for
+// very negative z.  Accuracy is checked against float64 log1p in
+// tests/test_softplus_poly.py.
+#pragma once
+#include "ptx.cuh"
+
+namespace mlpk {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kSpC0 = 0.9999915957450867f;
+constexpr float kSpC1 = -0.4993613660335541f;
+constexpr float kSpC2 = 0.3252066671848297f;
+constexpr float kSpC3 = -0.21004869043827057f;
+constexpr float kSpC4 = 0.10122228413820267f;
+constexpr float kSpC5 = -0.02386915124952793f;
+
+__device__ __forceinline__ float log1p_unit(float t) {  // t in [0, 1]
+  float q = kSpC5;
+  q = fmaf(q, t, kSpC4);
+  q = fmaf(q, t, kSpC3);
+  q = fmaf(q, t, kSpC2);
+  q = fmaf(q, t, kSpC1);
+  q = fmaf(q, t, kSpC0);
+  return q * t;
+}
+
+__device__ __forceinline__ float softplus_f32(float z) {
+  const float e = ex2_approx(fabsf(z) * -kLog2e);  // e^{-|z|} in (0, 1]
+  return fmaxf(z, 0.0f) + log1p_unit(e);
+}
+
+// d softplus / dz expressed through the post-activation h = softplus(z):
+// sigmoid(z) = 1 - e^{-h}  (mlp_fused.md:87-95).
+__device__ __forceinline__ float dsoftplus_from_h(float h) {
+  return 1.0f - ex2_approx(h * -kLog2e);
+}
+
+}  // namespace mlpk

@@ -1,0 +1,88 @@
+"""Functional API of the fused softplus MLP (forward).
+
+Mirrors the reference's functional surface:
+
+* ``_fused_mlp_fwd(x, w1, w2, w3)`` -- kernel.py:130-156 (same argument
+  meaning: x ``[M, K1]``, ``w_i`` ``[in, out]``, returns a new ``[M, N3]``
+  tensor in x's dtype; inputs are made contiguous first, as at kernel.py:132-133);
+* ``fused_mlp_fwd(x, *weights)`` -- the same for any depth (the 5-layer chain of
+  README.md:9);
+* ``ModelNew`` -- the nn.Module shim of kernel.py:174-180.
+
+Every call runs the sm_100a kernel in libmlpk through its C ABI on the current
+CUDA stream.  There is no CPU or PyTorch fallback: CPU tensors, unsupported
+dtypes or shapes raise.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    t = t.contiguous()
+    if t.data_ptr() % 16 != 0:
+        t = t.clone()
+    return t
+
+
+def _check_operands(x: torch.Tensor, weights) -> list:
+    if not isinstance(x, torch.Tensor) or x.dim() != 2:
+        raise ValueError("x must be a 2-D tensor [M, in_features]")
+    if not x.is_cuda:
+        raise RuntimeError("fused MLP runs on CUDA (sm_100) only; got a CPU tensor")
+    if x.dtype != torch.float16:
+        raise TypeError(f"fused MLP computes in fp16 (fp32 accumulate); got x.dtype={x.dtype}")
+    if len(weights) < 1:
+        raise ValueError("need at least one weight matrix")
+    dims = [x.shape[1]]
+    for i, w in enumerate(weights):
+        if w.dim() != 2 or w.device != x.device or w.dtype != x.dtype:
+            raise ValueError(f"weight {i} must be a 2-D {x.dtype} tensor on {x.device}")
+        if w.shape[0] != dims[-1]:
+            raise ValueError(
+                f"weight {i} has {w.shape[0]} input features, expected {dims[-1]} "
+                f"(weights are [in, out], out = x @ W)"
+            )
+        dims.append(w.shape[1])
+    return dims
+
+
+def fused_mlp_fwd(x: torch.Tensor, *weights: torch.Tensor) -> torch.Tensor:
+    """``softplus(...softplus(x @ W_0)...) @ W_{L-1}`` in one kernel launch.
+
+    Softplus is beta=1, threshold=20 (kernel.py:108); products accumulate in
+    fp32 and every hidden activation is rounded to fp16 before the next GEMM
+    (kernel.py:110, kernel.py:117).
+    """
+    dims = _check_operands(x, weights)
+    x = _aligned(x)
+    ws = [_aligned(w) for w in weights]
+    M = x.shape[0]
+    out = torch.empty((M, dims[-1]), device=x.device, dtype=x.dtype)
+    if M == 0:
+        return out
+    lib = _lib.lib()
+    shape = _lib.shape_struct(dims)
+    wptr = _lib.ptr_array([w.data_ptr() for w in ws])
+    with torch.cuda.device(x.device):
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        rc = lib.mlpk_fwd(ctypes.byref(shape), M, x.data_ptr(), wptr, out.data_ptr(), stream)
+    _lib.check("mlpk_fwd", rc)
+    return out
+
+
+def _fused_mlp_fwd(x, w1, w2, w3):
+    """3-layer inference forward -- drop-in for kernel.py:130-156."""
+    return fused_mlp_fwd(x, w1, w2, w3)
+
+
+class ModelNew(nn.Module):
+    """Fused 3-layer softplus MLP, weights passed per call (kernel.py:174-180)."""
+
+    def forward(self, x, w1, w2, w3):
+        return _fused_mlp_fwd(x, w1, w2, w3)

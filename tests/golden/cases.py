@@ -1,0 +1,44 @@
+"""Golden forward cases: names, seeds and input regeneration.
+
+The fixtures ``fwd_<name>.npz`` hold the outputs of the REFERENCE's own fused
+kernel on these inputs (made by make_golden.py); tests regenerate the inputs
+from the seeds below and check them against the recorded SHA-256 digests.
+"""
+from __future__ import annotations
+
+import torch
+
+from mlp_megakernel_b200.synthetic import make_weights, make_x
+
+
+# name -> (dims, M, x_dist, x_seed, weight scale, subsample_rows)
+CASES = {
+    # 3L128 forward at M=4096, x~N(0,1) seed 0, W~U(+-1/sqrt(in)) seed 1.
+    "cfg1_3L128_M4096": ((128, 128, 128, 128), 4096, "normal", 0, 1.0, 256),
+    # ragged batch sizes (tile = 128 rows): M=1, 127, 129, 300
+    "ragged_M1": ((128, 128, 128, 128), 1, "normal", 10, 1.0, 0),
+    "ragged_M127": ((128, 128, 128, 128), 127, "normal", 11, 1.0, 0),
+    "ragged_M129": ((128, 128, 128, 128), 129, "normal", 12, 1.0, 0),
+    "ragged_M300": ((128, 128, 128, 128), 300, "normal", 13, 1.0, 0),
+    # large |pre-activation|: weights x12 push z past the threshold (z > 20)
+    # and far below zero (softplus underflow side)
+    "large_preact_M256": ((128, 128, 128, 128), 256, "normal", 14, 12.0, 0),
+    # the reference's own benchmark distribution: x, W ~ 0.02*N(0,1) (profile.py:307-310)
+    "profile_dist_M512": ((128, 128, 128, 128), 512, "normal", 15, None, 0),
+    # wide 3-layer network D=H=OUT=256 (BASELINE config 5 shape), x seed 4
+    "w256_M384": ((256, 256, 256, 256), 384, "normal", 4, 1.0, 0),
+    # narrow 3-layer network D=H=OUT=64
+    "d64_M200": ((64, 64, 64, 64), 200, "normal", 16, 1.0, 0),
+}
+
+
+def make_case_inputs(dims, M, dist, seed, scale):
+    """Regenerate a case's fp16 inputs from its seeds (used by the tests too)."""
+    x = make_x(M, dims[0], dist, seed)
+    if scale is None:  # profile.py:307-310 distribution
+        g = torch.Generator().manual_seed(seed + 1000)
+        x = (torch.randn(M, dims[0], generator=g) * 0.02).half()
+        ws = [(torch.randn(i, o, generator=g) * 0.02).half() for i, o in zip(dims[:-1], dims[1:])]
+    else:
+        ws = [(w.float() * scale).half() for w in make_weights(dims)]
+    return x, ws

@@ -1,0 +1,74 @@
+"""CPU tests of the C ABI: libmlpk.so builds, loads without a GPU, exports
+every function declared in include/mlpk.h, and validates arguments before it
+touches the device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from mlp_megakernel_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_functions():
+    names = []
+    for hdr in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if hdr.endswith(".h"):
+            txt = open(os.path.join(ROOT, "include", hdr)).read()
+            txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+            names += re.findall(r"\b(mlpk_[a-z0-9_]+)\s*\(", txt)
+    return sorted(set(names))
+
+
+def test_header_declares_entry_points():
+    names = _declared_functions()
+    assert "mlpk_fwd" in names and "mlpk_status_string" in names
+
+
+def test_library_exports_every_declared_symbol(built_lib):
+    for name in _declared_functions():
+        assert hasattr(built_lib, name), f"libmlpk.so does not export {name}"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature in _lib.SIGNATURES"
+
+
+def test_status_strings(built_lib):
+    assert _lib.status_string(0) == "ok"
+    for code in range(1, 8):
+        assert _lib.status_string(code) != "unknown status"
+
+
+@pytest.mark.parametrize("dims,ok", [
+    ((128, 128, 128, 128), True),
+    ((32, 64, 64, 64, 64, 16), True),
+    ((64, 64, 64, 64), True),
+    ((128, 96, 128, 128), False),
+])
+def test_shape_supported(built_lib, dims, ok):
+    assert _lib.shape_supported(dims) == ok
+
+
+def test_fwd_rejects_bad_arguments_without_touching_the_device(built_lib):
+    lib = built_lib
+    shape = _lib.shape_struct((128, 128, 128, 128))
+    w = _lib.ptr_array([256, 512, 768])
+    # NULL shape
+    assert lib.mlpk_fwd(None, 16, 256, w, 512, None) == 6
+    # negative M
+    assert lib.mlpk_fwd(ctypes.byref(shape), -1, 256, w, 512, None) == 1
+    # NULL weight pointer
+    wn = _lib.ptr_array([256, 0, 768])
+    assert lib.mlpk_fwd(ctypes.byref(shape), 16, 256, wn, 512, None) == 6
+    # misaligned x
+    assert lib.mlpk_fwd(ctypes.byref(shape), 16, 258, w, 512, None) == 5
+    # unsupported shape
+    bad = _lib.MlpkShape()
+    bad.num_layers = 3
+    for i, d in enumerate((128, 96, 128, 128)):
+        bad.dims[i] = d
+    assert lib.mlpk_fwd(ctypes.byref(bad), 16, 256, w, 512, None) == 2
+    # zero layers
+    z = _lib.MlpkShape()
+    z.num_layers = 0
+    assert lib.mlpk_fwd(ctypes.byref(z), 16, 256, w, 512, None) == 1
