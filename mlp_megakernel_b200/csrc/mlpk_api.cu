@@ -87,9 +87,9 @@ int make_map_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t oute
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ------------------------------------------------------------------ forward
-template <class NetT, int NS, int NEW>
+template <class NetT, int NS, int EPW>
 int launch_fwd(const void* x, const void* const* W, void* out, int64_t M, cudaStream_t st) {
-  using Cfg = FwdCfg<NetT, NS, NEW>;
+  using Cfg = FwdCfg<NetT, NS, EPW>;
   constexpr int L = NetT::L;
   DevInfo di;
   int dev = 0;
@@ -113,7 +113,7 @@ int launch_fwd(const void* x, const void* const* W, void* out, int64_t M, cudaSt
   });
   if (wrc) return wrc;
 
-  auto kern = mlpk::mlp_fwd_kernel<NetT, NS, NEW>;
+  auto kern = mlpk::mlp_fwd_kernel<NetT, NS, EPW>;
   static bool attr_set[kMaxDevices] = {};
   if (!attr_set[dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,

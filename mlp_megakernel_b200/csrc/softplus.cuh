@@ -41,6 +41,21 @@ __device__ __forceinline__ float softplus_f32(float z) {
   return fmaxf(z, 0.0f) + log1p_unit(e);
 }
 
+// Two softplus evaluations with packed f32x2 arithmetic (sm_100 FFMA2 /
+// FMUL2: one instruction for both lanes); same formula and coefficients as
+// softplus_f32, with the last Horner step fused with the relu term:
+// h = q(e) * e + max(z, 0).
+__device__ __forceinline__ float2 softplus_x2(float2 z) {
+  const float2 s = __fmul2_rn(z, make_float2(kLog2e, kLog2e));
+  const float2 e = make_float2(ex2_approx(-fabsf(s.x)), ex2_approx(-fabsf(s.y)));  // e^{-|z|}
+  float2 q = __ffma2_rn(make_float2(kSpC5, kSpC5), e, make_float2(kSpC4, kSpC4));
+  q = __ffma2_rn(q, e, make_float2(kSpC3, kSpC3));
+  q = __ffma2_rn(q, e, make_float2(kSpC2, kSpC2));
+  q = __ffma2_rn(q, e, make_float2(kSpC1, kSpC1));
+  q = __ffma2_rn(q, e, make_float2(kSpC0, kSpC0));
+  return __ffma2_rn(q, e, make_float2(fmaxf(z.x, 0.0f), fmaxf(z.y, 0.0f)));
+}
+
 // d softplus / dz expressed through the post-activation h = softplus(z):
 // sigmoid(z) = 1 - e^{-h}  (mlp_fused.md:87-95).
 __device__ __forceinline__ float dsoftplus_from_h(float h) {

@@ -17,14 +17,19 @@ def _coeffs():
 
 
 def _device_softplus_f32(z):
+    """float32 model of softplus_x2: e = 2^(-|z*log2e|), q by Horner (FFMA),
+    h = fma(q, e, max(z, 0)) (one rounding)."""
     z = z.astype(np.float32)
     c = [np.float32(v) for v in _coeffs()]
+    s = (z * np.float32(1.4426950408889634)).astype(np.float32)
     # ex2.approx has ~2^-22 relative error; model it with the exact value
-    e = np.exp(-np.abs(z).astype(np.float64)).astype(np.float32)
+    e = np.exp2(-np.abs(s).astype(np.float64)).astype(np.float32)
     q = c[5]
     for k in (4, 3, 2, 1, 0):
-        q = (q * e + c[k]).astype(np.float32)
-    return (np.maximum(z, np.float32(0)) + (q * e).astype(np.float32)).astype(np.float32)
+        q = (q.astype(np.float64) * e + c[k]).astype(np.float32) if hasattr(q, "astype") else \
+            np.float32(np.float64(q) * e.astype(np.float64) + c[k])
+    h = q.astype(np.float64) * e.astype(np.float64) + np.maximum(z, np.float32(0)).astype(np.float64)
+    return h.astype(np.float32)
 
 
 def _softplus_f64(z):
