@@ -15,15 +15,21 @@
 //    shared memory ONCE per CTA, then streams x tiles into an NS-deep ring.
 //  * warp 1: allocates TMEM; one lane issues tcgen05.mma (M=128, N=d_{l+1},
 //    K=16 steps) for every layer of every tile; fp32 accumulators live in TMEM
-//    (one accumulator region per slot, reused by all layers of that slot).
+//    (two accumulator buffers per slot, alternating between layers, so layer
+//    l+1 accumulates while the epilogue still drains layer l).
 //  * warps 2..2+NS*EPW-1: epilogue, EPW warps per slot.  tcgen05.ld the
 //    accumulator (warp w owns TMEM lanes 32*(w%4)..+31 = tile rows; the slot's
 //    EPW/4 column groups split the columns), softplus in fp32 registers with
-//    packed f32x2 math, cast to fp16 and st.shared straight into the next
-//    layer's K-major, swizzled A operand; for the last layer the fp16 result is
-//    staged in the same buffer and written by TMA stores (OOB rows of the last
-//    tile are clipped by TMA).  TMEM loads are software-pipelined: the next 32
-//    columns are in flight while the current 32 are computed.
+//    packed f32x2 math, cast to fp16 and tcgen05.st the activation back into
+//    TMEM, packed two per column over the accumulator columns it has consumed.
+//    The next layer's UMMA takes that activation as its A operand straight from
+//    TMEM (kind::f16 with [a_tmem]), so a hidden-layer UMMA reads only its
+//    weight tile from shared memory -- an SS UMMA at M=N=128 needs the whole
+//    shared-memory bandwidth and runs at about half the tensor rate.  For the
+//    last layer the fp16 result is staged in shared memory and written by TMA
+//    stores (OOB rows of the last tile are clipped by TMA).  TMEM loads are
+//    software-pipelined: the next 32 columns are in flight while the current 32
+//    are computed.
 //  * No activation touches HBM: HBM traffic is x in, out out (plus weights once
 //    per CTA from L2).
 //  * Hand-offs are mbarriers; all waits are bounded (ptx.cuh).
@@ -95,11 +101,11 @@ struct FwdCfg {
   static constexpr int DL = NetT::template D<L>();
   static constexpr int HMAX = NetT::max_hidden_or_out();
   static constexpr int X_BYTES = align_up(tile_bytes(kTileM, D0), 1024);
-  static constexpr int H_BYTES = align_up(tile_bytes(kTileM, HMAX), 1024);
+  static constexpr int O_BYTES = align_up(tile_bytes(kTileM, DL), 1024);  // out staging
   static constexpr int W_TOTAL = NetT::w_total();
   static constexpr int OFF_X = W_TOTAL;
-  static constexpr int OFF_H = OFF_X + NS * X_BYTES;
-  static constexpr int OFF_BAR = OFF_H + NS * H_BYTES;
+  static constexpr int OFF_O = OFF_X + NS * X_BYTES;
+  static constexpr int OFF_BAR = OFF_O + NS * O_BYTES;
   static constexpr int CHUNK = 32;                       // columns per h hand-off chunk
   static constexpr int MAXCH = (HMAX + CHUNK - 1) / CHUNK;  // chunks per layer, max
   // x_full, x_empty, acc_full, out_ready, store_free per slot; MAXCH h-chunk
@@ -124,75 +130,94 @@ struct FwdCfg {
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
 };
 
-// Converts CH fp32 accumulator values (columns col..col+CH-1 of row `row`) to
-// fp16 -- through softplus when ACT -- and stores them as CH/8 16-byte units
-// into an operand tile of extent N stored as swizzled chunks (layout.cuh).
-template <int N, int CH, bool ACT>
-__device__ __forceinline__ void emit_cols(const uint32_t (&r)[CH], uint32_t tile_base,
-                                          uint32_t row, int col) {
-  constexpr int C = chunk_elems(N);
-  constexpr int P = pitch_bytes(N);
+// TMEM column (relative to the accumulator buffer) where the fp16 activation
+// of accumulator column `col` is stored: each of the NG column groups packs its
+// NCOL columns two per 32-bit TMEM column at the start of its own range.
+template <int NCOL>
+__host__ __device__ constexpr int h_tmem_col(int col) {
+  return (col / NCOL) * NCOL + (col % NCOL) / 2;
+}
+
+// Packs 2*NP fp32 values to NP half2 words, through softplus when ACT.
+template <int NP, bool ACT>
+__device__ __forceinline__ void pack_cols(const uint32_t* r, uint32_t* w) {
 #pragma unroll
-  for (int u = 0; u < CH / 8; ++u) {
-    const int cc = col + 8 * u;
-    uint32_t w[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float2 z = make_float2(__uint_as_float(r[8 * u + 2 * j]), __uint_as_float(r[8 * u + 2 * j + 1]));
-      if constexpr (ACT) z = softplus_x2(z);
-      w[j] = pack_half2(z.x, z.y);
-    }
-    st_shared_v4(tile_base + (cc / C) * (kTileM * P) + swz_off<P>(row, (cc % C) / 8), w[0], w[1],
-                 w[2], w[3]);
+  for (int j = 0; j < NP; ++j) {
+    float2 z = make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+    if constexpr (ACT) z = softplus_x2(z);
+    w[j] = pack_half2(z.x, z.y);
   }
 }
 
-// Publishes one finished chunk of h: the smem writes become visible to the
-// tensor core (async proxy), the chunk's TMEM reads are ordered before any
-// later MMA, and lane 0 arrives on the chunk's barrier (count: 4 warps).
+// Publishes one finished chunk of h to the MMA issuer: the TMEM stores are
+// complete and ordered (with this chunk's TMEM loads) before the arrive.
 __device__ __forceinline__ void publish_chunk(uint32_t bar) {
-  fence_proxy_async_smem();
+  tmem_wait_st();
   tc_fence_before();
   __syncwarp();
   if (lane_id() == 0) mbar_arrive(bar);
 }
 
-// One epilogue job of one warp: NCOL accumulator columns starting at TMEM
-// address taddr (lane field = the warp's quarter) -> fp16 operand tile.  For a
-// hidden layer (PUB) every 32 finished columns are published on
-// chunk_bar0 + 8*(chunk index) so the next layer's MMA can start on them.
-// Inlined; the epilogue calls it from one runtime loop over the hidden layers
-// and once for the output layer, so the kernel holds two copies.
-template <int N, int NCOL, bool ACT, bool PUB>
-__device__ __forceinline__ void epi_job(uint32_t taddr, uint32_t tile_base, uint32_t row, int col0,
-                                     uint32_t chunk_bar0) {
-  static_assert(!PUB || NCOL % 32 == 0,
-                "hidden widths must give every column group whole 32-column chunks");
-  if constexpr (NCOL == 8) {
-    uint32_t r[8];
-    tmem_ld_wait_x8(taddr, r);
-    emit_cols<N, 8, ACT>(r, tile_base, row, col0);
-    if constexpr (PUB) publish_chunk(chunk_bar0 + 8 * (col0 / 32));
-  } else if constexpr (NCOL == 16) {
-    uint32_t r[16];
-    tmem_ld_wait_x16(taddr, r);
-    emit_cols<N, 16, ACT>(r, tile_base, row, col0);
-    if constexpr (PUB) publish_chunk(chunk_bar0 + 8 * (col0 / 32));
+// Hidden-layer job of one warp: NCOL accumulator columns starting at column
+// col0 of the buffer at TMEM address tbuf (lane field = the warp's quarter)
+// -> softplus -> fp16 back into TMEM at h_tmem_col(), publishing every 32
+// finished columns on chunk_bar0 + 8*(col/32).  A column is always loaded
+// before the packed activation overwrites it: packed column col/2 (within the
+// group) is below col, and the async load of the next 32 columns is issued
+// before this chunk's store.
+template <int NCOL>
+__device__ __forceinline__ void hidden_job(uint32_t tbuf, int col0, uint32_t chunk_bar0) {
+  if constexpr (NCOL < 32) {
+    static_assert(NCOL == 8 || NCOL == 16, "unsupported width");
+    uint32_t r[NCOL], w[NCOL / 2];
+    if constexpr (NCOL == 16) tmem_ld_wait_x16(tbuf + col0, r);
+    else tmem_ld_wait_x8(tbuf + col0, r);
+    pack_cols<NCOL / 2, true>(r, w);
+    if constexpr (NCOL == 16) tmem_st_x8(tbuf + h_tmem_col<NCOL>(col0), w);
+    else tmem_st_x4(tbuf + h_tmem_col<NCOL>(col0), w);
+    publish_chunk(chunk_bar0 + 8 * (col0 / 32));
   } else {
     static_assert(NCOL % 32 == 0, "columns per thread: 8, 16 or a multiple of 32");
     uint32_t a[32];
-    tmem_ld_wait_x32(taddr, a);
+    tmem_ld_wait_x32(tbuf + col0, a);
 #pragma unroll
     for (int c = 0; c < NCOL; c += 32) {
       uint32_t b[32];
-      if (c + 32 < NCOL) tmem_ld_async_x32(taddr + c + 32, b);
-      emit_cols<N, 32, ACT>(a, tile_base, row, col0 + c);
-      if constexpr (PUB) publish_chunk(chunk_bar0 + 8 * ((col0 + c) / 32));
+      if (c + 32 < NCOL) tmem_ld_async_x32(tbuf + col0 + c + 32, b);
+      uint32_t w[16];
+      pack_cols<16, true>(a, w);
+      tmem_st_x16(tbuf + h_tmem_col<NCOL>(col0 + c), w);
+      publish_chunk(chunk_bar0 + 8 * ((col0 + c) / 32));
       if (c + 32 < NCOL) {
         tmem_wait_ld_bind_x32(b);
 #pragma unroll
         for (int i = 0; i < 32; ++i) a[i] = b[i];
       }
+    }
+  }
+}
+
+// Output-layer job of one warp: NCOL accumulator columns -> fp16 -> the
+// swizzled smem staging tile of extent N (TMA-store layout, layout.cuh).
+template <int N, int NCOL>
+__device__ __forceinline__ void out_job(uint32_t tbuf, uint32_t tile_base, uint32_t row, int col0) {
+  constexpr int C = chunk_elems(N);
+  constexpr int P = pitch_bytes(N);
+  constexpr int CH = NCOL < 32 ? NCOL : 32;
+  static_assert(NCOL % CH == 0 && CH % 8 == 0, "unsupported width");
+#pragma unroll
+  for (int c = 0; c < NCOL; c += CH) {
+    uint32_t r[CH];
+    if constexpr (CH == 32) tmem_ld_wait_x32(tbuf + col0 + c, r);
+    if constexpr (CH == 16) tmem_ld_wait_x16(tbuf + col0 + c, r);
+    if constexpr (CH == 8) tmem_ld_wait_x8(tbuf + col0 + c, r);
+#pragma unroll
+    for (int u = 0; u < CH / 8; ++u) {
+      uint32_t w[4];
+      pack_cols<4, false>(r + 8 * u, w);
+      const int cc = col0 + c + 8 * u;
+      st_shared_v4(tile_base + (cc / C) * (kTileM * P) + swz_off<P>(row, (cc % C) / 8), w[0],
+                   w[1], w[2], w[3]);
     }
   }
 }
@@ -209,14 +234,14 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
 
   const uint32_t s_w = sbase;
   const uint32_t s_x = sbase + Cfg::OFF_X;
-  const uint32_t s_h = sbase + Cfg::OFF_H;
+  const uint32_t s_o = sbase + Cfg::OFF_O;
   const uint32_t s_bar = sbase + Cfg::OFF_BAR;
   auto bar_x_full = [&](int s) { return s_bar + 8u * s; };
   auto bar_x_empty = [&](int s) { return s_bar + 8u * (NS + s); };
   auto bar_acc_full = [&](int s) { return s_bar + 8u * (2 * NS + s); };
   auto bar_out_ready = [&](int s) { return s_bar + 8u * (3 * NS + s); };
   auto bar_store_free = [&](int s) { return s_bar + 8u * (4 * NS + s); };
-  // h chunk c of slot s: columns [32c, 32c+32) of the activation in hbuf[s]
+  // h chunk c of slot s: activation columns [32c, 32c+32), packed in TMEM
   auto bar_chunk = [&](int s, int c) { return s_bar + 8u * (5 * NS + s * Cfg::MAXCH + c); };
   const uint32_t bar_w_full = s_bar + 8u * (5 * NS + NS * Cfg::MAXCH);
   const uint32_t bar_mma_done = bar_w_full + 8u;
@@ -308,69 +333,83 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
     // slot, so layer l+1 can run while the epilogue still reads layer l.
     // Layer 0 consumes the whole x tile; layer l >= 1 consumes h_{l-1} chunk by
     // chunk as the epilogue publishes it (fixed order -> deterministic sums).
-    if (lane == 0) {
-      bool ok = mbar_wait(bar_w_full, 0, abort_flag, kDevTimeoutMma);
-      tc_fence_after();
-      for (int i = 0; ok; ++i) {
-        if (tile_of(i, 0) >= num_tiles) break;
-        static_for<0, L>([&](auto lc) {
-          constexpr int l = decltype(lc)::value;
-          constexpr int K = NetT::template D<l>();
-          constexpr int N = NetT::template D<l + 1>();
-          constexpr uint32_t idesc = make_idesc_f16(kTileM, N, 0, 1);
-          const uint32_t b_base = s_w + NetT::template w_off<l>();
+    // The whole warp runs the loop (waits and descriptors are warp-uniform, so
+    // they live in uniform registers); lane 0 issues the tcgen05 instructions.
+    const bool issuer = (lane == 0);
+    bool ok = __all_sync(0xffffffffu, mbar_wait(bar_w_full, 0, abort_flag, kDevTimeoutMma));
+    tc_fence_after();
+    for (int i = 0; ok; ++i) {
+      if (tile_of(i, 0) >= num_tiles) break;
+      static_for<0, L>([&](auto lc) {
+        constexpr int l = decltype(lc)::value;
+        constexpr int K = NetT::template D<l>();
+        constexpr int N = NetT::template D<l + 1>();
+        constexpr uint32_t idesc = make_idesc_f16(kTileM, N, 0, 1);
+        const uint64_t bdesc0 = mnmajor_base_desc<K, N>(s_w + NetT::template w_off<l>());
 #pragma unroll
-          for (int s = 0; s < NS; ++s) {
-            if (!ok || tile_of(i, s) >= num_tiles) break;
-            const uint32_t d_tmem = tmem_base + (2 * s + ((i * L + l) & 1)) * Cfg::SLOT_COLS;
-            if constexpr (l == 0) {
-              ok = mbar_wait(bar_x_full(s), i & 1, abort_flag, kDevTimeoutMma);
-              if (!ok) break;
-              tc_fence_after();
-              const uint32_t a_base = s_x + s * Cfg::X_BYTES;
+        for (int s = 0; s < NS; ++s) {
+          if (!ok || tile_of(i, s) >= num_tiles) break;
+          const uint32_t d_tmem = tmem_base + (2 * s + ((i * L + l) & 1)) * Cfg::SLOT_COLS;
+          if constexpr (l == 0) {
+            ok = __all_sync(0xffffffffu,
+                            mbar_wait(bar_x_full(s), i & 1, abort_flag, kDevTimeoutMma));
+            if (!ok) break;
+            tc_fence_after();
+            const uint64_t adesc0 = kmajor_base_desc<K>(s_x + s * Cfg::X_BYTES);
+            if (issuer) {
 #pragma unroll
               for (int k = 0; k < K / 16; ++k)
-                umma_f16(d_tmem, kmajor_desc<kTileM, K>(a_base, k), mnmajor_desc<K, N>(b_base, k),
-                         idesc, k > 0 ? 1u : 0u);
+                umma_f16(d_tmem, adesc0 + (kmajor_koff<kTileM, K>(k) >> 4),
+                         bdesc0 + (mnmajor_koff<N>(k) >> 4), idesc, k > 0 ? 1u : 0u);
               umma_commit(bar_x_empty(s));
-            } else {
-              // chunks of h_{l-1}: 32 columns each, produced by column group g
-              // as its sub-chunk j; consume sub-chunk-major (both groups' first
-              // halves first).
-              constexpr int KC = K < 32 ? K : 32;        // columns per chunk
-              constexpr int NCH = K / KC;                 // chunks of this input
-              constexpr int NGRP = Cfg::NG;               // producer column groups
-              constexpr int SUBS = NCH / NGRP > 0 ? NCH / NGRP : 1;
-              const uint32_t a_base = s_h + s * Cfg::H_BYTES;
-              const uint32_t par = (i * (L - 1) + l - 1) & 1;
-              int issued = 0;
+            }
+            __syncwarp();
+          } else {
+            // chunks of h_{l-1}: 32 columns each, produced by column group g
+            // as its sub-chunk j; consume sub-chunk-major (both groups' first
+            // halves first).  A comes from TMEM: the previous job's buffer,
+            // where the epilogue packed h_{l-1} (h_tmem_col).
+            constexpr int KC = K < 32 ? K : 32;        // columns per chunk
+            constexpr int NCH = K / KC;                 // chunks of this input
+            constexpr int NGRP = Cfg::NG;               // producer column groups
+            constexpr int SUBS = NCH / NGRP > 0 ? NCH / NGRP : 1;
+            constexpr int PCOL = K / NGRP;              // producer columns per group
+            const uint32_t a_tmem = tmem_base + (2 * s + ((i * L + l - 1) & 1)) * Cfg::SLOT_COLS;
+            const uint32_t par = (i * (L - 1) + l - 1) & 1;
 #pragma unroll
-              for (int j = 0; j < SUBS; ++j) {
+            for (int j = 0; j < SUBS; ++j) {
 #pragma unroll
-                for (int g = 0; g < NGRP; ++g) {
-                  const int c = g * SUBS + j;
-                  if (c >= NCH) continue;
-                  ok = mbar_wait(bar_chunk(s, c), par, abort_flag, kDevTimeoutMma);
-                  if (!ok) break;
-                  tc_fence_after();
+              for (int g = 0; g < NGRP; ++g) {
+                const int c = g * SUBS + j;
+                if (c >= NCH) continue;
+                ok = __all_sync(0xffffffffu,
+                                mbar_wait(bar_chunk(s, c), par, abort_flag, kDevTimeoutMma));
+                if (!ok) break;
+                tc_fence_after();
+                if (issuer) {
 #pragma unroll
                   for (int kk = 0; kk < KC / 16; ++kk) {
                     const int k = c * (KC / 16) + kk;
-                    umma_f16(d_tmem, kmajor_desc<kTileM, K>(a_base, k),
-                             mnmajor_desc<K, N>(b_base, k), idesc, issued > 0 ? 1u : 0u);
-                    ++issued;
+                    umma_f16_ts(d_tmem, a_tmem + h_tmem_col<PCOL>(16 * k),
+                                bdesc0 + (mnmajor_koff<N>(k) >> 4), idesc,
+                                (j == 0 && g == 0 && kk == 0) ? 0u : 1u);
                   }
                 }
-                if (!ok) break;
+                __syncwarp();
               }
               if (!ok) break;
             }
-            umma_commit(bar_acc_full(s));
+            if (!ok) break;
           }
-        });
-      }
-      // Drain: all issued MMAs complete before TMEM is freed.
-      umma_commit(bar_mma_done);
+          if (issuer) umma_commit(bar_acc_full(s));
+          __syncwarp();
+        }
+      });
+    }
+    // Drain: all issued MMAs complete before TMEM is freed.
+    if (issuer) umma_commit(bar_mma_done);
+    __syncwarp();
+    {
       volatile int no_abort = 0;
       mbar_wait(bar_mma_done, 0, &no_abort, kDevTimeoutMma);
     }
@@ -384,7 +423,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
     const int grp = ew >> 2;           // column group
     const uint32_t row = q * 32 + lane;
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + 2 * s * Cfg::SLOT_COLS;
-    const uint32_t hbuf = s_h + s * Cfg::H_BYTES;
+    const uint32_t obuf = s_o + s * Cfg::O_BYTES;
     const bool leader = (ew == 0 && lane == 0);
     bool ok = true;
     constexpr int H = Cfg::H;
@@ -401,7 +440,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
         if (!ok) break;
         tc_fence_after();
         if (l == 0 && i > 0) {
-          // hbuf may still be the source of this slot's previous TMA store:
+          // obuf may still be the source of this slot's previous TMA store:
           // the leader waits for that store to finish reading, then frees it.
           if (leader) {
             bulk_wait_group_read<0>();
@@ -413,11 +452,10 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
           if (!ok) break;
         }
         const uint32_t t_buf = t_lane + ((i * L + l) & 1) * Cfg::SLOT_COLS;
-        epi_job<H, NCOL_H, true, true>(t_buf + grp * NCOL_H, hbuf, row, grp * NCOL_H,
-                                       bar_chunk(s, 0));
+        hidden_job<NCOL_H>(t_buf, grp * NCOL_H, bar_chunk(s, 0));
       }
       if (!ok) break;
-      // output layer: fp16 result staged in hbuf, written by TMA
+      // output layer: fp16 result staged in obuf, written by TMA
       {
         constexpr int l = L - 1;
         ok = __all_sync(0xffffffffu, mbar_wait(bar_acc_full(s), (i * L + l) & 1, abort_flag,
@@ -425,7 +463,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
         if (!ok) break;
         tc_fence_after();
         const uint32_t t_buf = t_lane + ((i * L + l) & 1) * Cfg::SLOT_COLS;
-        epi_job<Cfg::DL, NCOL_O, false, false>(t_buf + grp * NCOL_O, hbuf, row, grp * NCOL_O, 0);
+        out_job<Cfg::DL, NCOL_O>(t_buf, obuf, row, grp * NCOL_O);
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
@@ -437,7 +475,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
           constexpr int P = pitch_bytes(Cfg::DL);
 #pragma unroll
           for (int c = 0; c < Cfg::DL / C; ++c)
-            tma_store_2d(&maps.out, hbuf + c * kTileM * P, c * C, t * kTileM);
+            tma_store_2d(&maps.out, obuf + c * kTileM * P, c * C, t * kTileM);
           bulk_commit_group();
         }
       }

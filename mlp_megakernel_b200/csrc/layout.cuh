@@ -56,6 +56,30 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, int a_mn_maj
          | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Byte offset of K-step `k` (16 elements of K) inside a K-major operand with
+// `ROWS` rows and K extent `KEXT` (see the chunk layout above).
+template <int ROWS, int KEXT>
+__host__ __device__ constexpr uint32_t kmajor_koff(int k) {
+  return (k * 16 / chunk_elems(KEXT)) * (ROWS * pitch_bytes(KEXT)) +
+         (k * 16 % chunk_elems(KEXT)) * 2;
+}
+// Byte offset of K-step `k` inside an MN-major operand [K rows][NEXT cols].
+template <int NEXT>
+__host__ __device__ constexpr uint32_t mnmajor_koff(int k) {
+  return k * 16 * pitch_bytes(NEXT);
+}
+// Base descriptors: the K-step descriptor is base + (koff >> 4) (the start
+// address field is the low 14 bits; operands live below 256 KB, no carry).
+template <int KEXT>
+__device__ __forceinline__ uint64_t kmajor_base_desc(uint32_t base) {
+  return make_sdesc(base, 16, 8 * pitch_bytes(KEXT), umma_layout_code(pitch_bytes(KEXT)));
+}
+template <int KROWS, int NEXT>
+__device__ __forceinline__ uint64_t mnmajor_base_desc(uint32_t base) {
+  return make_sdesc(base, KROWS * pitch_bytes(NEXT), 8 * pitch_bytes(NEXT),
+                    umma_layout_code(pitch_bytes(NEXT)));
+}
+
 // Descriptor for K-step `k` (16 elements of K) of a K-major operand with
 // `rows` rows and K extent `kext`, stored as chunks (see above).
 template <int ROWS, int KEXT>
