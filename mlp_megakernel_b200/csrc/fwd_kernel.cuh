@@ -106,8 +106,10 @@ struct FwdCfg {
   static constexpr int OFF_X = W_TOTAL;
   static constexpr int OFF_O = OFF_X + NS * X_BYTES;
   static constexpr int OFF_BAR = OFF_O + NS * O_BYTES;
-  static constexpr int CHUNK = 32;                       // columns per h hand-off chunk
-  static constexpr int MAXCH = (HMAX + CHUNK - 1) / CHUNK;  // chunks per layer, max
+  // Hidden activations are handed to the MMA warp in chunks: a chunk is one
+  // 32-column stripe from every column group (32*NG columns); its barrier
+  // counts all EPW warps of the slot.
+  static constexpr int MAXCH = (HMAX / (EPW / 4) + 31) / 32;  // chunks per layer, max
   // x_full, x_empty, acc_full, out_ready, store_free per slot; MAXCH h-chunk
   // barriers per slot; w_full; mma_done
   static constexpr int NUM_BARS = 5 * NS + NS * MAXCH + 2;
@@ -131,12 +133,10 @@ struct FwdCfg {
 };
 
 // TMEM column (relative to the accumulator buffer) where the fp16 activation
-// of accumulator column `col` is stored: each of the NG column groups packs its
-// NCOL columns two per 32-bit TMEM column at the start of its own range.
-template <int NCOL>
-__host__ __device__ constexpr int h_tmem_col(int col) {
-  return (col / NCOL) * NCOL + (col % NCOL) / 2;
-}
+// of accumulator column `col` is stored: columns are processed in 32-column
+// stripes, and each stripe's activation is packed two per 32-bit TMEM column
+// into the first 16 columns of that stripe's own range.
+__host__ __device__ constexpr int h_tmem_col(int col) { return (col / 32) * 32 + (col % 32) / 2; }
 
 // Packs 2*NP fp32 values to NP half2 words, through softplus when ACT.
 template <int NP, bool ACT>
@@ -158,41 +158,33 @@ __device__ __forceinline__ void publish_chunk(uint32_t bar) {
   if (lane_id() == 0) mbar_arrive(bar);
 }
 
-// Hidden-layer job of one warp: NCOL accumulator columns starting at column
-// col0 of the buffer at TMEM address tbuf (lane field = the warp's quarter)
-// -> softplus -> fp16 back into TMEM at h_tmem_col(), publishing every 32
-// finished columns on chunk_bar0 + 8*(col/32).  A column is always loaded
-// before the packed activation overwrites it: packed column col/2 (within the
-// group) is below col, and the async load of the next 32 columns is issued
-// before this chunk's store.
-template <int NCOL>
-__device__ __forceinline__ void hidden_job(uint32_t tbuf, int col0, uint32_t chunk_bar0) {
-  if constexpr (NCOL < 32) {
-    static_assert(NCOL == 8 || NCOL == 16, "unsupported width");
-    uint32_t r[NCOL], w[NCOL / 2];
-    if constexpr (NCOL == 16) tmem_ld_wait_x16(tbuf + col0, r);
-    else tmem_ld_wait_x8(tbuf + col0, r);
-    pack_cols<NCOL / 2, true>(r, w);
-    if constexpr (NCOL == 16) tmem_st_x8(tbuf + h_tmem_col<NCOL>(col0), w);
-    else tmem_st_x4(tbuf + h_tmem_col<NCOL>(col0), w);
-    publish_chunk(chunk_bar0 + 8 * (col0 / 32));
-  } else {
-    static_assert(NCOL % 32 == 0, "columns per thread: 8, 16 or a multiple of 32");
-    uint32_t a[32];
-    tmem_ld_wait_x32(tbuf + col0, a);
+// Hidden-layer job of one warp of column group `grp` (of NG): stripes
+// grp, grp+NG, grp+2NG, ... (32 columns each) of the accumulator buffer at
+// TMEM address tbuf (lane field = the warp's quarter) -> softplus -> fp16 back
+// into TMEM at h_tmem_col(); after stripe j it arrives on chunk barrier j
+// (chunk_bar0 + 8j), which completes once all NG groups finished stripe j.  A
+// column is always loaded before the packed activation overwrites it: a
+// stripe's packed columns lie in its own range, and the async load of the
+// next stripe is issued before this stripe's store.
+template <int N, int NG>
+__device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chunk_bar0) {
+  static_assert(N % (32 * NG) == 0, "hidden width must be a multiple of 32 * column groups");
+  constexpr int SUBS = N / (32 * NG);
+  uint32_t a[32];
+  tmem_ld_wait_x32(tbuf + 32 * grp, a);
 #pragma unroll
-    for (int c = 0; c < NCOL; c += 32) {
-      uint32_t b[32];
-      if (c + 32 < NCOL) tmem_ld_async_x32(tbuf + col0 + c + 32, b);
-      uint32_t w[16];
-      pack_cols<16, true>(a, w);
-      tmem_st_x16(tbuf + h_tmem_col<NCOL>(col0 + c), w);
-      publish_chunk(chunk_bar0 + 8 * ((col0 + c) / 32));
-      if (c + 32 < NCOL) {
-        tmem_wait_ld_bind_x32(b);
+  for (int j = 0; j < SUBS; ++j) {
+    const int col = 32 * (j * NG + grp);
+    uint32_t b[32];
+    if (j + 1 < SUBS) tmem_ld_async_x32(tbuf + col + 32 * NG, b);
+    uint32_t w[16];
+    pack_cols<16, true>(a, w);
+    tmem_st_x16(tbuf + h_tmem_col(col), w);
+    publish_chunk(chunk_bar0 + 8 * j);
+    if (j + 1 < SUBS) {
+      tmem_wait_ld_bind_x32(b);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) a[i] = b[i];
-      }
+      for (int i = 0; i < 32; ++i) a[i] = b[i];
     }
   }
 }
@@ -258,7 +250,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
       mbar_init(bar_acc_full(s), 1);
       mbar_init(bar_out_ready(s), EPW);
       mbar_init(bar_store_free(s), 1);
-      for (int c = 0; c < Cfg::MAXCH; ++c) mbar_init(bar_chunk(s, c), 4);
+      for (int c = 0; c < Cfg::MAXCH; ++c) mbar_init(bar_chunk(s, c), EPW);
     }
     mbar_init(bar_w_full, 1);
     mbar_init(bar_mma_done, 1);
@@ -365,39 +357,34 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
             }
             __syncwarp();
           } else {
-            // chunks of h_{l-1}: 32 columns each, produced by column group g
-            // as its sub-chunk j; consume sub-chunk-major (both groups' first
-            // halves first).  A comes from TMEM: the previous job's buffer,
-            // where the epilogue packed h_{l-1} (h_tmem_col).
-            constexpr int KC = K < 32 ? K : 32;        // columns per chunk
-            constexpr int NCH = K / KC;                 // chunks of this input
-            constexpr int NGRP = Cfg::NG;               // producer column groups
-            constexpr int SUBS = NCH / NGRP > 0 ? NCH / NGRP : 1;
-            constexpr int PCOL = K / NGRP;              // producer columns per group
+            // chunk j of h_{l-1} = stripe j of every column group (32*NG
+            // columns), complete once all epilogue warps of the slot arrived.
+            // A comes from TMEM: the previous job's buffer, where the
+            // epilogue packed h_{l-1} (h_tmem_col).
+            constexpr int NGRP = Cfg::NG;
+            constexpr int NCH = K / (32 * NGRP);
+            static_assert(NCH >= 1 && K % (32 * NGRP) == 0, "hidden width vs column groups");
             const uint32_t a_tmem = tmem_base + (2 * s + ((i * L + l - 1) & 1)) * Cfg::SLOT_COLS;
             const uint32_t par = (i * (L - 1) + l - 1) & 1;
 #pragma unroll
-            for (int j = 0; j < SUBS; ++j) {
+            for (int j = 0; j < NCH; ++j) {
+              ok = __all_sync(0xffffffffu,
+                              mbar_wait(bar_chunk(s, j), par, abort_flag, kDevTimeoutMma));
+              if (!ok) break;
+              tc_fence_after();
+              if (issuer) {
 #pragma unroll
-              for (int g = 0; g < NGRP; ++g) {
-                const int c = g * SUBS + j;
-                if (c >= NCH) continue;
-                ok = __all_sync(0xffffffffu,
-                                mbar_wait(bar_chunk(s, c), par, abort_flag, kDevTimeoutMma));
-                if (!ok) break;
-                tc_fence_after();
-                if (issuer) {
+                for (int g = 0; g < NGRP; ++g) {
 #pragma unroll
-                  for (int kk = 0; kk < KC / 16; ++kk) {
-                    const int k = c * (KC / 16) + kk;
-                    umma_f16_ts(d_tmem, a_tmem + h_tmem_col<PCOL>(16 * k),
+                  for (int kk = 0; kk < 2; ++kk) {
+                    const int k = 2 * (j * NGRP + g) + kk;   // K-step (16 columns)
+                    umma_f16_ts(d_tmem, a_tmem + h_tmem_col(16 * k),
                                 bdesc0 + (mnmajor_koff<N>(k) >> 4), idesc,
                                 (j == 0 && g == 0 && kk == 0) ? 0u : 1u);
                   }
                 }
-                __syncwarp();
               }
-              if (!ok) break;
+              __syncwarp();
             }
             if (!ok) break;
           }
@@ -452,7 +439,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
           if (!ok) break;
         }
         const uint32_t t_buf = t_lane + ((i * L + l) & 1) * Cfg::SLOT_COLS;
-        hidden_job<NCOL_H>(t_buf, grp * NCOL_H, bar_chunk(s, 0));
+        hidden_job<H, Cfg::NG>(t_buf, grp, bar_chunk(s, 0));
       }
       if (!ok) break;
       // output layer: fp16 result staged in obuf, written by TMA

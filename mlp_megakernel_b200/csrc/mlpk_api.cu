@@ -141,9 +141,9 @@ bool shape_is(const mlpk_shape* s) {
 using Fwd = int (*)(const void*, const void* const*, void*, int64_t, cudaStream_t);
 
 Fwd pick_fwd(const mlpk_shape* s) {
-  if (shape_is<128, 128, 128, 128>(s)) return &launch_fwd<Net<128, 128, 128, 128>, 2, 8>;
-  if (shape_is<32, 64, 64, 64, 64, 16>(s)) return &launch_fwd<Net<32, 64, 64, 64, 64, 16>, 2, 8>;
-  if (shape_is<64, 64, 64, 64>(s)) return &launch_fwd<Net<64, 64, 64, 64>, 2, 8>;
+  if (shape_is<128, 128, 128, 128>(s)) return &launch_fwd<Net<128, 128, 128, 128>, 2, 4>;
+  if (shape_is<32, 64, 64, 64, 64, 16>(s)) return &launch_fwd<Net<32, 64, 64, 64, 64, 16>, 2, 4>;
+  if (shape_is<64, 64, 64, 64>(s)) return &launch_fwd<Net<64, 64, 64, 64>, 2, 4>;
   return nullptr;
 }
 
