@@ -109,7 +109,9 @@ struct FwdCfg {
   // Hidden activations are handed to the MMA warp in chunks: a chunk is one
   // 32-column stripe from every column group (32*NG columns); its barrier
   // counts all EPW warps of the slot.
-  static constexpr int MAXCH = (HMAX / (EPW / 4) + 31) / 32;  // chunks per layer, max
+  // SPC: stripes per chunk per column group (chunk = SPC*NG stripes).
+  static constexpr int SPC = (HMAX / (EPW / 4)) / 32 >= 4 ? 2 : 1;
+  static constexpr int MAXCH = ((HMAX / (EPW / 4) + 31) / 32 + SPC - 1) / SPC;  // chunks/layer
   // x_full, x_empty, acc_full, out_ready, store_free per slot; MAXCH h-chunk
   // barriers per slot; w_full; mma_done
   static constexpr int NUM_BARS = 5 * NS + NS * MAXCH + 2;
@@ -161,15 +163,17 @@ __device__ __forceinline__ void publish_chunk(uint32_t bar) {
 // Hidden-layer job of one warp of column group `grp` (of NG): stripes
 // grp, grp+NG, grp+2NG, ... (32 columns each) of the accumulator buffer at
 // TMEM address tbuf (lane field = the warp's quarter) -> softplus -> fp16 back
-// into TMEM at h_tmem_col(); after stripe j it arrives on chunk barrier j
-// (chunk_bar0 + 8j), which completes once all NG groups finished stripe j.  A
+// into TMEM at h_tmem_col(); after every SPC stripes it arrives on the next
+// chunk barrier (chunk_bar0 + 8*(j/SPC)), which completes once all NG groups
+// finished those stripes.  A
 // column is always loaded before the packed activation overwrites it: a
 // stripe's packed columns lie in its own range, and the async load of the
 // next stripe is issued before this stripe's store.
-template <int N, int NG>
+template <int N, int NG, int SPC>
 __device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chunk_bar0) {
   static_assert(N % (32 * NG) == 0, "hidden width must be a multiple of 32 * column groups");
   constexpr int SUBS = N / (32 * NG);
+  static_assert(SUBS % SPC == 0, "stripes per chunk must divide the stripes per group");
   uint32_t a[32];
   tmem_ld_wait_x32(tbuf + 32 * grp, a);
 #pragma unroll
@@ -180,7 +184,7 @@ __device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chun
     uint32_t w[16];
     pack_cols<16, true>(a, w);
     tmem_st_x16(tbuf + h_tmem_col(col), w);
-    publish_chunk(chunk_bar0 + 8 * j);
+    if ((j + 1) % SPC == 0) publish_chunk(chunk_bar0 + 8 * (j / SPC));
     if (j + 1 < SUBS) {
       tmem_wait_ld_bind_x32(b);
 #pragma unroll
@@ -362,8 +366,9 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
             // A comes from TMEM: the previous job's buffer, where the
             // epilogue packed h_{l-1} (h_tmem_col).
             constexpr int NGRP = Cfg::NG;
-            constexpr int NCH = K / (32 * NGRP);
-            static_assert(NCH >= 1 && K % (32 * NGRP) == 0, "hidden width vs column groups");
+            constexpr int SPC = Cfg::SPC;
+            constexpr int NCH = K / (32 * NGRP * SPC);
+            static_assert(NCH >= 1 && K % (32 * NGRP * SPC) == 0, "hidden width vs chunks");
             const uint32_t a_tmem = tmem_base + (2 * s + ((i * L + l - 1) & 1)) * Cfg::SLOT_COLS;
             const uint32_t par = (i * (L - 1) + l - 1) & 1;
 #pragma unroll
@@ -374,13 +379,16 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
               tc_fence_after();
               if (issuer) {
 #pragma unroll
-                for (int g = 0; g < NGRP; ++g) {
+                for (int js = 0; js < SPC; ++js) {
 #pragma unroll
-                  for (int kk = 0; kk < 2; ++kk) {
-                    const int k = 2 * (j * NGRP + g) + kk;   // K-step (16 columns)
-                    umma_f16_ts(d_tmem, a_tmem + h_tmem_col(16 * k),
-                                bdesc0 + (mnmajor_koff<N>(k) >> 4), idesc,
-                                (j == 0 && g == 0 && kk == 0) ? 0u : 1u);
+                  for (int g = 0; g < NGRP; ++g) {
+#pragma unroll
+                    for (int kk = 0; kk < 2; ++kk) {
+                      const int k = 2 * ((j * SPC + js) * NGRP + g) + kk;  // K-step
+                      umma_f16_ts(d_tmem, a_tmem + h_tmem_col(16 * k),
+                                  bdesc0 + (mnmajor_koff<N>(k) >> 4), idesc,
+                                  (j == 0 && js == 0 && g == 0 && kk == 0) ? 0u : 1u);
+                    }
                   }
                 }
               }
@@ -439,7 +447,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
           if (!ok) break;
         }
         const uint32_t t_buf = t_lane + ((i * L + l) & 1) * Cfg::SLOT_COLS;
-        hidden_job<H, Cfg::NG>(t_buf, grp, bar_chunk(s, 0));
+        hidden_job<H, Cfg::NG, Cfg::SPC>(t_buf, grp, bar_chunk(s, 0));
       }
       if (!ok) break;
       // output layer: fp16 result staged in obuf, written by TMA
