@@ -71,6 +71,20 @@ struct Net {
     for (int i = 0; i < L; ++i) o += tile_bytes(a[i], a[i + 1]);
     return o;
   }
+  // Offsets/bytes when each CTA of a pair holds half of every weight's columns.
+  template <int l>
+  __host__ __device__ static constexpr int w_half_off() {
+    constexpr int a[] = {Ds...};
+    int o = 0;
+    for (int i = 0; i < l; ++i) o += align_up(tile_bytes(a[i], a[i + 1] / 2), 1024);
+    return o;
+  }
+  __host__ __device__ static constexpr int w_half_bytes_exact() {
+    constexpr int a[] = {Ds...};
+    int o = 0;
+    for (int i = 0; i < L; ++i) o += tile_bytes(a[i], a[i + 1] / 2);
+    return o;
+  }
   __host__ __device__ static constexpr bool hidden_uniform() {
     constexpr int a[] = {Ds...};
     for (int i = 2; i < L; ++i)
@@ -152,12 +166,17 @@ __device__ __forceinline__ void pack_cols(const uint32_t* r, uint32_t* w) {
 }
 
 // Publishes one finished chunk of h to the MMA issuer: the TMEM stores are
-// complete and ordered (with this chunk's TMEM loads) before the arrive.
+// complete and ordered (with this chunk's TMEM loads) before the arrive.  With
+// CLUSTER the barrier is a cluster address (the pair leader's barrier).
+template <bool CLUSTER = false>
 __device__ __forceinline__ void publish_chunk(uint32_t bar) {
   tmem_wait_st();
   tc_fence_before();
   __syncwarp();
-  if (lane_id() == 0) mbar_arrive(bar);
+  if (lane_id() == 0) {
+    if constexpr (CLUSTER) mbar_arrive_cluster(bar);
+    else mbar_arrive(bar);
+  }
 }
 
 // Hidden-layer job of one warp of column group `grp` (of NG): stripes
@@ -169,7 +188,7 @@ __device__ __forceinline__ void publish_chunk(uint32_t bar) {
 // column is always loaded before the packed activation overwrites it: a
 // stripe's packed columns lie in its own range, and the async load of the
 // next stripe is issued before this stripe's store.
-template <int N, int NG, int SPC>
+template <int N, int NG, int SPC, bool CLUSTER = false>
 __device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chunk_bar0) {
   static_assert(N % (32 * NG) == 0, "hidden width must be a multiple of 32 * column groups");
   constexpr int SUBS = N / (32 * NG);
@@ -184,7 +203,7 @@ __device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chun
     uint32_t w[16];
     pack_cols<16, true>(a, w);
     tmem_st_x16(tbuf + h_tmem_col(col), w);
-    if ((j + 1) % SPC == 0) publish_chunk(chunk_bar0 + 8 * (j / SPC));
+    if ((j + 1) % SPC == 0) publish_chunk<CLUSTER>(chunk_bar0 + 8 * (j / SPC));
     if (j + 1 < SUBS) {
       tmem_wait_ld_bind_x32(b);
 #pragma unroll

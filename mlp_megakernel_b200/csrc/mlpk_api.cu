@@ -8,11 +8,12 @@
 #include <cudaTypedefs.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
 #include "../../include/mlpk.h"
-#include "fwd_kernel.cuh"
+#include "fwd2_kernel.cuh"
 
 namespace {
 
@@ -127,6 +128,49 @@ int launch_fwd(const void* x, const void* const* W, void* out, int64_t M, cudaSt
   return cudaGetLastError() == cudaSuccess ? MLPK_OK : MLPK_ERR_CUDA;
 }
 
+// CTA-pair forward: clusters of 2 CTAs, one M=256 UMMA per pair tile.
+template <class NetT, int NS, int EPW>
+int launch_fwd2(const void* x, const void* const* W, void* out, int64_t M, cudaStream_t st) {
+  using Cfg = mlpk::Fwd2Cfg<NetT, NS, EPW>;
+  constexpr int L = NetT::L;
+  DevInfo di;
+  int dev = 0;
+  int rc = current_device_info(&di, &dev);
+  if (rc != MLPK_OK) return rc;
+  if (M == 0) return MLPK_OK;
+  if (M > (int64_t(1) << 31) - 512) return MLPK_ERR_SHAPE;
+
+  FwdMaps<L> maps;
+  std::memset(&maps, 0, sizeof(maps));
+  rc = make_map_2d(&maps.x, x, Cfg::D0, M, mlpk::chunk_elems(Cfg::D0), mlpk::kTileM);
+  if (rc) return rc;
+  rc = make_map_2d(&maps.out, out, Cfg::DL, M, mlpk::chunk_elems(Cfg::DL), mlpk::kTileM);
+  if (rc) return rc;
+  int wrc = MLPK_OK;
+  mlpk::static_for<0, L>([&](auto lc) {
+    constexpr int l = decltype(lc)::value;
+    constexpr int K = NetT::template D<l>();
+    constexpr int NH = NetT::template D<l + 1>() / 2;
+    // box covers one CTA's half of the output columns
+    if (wrc == MLPK_OK) wrc = make_map_2d(&maps.w[l], W[l], 2 * NH, K, mlpk::chunk_elems(NH), K);
+  });
+  if (wrc) return wrc;
+
+  auto kern = mlpk::mlp_fwd2_kernel<NetT, NS, EPW>;
+  static bool attr_set[kMaxDevices] = {};
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg::SMEM_BYTES) != cudaSuccess)
+      return MLPK_ERR_CUDA;
+    attr_set[dev] = true;
+  }
+  const int num_pairs = static_cast<int>((M + 2 * mlpk::kTileM - 1) / (2 * mlpk::kTileM));
+  const int max_clusters = di.sm_count / 2;
+  const int clusters = num_pairs < max_clusters ? num_pairs : max_clusters;
+  kern<<<2 * clusters, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(maps, num_pairs);
+  return cudaGetLastError() == cudaSuccess ? MLPK_OK : MLPK_ERR_CUDA;
+}
+
 // ------------------------------------------------------------------ dispatch
 template <int... Ds>
 bool shape_is(const mlpk_shape* s) {
@@ -140,8 +184,18 @@ bool shape_is(const mlpk_shape* s) {
 
 using Fwd = int (*)(const void*, const void* const*, void*, int64_t, cudaStream_t);
 
+// MLPK_FWD_PAIR=1 selects the CTA-pair (cta_group::2) forward for shapes that
+// have one; the single-SM kernel is the default (measured faster on B200 for
+// the 128-wide network).  Read on every call so a process can switch.
+bool prefer_pair() {
+  const char* e = std::getenv("MLPK_FWD_PAIR");
+  return e && e[0] == '1';
+}
+
 Fwd pick_fwd(const mlpk_shape* s) {
-  if (shape_is<128, 128, 128, 128>(s)) return &launch_fwd<Net<128, 128, 128, 128>, 2, 4>;
+  if (shape_is<128, 128, 128, 128>(s))
+    return prefer_pair() ? &launch_fwd2<Net<128, 128, 128, 128>, 2, 4>
+                         : &launch_fwd<Net<128, 128, 128, 128>, 2, 4>;
   if (shape_is<32, 64, 64, 64, 64, 16>(s)) return &launch_fwd<Net<32, 64, 64, 64, 64, 16>, 2, 4>;
   if (shape_is<64, 64, 64, 64>(s)) return &launch_fwd<Net<64, 64, 64, 64>, 2, 4>;
   return nullptr;

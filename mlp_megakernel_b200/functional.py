@@ -52,18 +52,25 @@ def _check_operands(x: torch.Tensor, weights) -> list:
     return dims
 
 
-def fused_mlp_fwd(x: torch.Tensor, *weights: torch.Tensor) -> torch.Tensor:
+def fused_mlp_fwd(x: torch.Tensor, *weights: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
     """``softplus(...softplus(x @ W_0)...) @ W_{L-1}`` in one kernel launch.
 
     Softplus is beta=1, threshold=20 (kernel.py:108); products accumulate in
     fp32 and every hidden activation is rounded to fp16 before the next GEMM
-    (kernel.py:110, kernel.py:117).
+    (kernel.py:110, kernel.py:117).  Like the reference (kernel.py:136) the
+    result is a new tensor unless ``out`` (contiguous, ``[M, out_features]``,
+    x's dtype and device) is given, which lets a serving loop reuse one buffer.
     """
     dims = _check_operands(x, weights)
     x = _aligned(x)
     ws = [_aligned(w) for w in weights]
     M = x.shape[0]
-    out = torch.empty((M, dims[-1]), device=x.device, dtype=x.dtype)
+    if out is None:
+        out = torch.empty((M, dims[-1]), device=x.device, dtype=x.dtype)
+    elif (out.shape != (M, dims[-1]) or out.dtype != x.dtype or out.device != x.device
+          or not out.is_contiguous() or out.data_ptr() % 16 != 0):
+        raise ValueError("out must be a contiguous, 16-byte aligned "
+                         f"[{M}, {dims[-1]}] {x.dtype} tensor on {x.device}")
     if M == 0:
         return out
     lib = _lib.lib()

@@ -67,6 +67,23 @@ def test_fwd_ragged_batch_sizes(M):
     assert _rel_max(out, ref) <= TIGHT
 
 
+@pytest.mark.parametrize("M", [1, 129, 256, 300, 148 * 256 + 128, 1 << 20])
+def test_fwd_cta_pair_kernel(M, monkeypatch):
+    """The CTA-pair (cta_group::2, M=256 UMMA) forward gives the same results."""
+    x, ws = make_inputs("3L128", M)
+    xg, wg = x.cuda(), _gpu(ws)
+    monkeypatch.setenv("MLPK_FWD_PAIR", "1")
+    out2 = fused_mlp_fwd(xg, *wg)
+    monkeypatch.delenv("MLPK_FWD_PAIR")
+    out1 = fused_mlp_fwd(xg, *wg)
+    torch.cuda.synchronize()
+    rows = np.unique(np.concatenate([np.arange(min(M, 512)), np.arange(max(0, M - 512), M),
+                                     np.arange(0, M, max(1, M // 512))]))
+    ref = oracle.mlp_forward(x.numpy()[rows], [w.numpy() for w in ws])
+    assert _rel_max(out2.cpu().numpy()[rows], ref) <= TIGHT
+    assert _rel_max(out1.cpu().numpy()[rows], ref) <= TIGHT
+
+
 def test_fwd_empty_batch():
     x, ws = make_inputs("3L128", 0)
     out = fused_mlp_fwd(x.cuda(), *_gpu(ws))
@@ -123,6 +140,17 @@ def test_fwd_misaligned_device_view():
     out = fused_mlp_fwd(xv, *_gpu(ws)).cpu().numpy()
     ref = oracle.mlp_forward(x.numpy(), [w.numpy() for w in ws])
     assert _rel_max(out, ref) <= TIGHT
+
+
+def test_fwd_out_buffer():
+    x, ws = make_inputs("3L128", 700)
+    xg, wg = x.cuda(), _gpu(ws)
+    ref = fused_mlp_fwd(xg, *wg)
+    buf = torch.full((700, 128), float("nan"), dtype=torch.float16, device="cuda")
+    got = fused_mlp_fwd(xg, *wg, out=buf)
+    assert got.data_ptr() == buf.data_ptr() and torch.equal(got, ref)
+    with pytest.raises(ValueError):
+        fused_mlp_fwd(xg, *wg, out=torch.empty(700, 64, dtype=torch.float16, device="cuda"))
 
 
 def test_fwd_reference_api_names():
