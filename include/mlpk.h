@@ -59,6 +59,45 @@ int mlpk_shape_supported(const mlpk_shape* shape);
 int mlpk_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W, void* out,
              mlpk_stream_t stream);
 
+/* 1 if training (mlpk_train_fwd + mlpk_bwd) is compiled for this shape. */
+int mlpk_train_supported(const mlpk_shape* shape);
+
+/* Training forward: as mlpk_fwd, and also writes every hidden activation
+ * h_l = softplus(z_l), l = 1..num_layers-1, to h_saved[l-1] ([M, dims[l]],
+ * fp16 -- the exact operand the next GEMM consumed).
+ * Replaces the training forward of the reference (mlp_fused.md:52-61;
+ * fused_mlp.py is named at README.md:18 but absent from its tree). */
+int mlpk_train_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
+                   void* out, void* const* h_saved, mlpk_stream_t stream);
+
+/* Bytes of device workspace mlpk_bwd needs for M rows on the current device
+ * (one fp32 weight-gradient partial per persistent CTA); -1 if unsupported. */
+int64_t mlpk_bwd_workspace_size(const mlpk_shape* shape, int64_t M);
+
+/* Backward: from x, W, the saved h and grad_out ([M, dims[L]] fp16) writes
+ * dx ([M, dims[0]] fp16) and dW (fp32, all layers concatenated, layer l is
+ * [dims[l], dims[l+1]] row-major).  dW is a deterministic fixed-order sum over
+ * the per-CTA partials kept in `workspace` (>= mlpk_bwd_workspace_size bytes).
+ * Replaces the fused backward megakernel and its cuBLAS fallback
+ * (mlp_fused.md:80-146). */
+int mlpk_bwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
+             const void* const* h_saved, const void* grad_out, void* dx, void* workspace,
+             int64_t workspace_bytes, float* dW, mlpk_stream_t stream);
+
+/* Weight norm forward, all layers in one launch: W_l = g_l * v_l / ||v_l||
+ * per output column.  v_all: fp32 concat of v_l [dims[l], dims[l+1]]; g_all and
+ * inv_norm: fp32 concat of per-column vectors; W[l]: fp16 outputs.
+ * Replaces _wn_fwd_kernel (mlp_fused.md:466-480). */
+int mlpk_wn_fwd(const mlpk_shape* shape, const float* v_all, const float* g_all, void* const* W,
+                float* inv_norm, mlpk_stream_t stream);
+
+/* Weight norm backward, all layers in one launch: (dv_all, dg_all) from the
+ * fp32 dW_all of mlpk_bwd.  Replaces _wn_bwd_from_dw_T_kernel
+ * (mlp_fused.md:481-483). */
+int mlpk_wn_bwd(const mlpk_shape* shape, const float* dW_all, const float* v_all,
+                const float* g_all, const float* inv_norm, float* dv_all, float* dg_all,
+                mlpk_stream_t stream);
+
 /* Reads (and optionally clears) the device-side status word of the current
  * device: bit flags set by bounded waits that expired.  Synchronises. */
 int mlpk_device_status(int clear, int* status_out);

@@ -41,6 +41,13 @@ SIGNATURES = {
     "mlpk_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "mlpk_shape_supported": (ctypes.c_int, [_SHAPE_P]),
     "mlpk_fwd": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _vp, _vp]),
+    "mlpk_train_supported": (ctypes.c_int, [_SHAPE_P]),
+    "mlpk_train_fwd": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _vp, _VPP, _vp]),
+    "mlpk_bwd_workspace_size": (ctypes.c_int64, [_SHAPE_P, ctypes.c_int64]),
+    "mlpk_bwd": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _VPP, _vp, _vp, _vp,
+                                ctypes.c_int64, _vp, _vp]),
+    "mlpk_wn_fwd": (ctypes.c_int, [_SHAPE_P, _vp, _vp, _VPP, _vp, _vp]),
+    "mlpk_wn_bwd": (ctypes.c_int, [_SHAPE_P, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "mlpk_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
 }
 
@@ -106,6 +113,10 @@ def shape_struct(dims) -> MlpkShape:
 
 def shape_supported(dims) -> bool:
     return bool(lib().mlpk_shape_supported(ctypes.byref(shape_struct(dims))))
+
+
+def train_supported(dims) -> bool:
+    return bool(lib().mlpk_train_supported(ctypes.byref(shape_struct(dims))))
 
 
 def ptr_array(ptrs) -> ctypes.Array:

@@ -85,6 +85,16 @@ struct Net {
     for (int i = 0; i < L; ++i) o += tile_bytes(a[i], a[i + 1] / 2);
     return o;
   }
+  __host__ __device__ static constexpr int dim(int i) {
+    constexpr int a[] = {Ds...};
+    return a[i];
+  }
+  __host__ __device__ static constexpr bool all_dims_are(int v) {
+    constexpr int a[] = {Ds...};
+    for (int i = 0; i <= L; ++i)
+      if (a[i] != v) return false;
+    return true;
+  }
   __host__ __device__ static constexpr bool hidden_uniform() {
     constexpr int a[] = {Ds...};
     for (int i = 2; i < L; ++i)
@@ -98,6 +108,10 @@ struct alignas(64) FwdMaps {
   CUtensorMap x;       // [M, d0] fp16, box {chunk(d0), 128}
   CUtensorMap out;     // [M, dL] fp16, box {chunk(dL), 128}
   CUtensorMap w[L];    // [d_l, d_{l+1}] fp16, box {chunk(d_{l+1}), d_l}
+  // training forward only: where to save the hidden activations h_1..h_{L-1}
+  // ([M, d_l] fp16 each, the exact values fed to the next GEMM), and M
+  void* hsave[L > 1 ? L - 1 : 1];
+  int M;
 };
 
 template <int I, int N, class F>
@@ -188,8 +202,9 @@ __device__ __forceinline__ void publish_chunk(uint32_t bar) {
 // column is always loaded before the packed activation overwrites it: a
 // stripe's packed columns lie in its own range, and the async load of the
 // next stripe is issued before this stripe's store.
-template <int N, int NG, int SPC, bool CLUSTER = false>
-__device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chunk_bar0) {
+template <int N, int NG, int SPC, bool CLUSTER = false, bool SAVE = false>
+__device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chunk_bar0,
+                                           uint8_t* hrow = nullptr) {
   static_assert(N % (32 * NG) == 0, "hidden width must be a multiple of 32 * column groups");
   constexpr int SUBS = N / (32 * NG);
   static_assert(SUBS % SPC == 0, "stripes per chunk must divide the stripes per group");
@@ -203,6 +218,14 @@ __device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chun
     uint32_t w[16];
     pack_cols<16, true>(a, w);
     tmem_st_x16(tbuf + h_tmem_col(col), w);
+    if constexpr (SAVE) {
+      if (hrow != nullptr) {  // this thread's row exists (row < M): save h for backward
+        uint4* dst = reinterpret_cast<uint4*>(hrow + 2 * col);
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          dst[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+      }
+    }
     if ((j + 1) % SPC == 0) publish_chunk<CLUSTER>(chunk_bar0 + 8 * (j / SPC));
     if (j + 1 < SUBS) {
       tmem_wait_ld_bind_x32(b);
@@ -237,7 +260,7 @@ __device__ __forceinline__ void out_job(uint32_t tbuf, uint32_t tile_base, uint3
   }
 }
 
-template <class NetT, int NS, int EPW>
+template <class NetT, int NS, int EPW, bool TRAIN = false>
 __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
     mlp_fwd_kernel(const __grid_constant__ FwdMaps<NetT::L> maps, int num_tiles) {
   using Cfg = FwdCfg<NetT, NS, EPW>;
@@ -466,7 +489,15 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
           if (!ok) break;
         }
         const uint32_t t_buf = t_lane + ((i * L + l) & 1) * Cfg::SLOT_COLS;
-        hidden_job<H, Cfg::NG, Cfg::SPC>(t_buf, grp, bar_chunk(s, 0));
+        if constexpr (TRAIN) {
+          const int grow = t * kTileM + static_cast<int>(row);
+          uint8_t* hrow = grow < maps.M ? static_cast<uint8_t*>(maps.hsave[l]) +
+                                              static_cast<size_t>(grow) * H * 2
+                                        : nullptr;
+          hidden_job<H, Cfg::NG, Cfg::SPC, false, true>(t_buf, grp, bar_chunk(s, 0), hrow);
+        } else {
+          hidden_job<H, Cfg::NG, Cfg::SPC>(t_buf, grp, bar_chunk(s, 0));
+        }
       }
       if (!ok) break;
       // output layer: fp16 result staged in obuf, written by TMA

@@ -11,9 +11,13 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <set>
+#include <utility>
 
 #include "../../include/mlpk.h"
+#include "bwd_kernel.cuh"
 #include "fwd2_kernel.cuh"
+#include "wn_kernel.cuh"
 
 namespace {
 
@@ -87,9 +91,24 @@ int make_map_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t oute
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Raise a kernel's dynamic shared-memory limit once per (kernel, device).
+template <class Kern>
+bool set_smem_once(Kern kern, int bytes, int dev) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_pair(reinterpret_cast<const void*>(kern), dev);
+  if (done.count(key)) return true;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return false;
+  done.insert(key);
+  return true;
+}
+
 // ------------------------------------------------------------------ forward
 template <class NetT, int NS, int EPW>
-int launch_fwd(const void* x, const void* const* W, void* out, int64_t M, cudaStream_t st) {
+int launch_fwd(const void* x, const void* const* W, void* out, int64_t M, void* const* hsave,
+               cudaStream_t st) {
   using Cfg = FwdCfg<NetT, NS, EPW>;
   constexpr int L = NetT::L;
   DevInfo di;
@@ -113,24 +132,28 @@ int launch_fwd(const void* x, const void* const* W, void* out, int64_t M, cudaSt
     if (wrc == MLPK_OK) wrc = make_map_2d(&maps.w[l], W[l], N, K, mlpk::chunk_elems(N), K);
   });
   if (wrc) return wrc;
+  maps.M = static_cast<int>(M);
+  for (int l = 0; l + 1 < L; ++l) maps.hsave[l] = hsave ? hsave[l] : nullptr;
 
-  auto kern = mlpk::mlp_fwd_kernel<NetT, NS, EPW>;
-  static bool attr_set[kMaxDevices] = {};
-  if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Cfg::SMEM_BYTES) != cudaSuccess)
-      return MLPK_ERR_CUDA;
-    attr_set[dev] = true;
-  }
   const int num_tiles = static_cast<int>((M + mlpk::kTileM - 1) / mlpk::kTileM);
   const int grid = num_tiles < di.sm_count ? num_tiles : di.sm_count;
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(maps, num_tiles);
+  if (hsave) {
+    auto kern = mlpk::mlp_fwd_kernel<NetT, NS, EPW, true>;
+    if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(maps, num_tiles);
+  } else {
+    auto kern = mlpk::mlp_fwd_kernel<NetT, NS, EPW, false>;
+    if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(maps, num_tiles);
+  }
   return cudaGetLastError() == cudaSuccess ? MLPK_OK : MLPK_ERR_CUDA;
 }
 
 // CTA-pair forward: clusters of 2 CTAs, one M=256 UMMA per pair tile.
 template <class NetT, int NS, int EPW>
-int launch_fwd2(const void* x, const void* const* W, void* out, int64_t M, cudaStream_t st) {
+int launch_fwd2(const void* x, const void* const* W, void* out, int64_t M, void* const* hsave,
+                cudaStream_t st) {
+  if (hsave) return MLPK_ERR_UNSUPPORTED;  // the pair kernel is inference-only
   using Cfg = mlpk::Fwd2Cfg<NetT, NS, EPW>;
   constexpr int L = NetT::L;
   DevInfo di;
@@ -157,17 +180,64 @@ int launch_fwd2(const void* x, const void* const* W, void* out, int64_t M, cudaS
   if (wrc) return wrc;
 
   auto kern = mlpk::mlp_fwd2_kernel<NetT, NS, EPW>;
-  static bool attr_set[kMaxDevices] = {};
-  if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Cfg::SMEM_BYTES) != cudaSuccess)
-      return MLPK_ERR_CUDA;
-    attr_set[dev] = true;
-  }
+  if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
   const int num_pairs = static_cast<int>((M + 2 * mlpk::kTileM - 1) / (2 * mlpk::kTileM));
   const int max_clusters = di.sm_count / 2;
   const int clusters = num_pairs < max_clusters ? num_pairs : max_clusters;
   kern<<<2 * clusters, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(maps, num_pairs);
+  return cudaGetLastError() == cudaSuccess ? MLPK_OK : MLPK_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------ backward
+template <class NetT>
+int64_t bwd_grid(int64_t M, int sm_count) {
+  const int64_t tiles = (M + mlpk::kTileM - 1) / mlpk::kTileM;
+  return tiles < sm_count ? tiles : sm_count;
+}
+
+template <class NetT>
+size_t bwd_workspace(int64_t M, int sm_count) {
+  return static_cast<size_t>(bwd_grid<NetT>(M, sm_count)) * mlpk::BwdCfg<NetT>::PARTIAL_FLOATS *
+         sizeof(float);
+}
+
+template <class NetT>
+int launch_bwd(const void* x, const void* const* W, const void* const* h, const void* g, void* dx,
+               float* ws, size_t ws_bytes, float* dw, int64_t M, cudaStream_t st) {
+  using Cfg = mlpk::BwdCfg<NetT>;
+  constexpr int L = NetT::L;
+  DevInfo di;
+  int dev = 0;
+  int rc = current_device_info(&di, &dev);
+  if (rc != MLPK_OK) return rc;
+  if (M > (int64_t(1) << 31) - 256) return MLPK_ERR_SHAPE;
+  const int nfloats = Cfg::PARTIAL_FLOATS;
+  const int grid = static_cast<int>(bwd_grid<NetT>(M, di.sm_count));
+  if (grid > 0) {
+    if (ws_bytes < bwd_workspace<NetT>(M, di.sm_count)) return MLPK_ERR_SHAPE;
+    mlpk::BwdMaps<L> maps;
+    std::memset(&maps, 0, sizeof(maps));
+    if ((rc = make_map_2d(&maps.x, x, Cfg::D0, M, mlpk::chunk_elems(Cfg::D0), mlpk::kTileM))) return rc;
+    if ((rc = make_map_2d(&maps.g, g, Cfg::DL, M, mlpk::chunk_elems(Cfg::DL), mlpk::kTileM))) return rc;
+    if ((rc = make_map_2d(&maps.dx, dx, Cfg::D0, M, mlpk::chunk_elems(Cfg::D0), mlpk::kTileM))) return rc;
+    int wrc = MLPK_OK;
+    mlpk::static_for<0, L>([&](auto lc) {
+      constexpr int l = decltype(lc)::value;
+      constexpr int K = NetT::template D<l>();
+      constexpr int N = NetT::template D<l + 1>();
+      if (wrc == MLPK_OK) wrc = make_map_2d(&maps.w[l], W[l], N, K, mlpk::chunk_elems(N), K);
+      if constexpr (l >= 1)
+        if (wrc == MLPK_OK) wrc = make_map_2d(&maps.h[l - 1], h[l - 1], K, M, mlpk::chunk_elems(K), mlpk::kTileM);
+    });
+    if (wrc) return wrc;
+    maps.partials = ws;
+    auto kern = mlpk::mlp_bwd_kernel<NetT>;
+    if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
+    const int num_tiles = static_cast<int>((M + mlpk::kTileM - 1) / mlpk::kTileM);
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(maps, num_tiles);
+    if (cudaGetLastError() != cudaSuccess) return MLPK_ERR_CUDA;
+  }
+  mlpk::mlp_reduce_kernel<<<(nfloats + 255) / 256, 256, 0, st>>>(ws, grid, nfloats, dw);
   return cudaGetLastError() == cudaSuccess ? MLPK_OK : MLPK_ERR_CUDA;
 }
 
@@ -182,7 +252,16 @@ bool shape_is(const mlpk_shape* s) {
   return true;
 }
 
-using Fwd = int (*)(const void*, const void* const*, void*, int64_t, cudaStream_t);
+using Fwd = int (*)(const void*, const void* const*, void*, int64_t, void* const*, cudaStream_t);
+using Bwd = int (*)(const void*, const void* const*, const void* const*, const void*, void*, float*,
+                    size_t, float*, int64_t, cudaStream_t);
+using BwdWs = size_t (*)(int64_t, int);
+
+struct ShapeOps {
+  Fwd fwd = nullptr;
+  Bwd bwd = nullptr;
+  BwdWs bwd_ws = nullptr;
+};
 
 // MLPK_FWD_PAIR=1 selects the CTA-pair (cta_group::2) forward for shapes that
 // have one; the single-SM kernel is the default (measured faster on B200 for
@@ -192,13 +271,19 @@ bool prefer_pair() {
   return e && e[0] == '1';
 }
 
-Fwd pick_fwd(const mlpk_shape* s) {
-  if (shape_is<128, 128, 128, 128>(s))
-    return prefer_pair() ? &launch_fwd2<Net<128, 128, 128, 128>, 2, 4>
-                         : &launch_fwd<Net<128, 128, 128, 128>, 2, 4>;
-  if (shape_is<32, 64, 64, 64, 64, 16>(s)) return &launch_fwd<Net<32, 64, 64, 64, 64, 16>, 2, 4>;
-  if (shape_is<64, 64, 64, 64>(s)) return &launch_fwd<Net<64, 64, 64, 64>, 2, 4>;
-  return nullptr;
+ShapeOps pick_ops(const mlpk_shape* s, bool training) {
+  ShapeOps o;
+  if (shape_is<128, 128, 128, 128>(s)) {
+    using N3 = Net<128, 128, 128, 128>;
+    o.fwd = (prefer_pair() && !training) ? &launch_fwd2<N3, 2, 4> : &launch_fwd<N3, 2, 4>;
+    o.bwd = &launch_bwd<N3>;
+    o.bwd_ws = &bwd_workspace<N3>;
+  } else if (shape_is<32, 64, 64, 64, 64, 16>(s)) {
+    o.fwd = &launch_fwd<Net<32, 64, 64, 64, 64, 16>, 2, 4>;
+  } else if (shape_is<64, 64, 64, 64>(s)) {
+    o.fwd = &launch_fwd<Net<64, 64, 64, 64>, 2, 4>;
+  }
+  return o;
 }
 
 int check_shape(const mlpk_shape* s) {
@@ -229,11 +314,18 @@ const char* mlpk_status_string(int status) {
 
 int mlpk_shape_supported(const mlpk_shape* shape) {
   if (check_shape(shape) != MLPK_OK) return 0;
-  return pick_fwd(shape) != nullptr ? 1 : 0;
+  return pick_ops(shape, false).fwd != nullptr ? 1 : 0;
 }
 
-int mlpk_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W, void* out,
-             mlpk_stream_t stream) {
+int mlpk_train_supported(const mlpk_shape* shape) {
+  if (check_shape(shape) != MLPK_OK) return 0;
+  const ShapeOps o = pick_ops(shape, true);
+  return (o.fwd != nullptr && o.bwd != nullptr) ? 1 : 0;
+}
+
+namespace {
+int check_fwd_args(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
+                   const void* out) {
   int rc = check_shape(shape);
   if (rc) return rc;
   if (M < 0) return MLPK_ERR_SHAPE;
@@ -244,9 +336,110 @@ int mlpk_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* cons
     if (!aligned16(W[l])) return MLPK_ERR_ALIGN;
   }
   if (!aligned16(x) || !aligned16(out)) return MLPK_ERR_ALIGN;
-  Fwd f = pick_fwd(shape);
+  return MLPK_OK;
+}
+}  // namespace
+
+int mlpk_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W, void* out,
+             mlpk_stream_t stream) {
+  int rc = check_fwd_args(shape, M, x, W, out);
+  if (rc) return rc;
+  Fwd f = pick_ops(shape, false).fwd;
   if (!f) return MLPK_ERR_UNSUPPORTED;
-  return f(x, W, out, M, static_cast<cudaStream_t>(stream));
+  return f(x, W, out, M, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int mlpk_train_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
+                   void* out, void* const* h_saved, mlpk_stream_t stream) {
+  int rc = check_fwd_args(shape, M, x, W, out);
+  if (rc) return rc;
+  if (!h_saved) return MLPK_ERR_NULL;
+  for (int l = 0; l + 1 < shape->num_layers; ++l) {
+    if (M > 0 && !h_saved[l]) return MLPK_ERR_NULL;
+    if (!aligned16(h_saved[l])) return MLPK_ERR_ALIGN;
+  }
+  const ShapeOps o = pick_ops(shape, true);
+  if (!o.fwd || !o.bwd) return MLPK_ERR_UNSUPPORTED;
+  return o.fwd(x, W, out, M, h_saved, static_cast<cudaStream_t>(stream));
+}
+
+int64_t mlpk_bwd_workspace_size(const mlpk_shape* shape, int64_t M) {
+  if (check_shape(shape) != MLPK_OK || M < 0) return -1;
+  const ShapeOps o = pick_ops(shape, true);
+  if (!o.bwd_ws) return -1;
+  DevInfo di;
+  if (current_device_info(&di, nullptr) != MLPK_OK) return -1;
+  return static_cast<int64_t>(o.bwd_ws(M, di.sm_count));
+}
+
+int mlpk_bwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
+             const void* const* h_saved, const void* grad_out, void* dx, void* workspace,
+             int64_t workspace_bytes, float* dW, mlpk_stream_t stream) {
+  int rc = check_fwd_args(shape, M, x, W, grad_out);
+  if (rc) return rc;
+  if (!dW || (M > 0 && (!dx || !h_saved || !workspace))) return MLPK_ERR_NULL;
+  if (!aligned16(dx) || !aligned16(dW) || !aligned16(workspace)) return MLPK_ERR_ALIGN;
+  for (int l = 0; M > 0 && l + 1 < shape->num_layers; ++l) {
+    if (!h_saved[l]) return MLPK_ERR_NULL;
+    if (!aligned16(h_saved[l])) return MLPK_ERR_ALIGN;
+  }
+  if (workspace_bytes < 0) return MLPK_ERR_SHAPE;
+  const ShapeOps o = pick_ops(shape, true);
+  if (!o.bwd) return MLPK_ERR_UNSUPPORTED;
+  return o.bwd(x, W, h_saved, grad_out, dx, static_cast<float*>(workspace),
+               static_cast<size_t>(workspace_bytes), dW, M, static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+int make_wn_shape(const mlpk_shape* s, mlpk::WnShape* w) {
+  int rc = check_shape(s);
+  if (rc) return rc;
+  w->num_layers = s->num_layers;
+  long long vo = 0;
+  int go = 0;
+  for (int l = 0; l < s->num_layers; ++l) {
+    w->din[l] = s->dims[l];
+    w->dout[l] = s->dims[l + 1];
+    w->voff[l] = vo;
+    w->goff[l] = go;
+    vo += static_cast<long long>(s->dims[l]) * s->dims[l + 1];
+    go += s->dims[l + 1];
+  }
+  w->total_cols = go;
+  return MLPK_OK;
+}
+}  // namespace
+
+int mlpk_wn_fwd(const mlpk_shape* shape, const float* v_all, const float* g_all, void* const* W,
+                float* inv_norm, mlpk_stream_t stream) {
+  mlpk::WnShape ws;
+  int rc = make_wn_shape(shape, &ws);
+  if (rc) return rc;
+  if (!v_all || !g_all || !W || !inv_norm) return MLPK_ERR_NULL;
+  mlpk::WnOut out;
+  for (int l = 0; l < shape->num_layers; ++l) {
+    if (!W[l]) return MLPK_ERR_NULL;
+    out.w[l] = static_cast<__half*>(W[l]);
+  }
+  DevInfo di;
+  if ((rc = current_device_info(&di, nullptr)) != MLPK_OK) return rc;
+  mlpk::mlp_wn_fwd_kernel<<<(ws.total_cols + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      ws, v_all, g_all, out, inv_norm);
+  return cudaGetLastError() == cudaSuccess ? MLPK_OK : MLPK_ERR_CUDA;
+}
+
+int mlpk_wn_bwd(const mlpk_shape* shape, const float* dW_all, const float* v_all,
+                const float* g_all, const float* inv_norm, float* dv_all, float* dg_all,
+                mlpk_stream_t stream) {
+  mlpk::WnShape ws;
+  int rc = make_wn_shape(shape, &ws);
+  if (rc) return rc;
+  if (!dW_all || !v_all || !g_all || !inv_norm || !dv_all || !dg_all) return MLPK_ERR_NULL;
+  DevInfo di;
+  if ((rc = current_device_info(&di, nullptr)) != MLPK_OK) return rc;
+  mlpk::mlp_wn_bwd_kernel<<<(ws.total_cols + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      ws, dW_all, v_all, g_all, inv_norm, dv_all, dg_all);
+  return cudaGetLastError() == cudaSuccess ? MLPK_OK : MLPK_ERR_CUDA;
 }
 
 int mlpk_device_status(int clear, int* status_out) {

@@ -1,0 +1,240 @@
+"""Module API: FusedMLPSoftplus and FusedMLPSoftplusWN (training + inference).
+
+Mirrors the reference's module surface (README.md:58-70): constructed as
+``FusedMLPSoftplus(D=128, H=128, out_features=128)``, moved with
+``.cuda().half()``, called as ``model(x)`` followed by ``loss.backward()``.
+The reference's classes live in fused_mlp.py / fused_mlp5.py, which its
+published tree does not contain (README.md:18-19); their behaviour is known
+from mlp_fused.md:52-172 and mlp_fused.md:461-486, and is restated here:
+
+* one autograd.Function per model, with ``torch.amp.custom_fwd(device_type=
+  "cuda", cast_inputs=torch.float16)`` / ``custom_bwd`` (mlp_fused.md:168-172);
+* forward = one fused kernel launch that also saves the hidden activations;
+  backward = one fused kernel (data gradients + weight gradients) plus a
+  fixed-order reduction, called through the C ABI -- no per-op Python dispatch
+  (the cost the reference reports at mlp_fused.md:272-280);
+* the weight-norm model keeps all directions and gains in two contiguous
+  parameters ``v_all`` / ``g_all`` (mlp_fused.md:478-480) and normalises every
+  layer in one launch per direction.
+
+``num_layers`` selects the depth (3 or 5 in the reference; README.md:9); all
+hidden layers have width H.  Data-parallel training: pass a
+``torch.distributed`` process group and the fp32 weight gradients are
+all-reduced (sum) on the current stream between the backward kernel and the
+weight-norm backward (so every rank applies the same update).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+from .functional import _aligned
+
+
+def _dims(D: int, H: int, out_features: int, num_layers: int):
+    if num_layers < 2:
+        raise ValueError("num_layers must be >= 2")
+    return tuple([D] + [H] * (num_layers - 1) + [out_features])
+
+
+def _stream(dev):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _train_forward(x: torch.Tensor, ws, dims):
+    """Launch mlpk_train_fwd: returns (out, [h_1..h_{L-1}])."""
+    M = x.shape[0]
+    out = torch.empty((M, dims[-1]), device=x.device, dtype=torch.float16)
+    hs = [torch.empty((M, d), device=x.device, dtype=torch.float16) for d in dims[1:-1]]
+    if M > 0:
+        lib = _lib.lib()
+        rc = lib.mlpk_train_fwd(ctypes.byref(_lib.shape_struct(dims)), M, x.data_ptr(),
+                                _lib.ptr_array([w.data_ptr() for w in ws]), out.data_ptr(),
+                                _lib.ptr_array([h.data_ptr() for h in hs]), _stream(x.device))
+        _lib.check("mlpk_train_fwd", rc)
+    return out, hs
+
+
+def _backward(x, ws, hs, grad_out, dims, process_group=None):
+    """Launch mlpk_bwd: returns (dx fp16, dW_flat fp32)."""
+    M = x.shape[0]
+    lib = _lib.lib()
+    shape = _lib.shape_struct(dims)
+    g = _aligned(grad_out.to(torch.float16))
+    dx = torch.empty_like(x)
+    nflat = sum(a * b for a, b in zip(dims[:-1], dims[1:]))
+    dw = torch.empty(nflat, device=x.device, dtype=torch.float32)
+    wsb = lib.mlpk_bwd_workspace_size(ctypes.byref(shape), M)
+    if wsb < 0:
+        raise _lib.MlpkError("mlpk_bwd_workspace_size", 2)
+    work = torch.empty(max(int(wsb), 16), device=x.device, dtype=torch.uint8)
+    rc = lib.mlpk_bwd(ctypes.byref(shape), M, x.data_ptr(),
+                      _lib.ptr_array([w.data_ptr() for w in ws]),
+                      _lib.ptr_array([h.data_ptr() for h in hs]), g.data_ptr(), dx.data_ptr(),
+                      work.data_ptr(), int(work.numel()), dw.data_ptr(), _stream(x.device))
+    _lib.check("mlpk_bwd", rc)
+    if process_group is not None:
+        import torch.distributed as dist
+
+        dist.all_reduce(dw, op=dist.ReduceOp.SUM, group=process_group)
+    return dx, dw
+
+
+def _split_flat(flat: torch.Tensor, dims):
+    out, off = [], 0
+    for a, b in zip(dims[:-1], dims[1:]):
+        out.append(flat[off:off + a * b].view(a, b))
+        off += a * b
+    return out
+
+
+def _check_input(x: torch.Tensor, d0: int) -> torch.Tensor:
+    if not x.is_cuda:
+        raise RuntimeError("fused MLP runs on CUDA (sm_100) only; got a CPU tensor")
+    if x.dim() != 2 or x.shape[1] != d0:
+        raise ValueError(f"x must be [M, {d0}]")
+    return _aligned(x.to(torch.float16))
+
+
+class _FusedMLPFn(torch.autograd.Function):
+    @staticmethod
+    @torch.amp.custom_fwd(device_type="cuda", cast_inputs=torch.float16)
+    def forward(ctx, x, dims, process_group, *weights):
+        x = _check_input(x, dims[0])
+        ws = [_aligned(w.to(torch.float16)) for w in weights]
+        out, hs = _train_forward(x, ws, dims)
+        ctx.dims = dims
+        ctx.process_group = process_group
+        ctx.w_dtypes = [w.dtype for w in weights]
+        ctx.save_for_backward(x, *ws, *hs)
+        return out
+
+    @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
+    def backward(ctx, grad_out):
+        dims = ctx.dims
+        L = len(dims) - 1
+        saved = ctx.saved_tensors
+        x, ws, hs = saved[0], list(saved[1:1 + L]), list(saved[1 + L:])
+        dx, dw = _backward(x, ws, hs, grad_out, dims, ctx.process_group)
+        dws = [d.to(t) for d, t in zip(_split_flat(dw, dims), ctx.w_dtypes)]
+        return (dx if ctx.needs_input_grad[0] else None, None, None, *dws)
+
+
+class _FusedMLPWNFn(torch.autograd.Function):
+    @staticmethod
+    @torch.amp.custom_fwd(device_type="cuda", cast_inputs=torch.float16)
+    def forward(ctx, x, dims, process_group, v_all, g_all):
+        x = _check_input(x, dims[0])
+        lib = _lib.lib()
+        shape = _lib.shape_struct(dims)
+        v32 = _aligned(v_all.detach().to(torch.float32))
+        g32 = _aligned(g_all.detach().to(torch.float32))
+        ws = [torch.empty((a, b), device=x.device, dtype=torch.float16)
+              for a, b in zip(dims[:-1], dims[1:])]
+        inv = torch.empty_like(g32)
+        rc = lib.mlpk_wn_fwd(ctypes.byref(shape), v32.data_ptr(), g32.data_ptr(),
+                             _lib.ptr_array([w.data_ptr() for w in ws]), inv.data_ptr(),
+                             _stream(x.device))
+        _lib.check("mlpk_wn_fwd", rc)
+        out, hs = _train_forward(x, ws, dims)
+        ctx.dims = dims
+        ctx.process_group = process_group
+        ctx.dtypes = (v_all.dtype, g_all.dtype)
+        ctx.save_for_backward(x, v32, g32, inv, *ws, *hs)
+        return out
+
+    @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
+    def backward(ctx, grad_out):
+        dims = ctx.dims
+        L = len(dims) - 1
+        saved = ctx.saved_tensors
+        x, v32, g32, inv = saved[:4]
+        ws, hs = list(saved[4:4 + L]), list(saved[4 + L:])
+        dx, dw = _backward(x, ws, hs, grad_out, dims, ctx.process_group)
+        dv = torch.empty_like(v32)
+        dg = torch.empty_like(g32)
+        lib = _lib.lib()
+        rc = lib.mlpk_wn_bwd(ctypes.byref(_lib.shape_struct(dims)), dw.data_ptr(), v32.data_ptr(),
+                             g32.data_ptr(), inv.data_ptr(), dv.data_ptr(), dg.data_ptr(),
+                             _stream(x.device))
+        _lib.check("mlpk_wn_bwd", rc)
+        return (dx if ctx.needs_input_grad[0] else None, None, None,
+                dv.to(ctx.dtypes[0]), dg.to(ctx.dtypes[1]))
+
+
+class FusedMLPSoftplus(nn.Module):
+    """``softplus(...softplus(x @ W_1)...) @ W_L`` with fused training kernels.
+
+    Weights are ``[in, out]`` parameters ``w1 .. wL`` initialised
+    U(-1/sqrt(in), 1/sqrt(in)).
+    """
+
+    def __init__(self, D: int = 128, H: int = 128, out_features: int = 128, num_layers: int = 3,
+                 process_group=None):
+        super().__init__()
+        self.dims = _dims(D, H, out_features, num_layers)
+        self.process_group = process_group
+        for i, (a, b) in enumerate(zip(self.dims[:-1], self.dims[1:])):
+            w = torch.empty(a, b)
+            nn.init.uniform_(w, -1.0 / math.sqrt(a), 1.0 / math.sqrt(a))
+            self.register_parameter(f"w{i + 1}", nn.Parameter(w))
+
+    @property
+    def weights(self):
+        return [getattr(self, f"w{i + 1}") for i in range(len(self.dims) - 1)]
+
+    def forward(self, x):
+        return _FusedMLPFn.apply(x, self.dims, self.process_group, *self.weights)
+
+
+class FusedMLPSoftplusWN(nn.Module):
+    """Weight-normalised fused MLP: ``W_l = g_l * v_l / ||v_l||`` per output column.
+
+    ``v_all`` holds every v_l ([in, out], row-major) back to back, ``g_all``
+    every g_l; at construction v_l ~ U(+-1/sqrt(in)) and g_l = ||v_l||, so the
+    effective weights start equal to v.  ``weight(l)`` returns the effective
+    W_l.
+    """
+
+    def __init__(self, D: int = 128, H: int = 128, out_features: int = 128, num_layers: int = 3,
+                 process_group=None):
+        super().__init__()
+        self.dims = _dims(D, H, out_features, num_layers)
+        self.process_group = process_group
+        vs, gs = [], []
+        for a, b in zip(self.dims[:-1], self.dims[1:]):
+            v = torch.empty(a, b)
+            nn.init.uniform_(v, -1.0 / math.sqrt(a), 1.0 / math.sqrt(a))
+            vs.append(v.reshape(-1))
+            gs.append(v.norm(dim=0))
+        self.v_all = nn.Parameter(torch.cat(vs))
+        self.g_all = nn.Parameter(torch.cat(gs))
+
+    def v(self, l: int) -> torch.Tensor:
+        off = sum(a * b for a, b in zip(self.dims[:l], self.dims[1:l + 1]))
+        a, b = self.dims[l], self.dims[l + 1]
+        return self.v_all[off:off + a * b].view(a, b)
+
+    def g(self, l: int) -> torch.Tensor:
+        off = sum(self.dims[1:l + 1])
+        return self.g_all[off:off + self.dims[l + 1]]
+
+    def weight(self, l: int) -> torch.Tensor:
+        v = self.v(l).float()
+        return self.g(l).float() * v / v.norm(dim=0, keepdim=True)
+
+    @torch.no_grad()
+    def load_weights(self, weights):
+        """Set v = W and g = ||W|| (per column) from plain [in, out] weights."""
+        for l, w in enumerate(weights):
+            self.v(l).copy_(w)
+            self.g(l).copy_(w.float().norm(dim=0))
+
+    def forward(self, x):
+        return _FusedMLPWNFn.apply(x, self.dims, self.process_group, self.v_all, self.g_all)
