@@ -44,7 +44,8 @@ enum {
   MLPK_ERR_CUDA = 4,        /* a CUDA runtime/driver call failed */
   MLPK_ERR_ALIGN = 5,       /* a pointer is not 16-byte aligned */
   MLPK_ERR_NULL = 6,        /* a required pointer is NULL */
-  MLPK_ERR_DEVICE = 7       /* a kernel recorded a device-side error */
+  MLPK_ERR_DEVICE = 7,      /* a kernel recorded a device-side error */
+  MLPK_ERR_SCRATCH = 8      /* mlpk_bwd_noalloc: problem exceeds its static scratch */
 };
 
 /* Human-readable text for a status code. */
@@ -97,6 +98,25 @@ int mlpk_wn_fwd(const mlpk_shape* shape, const float* v_all, const float* g_all,
 int mlpk_wn_bwd(const mlpk_shape* shape, const float* dW_all, const float* v_all,
                 const float* g_all, const float* inv_norm, float* dv_all, float* dg_all,
                 mlpk_stream_t stream);
+
+/* Allocation-free backward.  No counterpart in the reference: it exists for
+ * callers that cannot allocate device memory at the time they call it (code
+ * running under CUDA stream capture, plain C / FFI callers that own only their
+ * input and output buffers, serving processes whose memory is fixed at
+ * start-up).  Same arguments and results as mlpk_bwd minus the workspace: the
+ * per-CTA weight-gradient partials live in a static device array of
+ * MLPK_BWD_NOALLOC_SCRATCH_BYTES (32 MiB) that every GPU which loads the
+ * library holds until the process exits.  Returns MLPK_ERR_SCRATCH when the
+ * problem needs more than that (mlpk_bwd_workspace_size > 32 MiB; 3L128 on a
+ * 148-SM B200 needs at most 29 MB).  Calls no allocator.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture.  All calls
+ * share the array, so calls that overlap on the GPU (other streams, other
+ * host threads) race: serialise them. */
+#define MLPK_BWD_NOALLOC_SCRATCH_BYTES (32u << 20)
+int mlpk_bwd_noalloc(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
+                     const void* const* h_saved, const void* grad_out, void* dx, float* dW,
+                     mlpk_stream_t stream);
 
 /* Reads (and optionally clears) the device-side status word of the current
  * device: bit flags set by bounded waits that expired.  Synchronises. */

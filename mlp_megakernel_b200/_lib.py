@@ -24,6 +24,7 @@ STATUS_NAMES = {
     5: "MLPK_ERR_ALIGN",
     6: "MLPK_ERR_NULL",
     7: "MLPK_ERR_DEVICE",
+    8: "MLPK_ERR_SCRATCH",
 }
 
 # Every symbol declared in include/mlpk.h, with (restype, argtypes).
@@ -46,6 +47,8 @@ SIGNATURES = {
     "mlpk_bwd_workspace_size": (ctypes.c_int64, [_SHAPE_P, ctypes.c_int64]),
     "mlpk_bwd": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _VPP, _vp, _vp, _vp,
                                 ctypes.c_int64, _vp, _vp]),
+    "mlpk_bwd_noalloc": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _VPP, _vp, _vp, _vp,
+                                        _vp]),
     "mlpk_wn_fwd": (ctypes.c_int, [_SHAPE_P, _vp, _vp, _VPP, _vp, _vp]),
     "mlpk_wn_bwd": (ctypes.c_int, [_SHAPE_P, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "mlpk_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),

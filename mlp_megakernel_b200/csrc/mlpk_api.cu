@@ -308,6 +308,8 @@ const char* mlpk_status_string(int status) {
     case MLPK_ERR_ALIGN: return "pointer not 16-byte aligned";
     case MLPK_ERR_NULL: return "required pointer is NULL";
     case MLPK_ERR_DEVICE: return "kernel recorded a device-side error";
+    case MLPK_ERR_SCRATCH:
+      return "problem needs more scratch than the allocation-free entry point's static buffer";
     default: return "unknown status";
   }
 }
@@ -440,6 +442,57 @@ int mlpk_wn_bwd(const mlpk_shape* shape, const float* dW_all, const float* v_all
   mlpk::mlp_wn_bwd_kernel<<<(ws.total_cols + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
       ws, dW_all, v_all, g_all, inv_norm, dv_all, dg_all);
   return cudaGetLastError() == cudaSuccess ? MLPK_OK : MLPK_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------ allocation-free backward
+// Backward for callers that cannot allocate device memory when they call it
+// (code running under CUDA stream capture, plain C / FFI callers that own only
+// their input and output buffers, serving processes whose device memory is
+// fixed at start-up).  Instead of a caller-provided workspace, the per-CTA
+// weight-gradient partials live in this file-scope array, which every GPU that
+// loads the library holds until the process exits.
+}  // extern "C"
+
+static __device__ __align__(256) unsigned char g_bwd_noalloc_scratch[MLPK_BWD_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+void* g_noalloc_scratch_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// The device address of the scratch array on the current device.  In host
+// code the array's name is only a host-side stand-in, so the address is looked
+// up once per device (with that device current) and cached.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MLPK_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_scratch_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_bwd_noalloc_scratch) != cudaSuccess || p == nullptr)
+      return MLPK_ERR_CUDA;
+    g_noalloc_scratch_ptr[dev] = p;
+  }
+  *out = g_noalloc_scratch_ptr[dev];
+  return MLPK_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int mlpk_bwd_noalloc(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
+                     const void* const* h_saved, const void* grad_out, void* dx, float* dW,
+                     mlpk_stream_t stream) {
+  const int64_t need = mlpk_bwd_workspace_size(shape, M);
+  if (need < 0) return check_shape(shape) != MLPK_OK || M < 0 ? MLPK_ERR_SHAPE : MLPK_ERR_UNSUPPORTED;
+  if (need > static_cast<int64_t>(MLPK_BWD_NOALLOC_SCRATCH_BYTES)) return MLPK_ERR_SCRATCH;
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != MLPK_OK) return rc;
+  // Every call reuses the same array: the backward kernel overwrites the
+  // partials of every CTA it launches before the reduction reads them, so no
+  // stale contents from an earlier call are ever read.
+  return mlpk_bwd(shape, M, x, W, h_saved, grad_out, dx, scratch,
+                  static_cast<int64_t>(MLPK_BWD_NOALLOC_SCRATCH_BYTES), dW, stream);
 }
 
 int mlpk_device_status(int clear, int* status_out) {

@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol(built_lib):
 
 def test_status_strings(built_lib):
     assert _lib.status_string(0) == "ok"
-    for code in range(1, 8):
+    for code in range(1, 9):
         assert _lib.status_string(code) != "unknown status"
 
 
