@@ -39,6 +39,9 @@ BYTES_PER_ROW = 2 * (DIMS[0] + DIMS[-1])                     # x in + out out, f
 FLOP_PER_ROW = 2 * sum(a * b for a, b in zip(DIMS[:-1], DIMS[1:]))
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 FWD_KERNEL = "mlp_fwd_kernel"
+TRAIN_ROWS = 262144                                           # BASELINE config 3 (split-K regime)
+TRAIN_BYTES_PER_ROW = 2 * (2 * DIMS[0] + 2 * DIMS[-1])        # x, out, grad_out, dx (fp16)
+TRAIN_FLOP_PER_ROW = 3 * FLOP_PER_ROW                         # forward, dgrad, wgrad
 
 
 def parse_args():
@@ -51,6 +54,9 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--train-rows", type=int, default=TRAIN_ROWS, help="training rows per GPU")
+    ap.add_argument("--train-steps", type=int, default=50)
+    ap.add_argument("--no-train", action="store_true")
     return ap.parse_args()
 
 
@@ -290,6 +296,8 @@ def run_mlpk(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
+    train = None if args.no_train else run_training(args, world, rank, dist, barrier)
+
     clocks = clk.summary()
     if dist is not None:
         dist.destroy_process_group()
@@ -345,6 +353,8 @@ def run_mlpk(args):
         "gpu_launches": args.steps,
         "clocks": clocks,
     }
+    if train is not None:
+        line["fwd_bwd"] = train
     if world == 1 and not args.no_cpu_baseline:
         rows = 65536
         rps, cores, calls, dt = cpu_forward_rows_per_s(rows, args.cpu_seconds)
@@ -354,6 +364,133 @@ def run_mlpk(args):
                       f"reference PyTorch formula (kernel.py:163-171) in fp32 on {cores} threads",
         }
     print(json.dumps(line), flush=True)
+
+
+def run_training(args, world, rank, dist, barrier):
+    """one 3L128 training step with weight norm per GPU on
+    `train_rows` rows -- weight-norm forward, training forward, fused backward
+    + fixed-order dW reduction, (N > 1: NCCL all-reduce of dW), weight-norm
+    backward -- all through the C ABI on preallocated buffers."""
+    import ctypes
+
+    import torch
+
+    from mlp_megakernel_b200 import _lib
+    from mlp_megakernel_b200.synthetic import make_grad, make_weights, make_x
+
+    M = args.train_rows
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lib = _lib.lib()
+    shape = ctypes.byref(_lib.shape_struct(DIMS))
+    st = torch.cuda.current_stream().cuda_stream
+    x = make_x(M, DIMS[0], "normal", rank, device=dev)
+    g = make_grad(M, DIMS[-1], seed=2 + rank, device=dev)
+    ws0 = make_weights(DIMS, device=dev)
+    v_all = torch.cat([w.float().reshape(-1) for w in ws0]).contiguous()
+    g_all = torch.cat([w.float().norm(dim=0) for w in ws0]).contiguous()
+    W = [torch.empty_like(w) for w in ws0]
+    inv = torch.empty_like(g_all)
+    out = torch.empty((M, DIMS[-1]), dtype=torch.float16, device=dev)
+    hs = [torch.empty((M, d), dtype=torch.float16, device=dev) for d in DIMS[1:-1]]
+    dx = torch.empty_like(x)
+    dw = torch.empty_like(v_all)
+    dv = torch.empty_like(v_all)
+    dg = torch.empty_like(g_all)
+    work = torch.empty(int(lib.mlpk_bwd_workspace_size(shape, M)), dtype=torch.uint8, device=dev)
+    Wp = _lib.ptr_array([w.data_ptr() for w in W])
+    Hp = _lib.ptr_array([h.data_ptr() for h in hs])
+
+    def step():
+        _lib.check("wn_fwd", lib.mlpk_wn_fwd(shape, v_all.data_ptr(), g_all.data_ptr(), Wp,
+                                             inv.data_ptr(), st))
+        _lib.check("train_fwd", lib.mlpk_train_fwd(shape, M, x.data_ptr(), Wp, out.data_ptr(), Hp, st))
+        _lib.check("bwd", lib.mlpk_bwd(shape, M, x.data_ptr(), Wp, Hp, g.data_ptr(), dx.data_ptr(),
+                                       work.data_ptr(), work.numel(), dw.data_ptr(), st))
+        if dist is not None:
+            dist.all_reduce(dw)
+        _lib.check("wn_bwd", lib.mlpk_wn_bwd(shape, dw.data_ptr(), v_all.data_ptr(), g_all.data_ptr(),
+                                             inv.data_ptr(), dv.data_ptr(), dg.data_ptr(), st))
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.train_steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if _lib.device_status() != 0:
+        raise RuntimeError("device status set during the training timing")
+
+    # e2e: x and grad_out from pinned host memory, gradients (dv, dg) back to host
+    xh, gh = x.cpu().pin_memory(), g.cpu().pin_memory()
+    dvh = torch.empty(dv.shape, dtype=dv.dtype, pin_memory=True)
+    dgh = torch.empty(dg.shape, dtype=dg.dtype, pin_memory=True)
+
+    def e2e_step():
+        x.copy_(xh, non_blocking=True)
+        g.copy_(gh, non_blocking=True)
+        step()
+        dvh.copy_(dv, non_blocking=True)
+        dgh.copy_(dg, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    n_e2e = 5
+    e2.record()
+    for _ in range(n_e2e):
+        e2e_step()
+    e3.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e2.elapsed_time(e3)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    peaks = load_peaks()
+    per_step = ms / 1e3 / args.train_steps
+    tflops = TRAIN_FLOP_PER_ROW * M / per_step / 1e12
+    gbs = TRAIN_BYTES_PER_ROW * M / per_step / 1e9
+    roof_rows = min(peaks["bf16_tflops"] * 1e12 / TRAIN_FLOP_PER_ROW,
+                    peaks["hbm_gbs"] * 1e9 / TRAIN_BYTES_PER_ROW)
+    return {
+        "metric": "fused MLP fwd+bwd rows/s (3L128 with weight norm)",
+        "value": world * M * args.train_steps / (ms / 1e3),
+        "unit": "rows/s",
+        "steps": args.train_steps,
+        "ms_per_step": ms / args.train_steps,
+        "config": {"workload": f"BASELINE config 3: 3L D=H=OUT=128 training step with weight "
+                               f"norm, M={M} rows per GPU",
+                   "rows_per_gpu": M, "parallelism": f"dp{world}" + (" (NCCL all-reduce of fp32 dW)"
+                                                                       if world > 1 else ""),
+                   "l2": "inputs larger than L2 (x, grad_out, saved h: 64 MiB each)"},
+        "roofline": {"bound": "tensor" if roof_rows < peaks["hbm_gbs"] * 1e9 / TRAIN_BYTES_PER_ROW
+                     else "hbm",
+                     "achieved": tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": tflops / peaks["bf16_tflops"],
+                     "rows_frac_of_roofline": (M / per_step) / roof_rows,
+                     "achieved_algorithmic_gbs": gbs, "traffic": None,
+                     "flop_per_row": TRAIN_FLOP_PER_ROW, "algorithmic_bytes_per_row": TRAIN_BYTES_PER_ROW},
+        "e2e": {"value": world * M * n_e2e / (e2e_ms / 1e3), "unit": "rows/s",
+                "h2d_bytes_per_step": 2 * M * DIMS[0] * 2,
+                "d2h_bytes_per_step": (dv.numel() + dg.numel()) * 4,
+                "api": "C ABI (mlpk_wn_fwd, mlpk_train_fwd, mlpk_bwd, mlpk_wn_bwd) with pinned host buffers"},
+        "gpu_launches": 5 * args.train_steps,
+    }
 
 
 def main():
