@@ -122,6 +122,13 @@ int mlpk_bwd_noalloc(const mlpk_shape* shape, int64_t M, const void* x, const vo
  * device: bit flags set by bounded waits that expired.  Synchronises. */
 int mlpk_device_status(int clear, int* status_out);
 
+/* Text of the CUDA runtime / driver failure behind the calling thread's most
+ * recent MLPK_ERR_CUDA ("no error" if none).  The reference reports failures as
+ * Python exceptions carrying the CUDA message (cutile_mlp.py:388); this is the
+ * message for the C caller.  The string stays valid until the thread's next
+ * failing call. */
+const char* mlpk_last_cuda_error(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(HERE, "lib", "libmlpk.so")
 MAX_LAYERS = 8
 
 MLPK_OK = 0
+MLPK_ERR_CUDA = 4
 STATUS_NAMES = {
     0: "MLPK_OK",
     1: "MLPK_ERR_SHAPE",
@@ -52,6 +53,7 @@ SIGNATURES = {
     "mlpk_wn_fwd": (ctypes.c_int, [_SHAPE_P, _vp, _vp, _VPP, _vp, _vp]),
     "mlpk_wn_bwd": (ctypes.c_int, [_SHAPE_P, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "mlpk_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    "mlpk_last_cuda_error": (ctypes.c_char_p, []),
 }
 
 _lock = threading.Lock()
@@ -64,7 +66,10 @@ class MlpkError(RuntimeError):
     def __init__(self, fn: str, status: int):
         self.status = status
         name = STATUS_NAMES.get(status, str(status))
-        super().__init__(f"{fn} failed: {name} ({status_string(status)})")
+        msg = f"{fn} failed: {name} ({status_string(status)})"
+        if status == MLPK_ERR_CUDA:
+            msg += f": {lib().mlpk_last_cuda_error().decode()}"
+        super().__init__(msg)
 
 
 def lib() -> ctypes.CDLL:

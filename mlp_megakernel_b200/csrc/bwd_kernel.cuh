@@ -48,30 +48,52 @@ struct BwdCfg {
   static constexpr int D0 = NetT::template D<0>();
   static constexpr int DL = NetT::template D<L>();
   static constexpr int H = NetT::template D<1>();
-  static constexpr int DMAX = [] {
-    int m = 0;
-    for (int v : {NetT::template D<0>(), NetT::max_hidden_or_out()}) m = v > m ? v : m;
-    return m;
-  }();
+  static constexpr int DMAX = D0 > NetT::max_hidden_or_out() ? D0 : NetT::max_hidden_or_out();
+  // Weight-gradient plan of layer l: UMMA M must be 64 or 128 and the
+  // accumulator is read with the M = 128 layout (TMEM lane = row), so the GEMM
+  // runs in the orientation with the wider M (dW_l = h_l^T dz, or, when
+  // d_l < 64, dW_l^T = dz^T h_l), and an M of 64 is padded to 128 with a zeroed
+  // shared-memory chunk (rows 64..127 of that accumulator stay zero).
+  __host__ __device__ static constexpr bool wg_trans(int l) { return NetT::dim(l) < 64; }
+  __host__ __device__ static constexpr int wg_m(int l) {
+    return wg_trans(l) ? NetT::dim(l + 1) : NetT::dim(l);
+  }
+  __host__ __device__ static constexpr int wg_n(int l) {
+    return wg_trans(l) ? NetT::dim(l) : NetT::dim(l + 1);
+  }
+  __host__ __device__ static constexpr bool wg_pad(int l) { return wg_m(l) < 128; }
+  __host__ __device__ static constexpr bool any_pad() {
+    for (int l = 0; l < L; ++l)
+      if (wg_pad(l)) return true;
+    return false;
+  }
+  __host__ __device__ static constexpr bool plans_ok() {
+    for (int l = 0; l < L; ++l) {
+      if (wg_m(l) != 64 && wg_m(l) != 128) return false;
+      if (wg_n(l) % 16 != 0 || wg_n(l) < 16 || wg_n(l) > 256) return false;
+    }
+    return true;
+  }
+  // TMEM: dW_l (wg_n(l) columns each), then the dgrad accumulator
+  __host__ __device__ static constexpr int dw_col(int l) {
+    int c = 0;
+    for (int i = 0; i < l; ++i) c += wg_n(i);
+    return c;
+  }
   static constexpr int TILE_BYTES = align_up(tile_bytes(kTileM, DMAX), 1024);
   static constexpr int W_TOTAL = NetT::w_total();
   static constexpr int OFF_G = W_TOTAL;
   static constexpr int OFF_X = OFF_G + TILE_BYTES;
   static constexpr int OFF_H = OFF_X + TILE_BYTES;                 // h_1 .. h_{L-1}
-  static constexpr int OFF_BAR = OFF_H + (L - 1) * TILE_BYTES;
-  // barriers: w_full, g_full, g_empty, x_full, x_empty, h_full[L-1], h_empty[L-1],
-  //           acc_full, dz_full, acc_free, out_ready, mma_done
+  static constexpr int OFF_ZERO = OFF_H + (L - 1) * TILE_BYTES;    // zero chunk (M padding)
+  static constexpr int ZERO_BYTES = any_pad() ? 16384 : 0;         // 128 rows x 128 B
+  static constexpr int OFF_BAR = OFF_ZERO + ZERO_BYTES;
+  // barriers: w_full, g_full, g_empty, x_full, x_empty, acc_full, dz_full,
+  //           acc_free, out_ready, mma_done, h_full[L-1], h_empty[L-1]
   static constexpr int NUM_BARS = 10 + 2 * (L - 1);
   static constexpr int OFF_MISC = OFF_BAR + 8 * NUM_BARS;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
-  // TMEM: dW_l at cumulative columns, then the dgrad accumulator
-  template <int l>
-  __host__ __device__ static constexpr int dw_col() {
-    int c = 0;
-    for (int i = 0; i < l; ++i) c += NetT::dim(i + 1);
-    return c;
-  }
-  static constexpr int ACC_COL = dw_col<L>();
+  static constexpr int ACC_COL = dw_col(L);
   static constexpr int TMEM_COLS_RAW = ACC_COL + align_up(DMAX, 32);
   static constexpr int TMEM_COLS = TMEM_COLS_RAW <= 128 ? 128 : TMEM_COLS_RAW <= 256 ? 256 : 512;
   static constexpr int PARTIAL_FLOATS = [] {
@@ -80,9 +102,9 @@ struct BwdCfg {
     return n;
   }();
   static constexpr int THREADS = 6 * 32;
+  static_assert(plans_ok(), "weight-gradient GEMM shapes not supported");
+  static_assert(NetT::hidden_uniform(), "all hidden layers must have the same width");
   static_assert(TMEM_COLS_RAW <= 512, "dW + dgrad accumulators exceed TMEM");
-  // wgrad UMMAs use M = d_l with the M=128 accumulator layout (lane = row)
-  static_assert(NetT::all_dims_are(128), "this backward kernel handles 128-wide layers");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
 };
 
@@ -172,6 +194,11 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
     tmem_alloc(s_tmem_slot, Cfg::TMEM_COLS);
     tmem_relinquish();
   }
+  if constexpr (Cfg::ZERO_BYTES > 0) {  // zero chunk that pads a 64-wide wgrad M to 128
+    for (int i = threadIdx.x; i < Cfg::ZERO_BYTES / 16; i += blockDim.x)
+      st_shared_v4(sbase + Cfg::OFF_ZERO + 16 * i, 0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -251,16 +278,27 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
         tc_fence_after();
         const uint32_t a_h = (l == 0) ? s_xb : s_h(l);
         if (issuer) {
-          // wgrad: dW_l[d_l x d_{l+1}] += h_l^T dz: A = h_l (MN-major), B = dz (MN-major),
-          // K = the 128 tile rows
-          constexpr uint32_t idesc_w = make_idesc_f16(DI, DO, 1, 1);
-          const uint64_t aw0 = mnmajor_base_desc<kTileM, DI>(a_h);
-          const uint64_t bw0 = mnmajor_base_desc<kTileM, DO>(s_g);
-          const uint32_t dw = tmem_base + Cfg::template dw_col<l>();
+          // wgrad over the 128 tile rows (K): dW_l += h_l^T dz (A = h_l, B = dz) or,
+          // transposed, dW_l^T += dz^T h_l (A = dz, B = h_l); both operands
+          // MN-major from shared memory; a 64-wide A is padded to M = 128 by
+          // pointing its second 64-column chunk (LBO) at the zero chunk.
+          {
+            constexpr bool TR = Cfg::wg_trans(l);
+            constexpr int MW = Cfg::wg_m(l);
+            constexpr int NW = Cfg::wg_n(l);
+            constexpr uint32_t idesc_w = make_idesc_f16(kTileM, NW, 1, 1);
+            const uint32_t a_base = TR ? s_g : a_h;
+            const uint32_t b_base = TR ? a_h : s_g;
+            constexpr int PA = pitch_bytes(MW);
+            const uint32_t lbo = (MW < 128) ? (sbase + Cfg::OFF_ZERO - a_base) : kTileM * PA;
+            const uint64_t aw0 = make_sdesc(a_base, lbo, 8 * PA, umma_layout_code(PA));
+            const uint64_t bw0 = mnmajor_base_desc<kTileM, NW>(b_base);
+            const uint32_t dw = tmem_base + Cfg::dw_col(l);
 #pragma unroll
-          for (int k = 0; k < kTileM / 16; ++k)
-            umma_f16(dw, aw0 + (mnmajor_koff<DI>(k) >> 4), bw0 + (mnmajor_koff<DO>(k) >> 4),
-                     idesc_w, (i > 0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < kTileM / 16; ++k)
+              umma_f16(dw, aw0 + (mnmajor_koff<MW>(k) >> 4), bw0 + (mnmajor_koff<NW>(k) >> 4),
+                       idesc_w, (i > 0 || k > 0) ? 1u : 0u);
+          }
           // dgrad: dh_l[128 x d_l] = dz W_l^T: A = dz (K-major, K = d_{l+1}),
           // B = W_l as stored ([d_l rows][d_{l+1}] = K-major W_l^T)
           constexpr uint32_t idesc_d = make_idesc_f16(kTileM, DI, 0, 0);
@@ -378,22 +416,37 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
       int off = 0;
       static_for<0, L>([&](auto lc) {
         constexpr int l = decltype(lc)::value;
-        constexpr int DI = NetT::template D<l>();
         constexpr int DO = NetT::template D<l + 1>();
-        const uint32_t dw = tmem_base + lane_off + Cfg::template dw_col<l>();
-        if (row < static_cast<uint32_t>(DI)) {
-          float4* dst = reinterpret_cast<float4*>(part + off + row * DO);
+        constexpr bool TR = Cfg::wg_trans(l);
+        constexpr int MW = Cfg::wg_m(l);
+        constexpr int NW = Cfg::wg_n(l);
+        const uint32_t dw = tmem_base + lane_off + Cfg::dw_col(l);
+        // lane `row` of the accumulator: row of dW_l, or (transposed) column
+        if (row < static_cast<uint32_t>(MW)) {
 #pragma unroll 1
-          for (int c = 0; c < DO; c += 16) {
+          for (int c = 0; c < NW; c += 16) {
             uint32_t r[16];
             tmem_ld_wait_x16(dw + c, r);
+            if constexpr (!TR) {
+              float4* dst = reinterpret_cast<float4*>(part + off + row * DO + c);
 #pragma unroll
-            for (int v = 0; v < 4; ++v)
-              dst[c / 4 + v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                                           __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+              for (int v = 0; v < 4; ++v)
+                dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                     __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+            } else {
+#pragma unroll
+              for (int v = 0; v < 16; ++v) part[off + (c + v) * DO + row] = __uint_as_float(r[v]);
+            }
+          }
+        } else {
+          // lanes past M still take part in the warp-wide TMEM loads
+#pragma unroll 1
+          for (int c = 0; c < NW; c += 16) {
+            uint32_t r[16];
+            tmem_ld_wait_x16(dw + c, r);
           }
         }
-        off += DI * DO;
+        off += NetT::dim(l) * DO;
       });
     }
     if (store_leader) bulk_wait_group<0>();
@@ -408,14 +461,31 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
   }
 }
 
-// Level-2 reduction: dW[e] = sum_{p < P} partials[p][e] in order p = 0..P-1.
-__global__ void mlp_reduce_kernel(const float* __restrict__ partials, int nparts, int nfloats,
-                                  float* __restrict__ dw) {
-  const int e = blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= nfloats) return;
-  float s = 0.0f;
-  for (int p = 0; p < nparts; ++p) s += partials[static_cast<size_t>(p) * nfloats + e];
-  dw[e] = s;
+// Level-2 reduction of the per-CTA partials: a block covers kReduceElems
+// elements with kReduceSlices threads each; slice s sums partials p = s,
+// s + kReduceSlices, ... in increasing p, and the slices are added in slice
+// order.  The order is fixed, so dW is bitwise reproducible.
+constexpr int kReduceElems = 64;
+constexpr int kReduceSlices = 4;
+
+__global__ void __launch_bounds__(kReduceElems * kReduceSlices)
+    mlp_reduce_kernel(const float* __restrict__ partials, int nparts, int nfloats,
+                      float* __restrict__ dw) {
+  __shared__ float red[kReduceSlices][kReduceElems];
+  const int le = threadIdx.x % kReduceElems, sl = threadIdx.x / kReduceElems;
+  const int e = blockIdx.x * kReduceElems + le;
+  float acc = 0.0f;
+  if (e < nfloats)
+    for (int p = sl; p < nparts; p += kReduceSlices)
+      acc += partials[static_cast<size_t>(p) * nfloats + e];
+  red[sl][le] = acc;
+  __syncthreads();
+  if (sl == 0 && e < nfloats) {
+    float t = red[0][le];
+#pragma unroll
+    for (int k = 1; k < kReduceSlices; ++k) t += red[k][le];
+    dw[e] = t;
+  }
 }
 
 }  // namespace mlpk

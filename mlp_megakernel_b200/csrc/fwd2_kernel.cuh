@@ -43,7 +43,7 @@ struct Fwd2Cfg {
   static constexpr int NG = EPW / 4;
   static constexpr int SPC = (HMAX / NG) / 32 >= 4 ? 2 : 1;
   static constexpr int MAXCH = ((HMAX / NG + 31) / 32 + SPC - 1) / SPC;
-  static constexpr int NUM_BARS = 5 * NS + NS * MAXCH + 2;
+  static constexpr int NUM_BARS = 6 * NS + NS * MAXCH + 2;
   static constexpr int OFF_MISC = OFF_BAR + 8 * NUM_BARS;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static constexpr int SLOT_COLS = align_up(HMAX, 32);
@@ -75,11 +75,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fwd2Cfg<NetT, NS, EP
   const uint32_t s_bar = sbase + Cfg::OFF_BAR;
   auto bar_x_full = [&](int s) { return s_bar + 8u * s; };       // leader: count 2 (+tx)
   auto bar_x_empty = [&](int s) { return s_bar + 8u * (NS + s); }; // both: commit multicast
-  auto bar_acc_full = [&](int s) { return s_bar + 8u * (2 * NS + s); };
-  auto bar_out_ready = [&](int s) { return s_bar + 8u * (3 * NS + s); };
-  auto bar_store_free = [&](int s) { return s_bar + 8u * (4 * NS + s); };
-  auto bar_chunk = [&](int s, int c) { return s_bar + 8u * (5 * NS + s * Cfg::MAXCH + c); };
-  const uint32_t bar_w_full = s_bar + 8u * (5 * NS + NS * Cfg::MAXCH);
+  // one accumulator-full barrier per slot and TMEM buffer (job g -> buffer
+  // g & 1, parity (g >> 1) & 1), as in mlp_fwd_kernel: a single barrier per slot
+  // could complete twice before a slow epilogue warp polls it
+  auto bar_acc_full = [&](int s, int b) { return s_bar + 8u * (2 * NS + 2 * s + b); };
+  auto bar_out_ready = [&](int s) { return s_bar + 8u * (4 * NS + s); };
+  auto bar_store_free = [&](int s) { return s_bar + 8u * (5 * NS + s); };
+  auto bar_chunk = [&](int s, int c) { return s_bar + 8u * (6 * NS + s * Cfg::MAXCH + c); };
+  const uint32_t bar_w_full = s_bar + 8u * (6 * NS + NS * Cfg::MAXCH);
   const uint32_t bar_mma_done = bar_w_full + 8u;
   const uint32_t s_tmem_slot = sbase + Cfg::OFF_MISC;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + Cfg::OFF_MISC + 4);
@@ -93,7 +96,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fwd2Cfg<NetT, NS, EP
     for (int s = 0; s < NS; ++s) {
       mbar_init(bar_x_full(s), 2);
       mbar_init(bar_x_empty(s), 1);
-      mbar_init(bar_acc_full(s), 1);
+      mbar_init(bar_acc_full(s, 0), 1);
+      mbar_init(bar_acc_full(s, 1), 1);
       mbar_init(bar_out_ready(s), EPW);
       mbar_init(bar_store_free(s), 1);
       for (int c = 0; c < Cfg::MAXCH; ++c) mbar_init(bar_chunk(s, c), 2 * EPW);
@@ -225,7 +229,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fwd2Cfg<NetT, NS, EP
               }
               if (!ok) break;
             }
-            if (issuer) umma_commit_pair(bar_acc_full(s), 0x3);
+            if (issuer) umma_commit_pair(bar_acc_full(s, (i * L + l) & 1), 0x3);
             __syncwarp();
           }
         });
@@ -260,7 +264,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fwd2Cfg<NetT, NS, EP
       const int row0 = (2 * pt + static_cast<int>(rank)) * kTileM;
 #pragma unroll 1
       for (int l = 0; l < L - 1; ++l) {
-        ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar_acc_full(s), (i * L + l) & 1, abort_flag,
+        ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar_acc_full(s, (i * L + l) & 1),
+                                                       ((i * L + l) >> 1) & 1, abort_flag,
                                                        kDevTimeoutEpi));
         if (!ok) break;
         tc_fence_after();
@@ -280,7 +285,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fwd2Cfg<NetT, NS, EP
       if (!ok) break;
       {
         constexpr int l = L - 1;
-        ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar_acc_full(s), (i * L + l) & 1, abort_flag,
+        ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar_acc_full(s, (i * L + l) & 1),
+                                                       ((i * L + l) >> 1) & 1, abort_flag,
                                                        kDevTimeoutEpi));
         if (!ok) break;
         tc_fence_after();

@@ -140,9 +140,9 @@ struct FwdCfg {
   // SPC: stripes per chunk per column group (chunk = SPC*NG stripes).
   static constexpr int SPC = (HMAX / (EPW / 4)) / 32 >= 4 ? 2 : 1;
   static constexpr int MAXCH = ((HMAX / (EPW / 4) + 31) / 32 + SPC - 1) / SPC;  // chunks/layer
-  // x_full, x_empty, acc_full, out_ready, store_free per slot; MAXCH h-chunk
-  // barriers per slot; w_full; mma_done
-  static constexpr int NUM_BARS = 5 * NS + NS * MAXCH + 2;
+  // x_full, x_empty, out_ready, store_free per slot; acc_full per slot and
+  // accumulator buffer; MAXCH h-chunk barriers per slot; w_full; mma_done
+  static constexpr int NUM_BARS = 6 * NS + NS * MAXCH + 2;
   static constexpr int OFF_MISC = OFF_BAR + 8 * NUM_BARS;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
   static constexpr int SLOT_COLS = align_up(HMAX, 32);   // one accumulator buffer
@@ -276,12 +276,20 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
   const uint32_t s_bar = sbase + Cfg::OFF_BAR;
   auto bar_x_full = [&](int s) { return s_bar + 8u * s; };
   auto bar_x_empty = [&](int s) { return s_bar + 8u * (NS + s); };
-  auto bar_acc_full = [&](int s) { return s_bar + 8u * (2 * NS + s); };
-  auto bar_out_ready = [&](int s) { return s_bar + 8u * (3 * NS + s); };
-  auto bar_store_free = [&](int s) { return s_bar + 8u * (4 * NS + s); };
+  // Accumulator of job g (= i*L + l) of slot s is complete: one barrier per
+  // TMEM buffer (g & 1), waited with parity (g >> 1) & 1.  A single barrier per
+  // slot could complete two phases before a slow epilogue warp polls it (a
+  // layer-0 job of the next tile depends on no epilogue work), and a parity
+  // wait cannot tell phase p from p + 2.  Per buffer this cannot happen: of
+  // jobs g + 1 and g + 2 at least one has layer >= 1 and waits for the
+  // epilogue's activation of the job before it, so the epilogue has consumed
+  // job g before job g + 2 can commit.
+  auto bar_acc_full = [&](int s, int b) { return s_bar + 8u * (2 * NS + 2 * s + b); };
+  auto bar_out_ready = [&](int s) { return s_bar + 8u * (4 * NS + s); };
+  auto bar_store_free = [&](int s) { return s_bar + 8u * (5 * NS + s); };
   // h chunk c of slot s: activation columns [32c, 32c+32), packed in TMEM
-  auto bar_chunk = [&](int s, int c) { return s_bar + 8u * (5 * NS + s * Cfg::MAXCH + c); };
-  const uint32_t bar_w_full = s_bar + 8u * (5 * NS + NS * Cfg::MAXCH);
+  auto bar_chunk = [&](int s, int c) { return s_bar + 8u * (6 * NS + s * Cfg::MAXCH + c); };
+  const uint32_t bar_w_full = s_bar + 8u * (6 * NS + NS * Cfg::MAXCH);
   const uint32_t bar_mma_done = bar_w_full + 8u;
   const uint32_t s_tmem_slot = sbase + Cfg::OFF_MISC;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + Cfg::OFF_MISC + 4);
@@ -293,7 +301,8 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
     for (int s = 0; s < NS; ++s) {
       mbar_init(bar_x_full(s), 1);
       mbar_init(bar_x_empty(s), 1);
-      mbar_init(bar_acc_full(s), 1);
+      mbar_init(bar_acc_full(s, 0), 1);
+      mbar_init(bar_acc_full(s, 1), 1);
       mbar_init(bar_out_ready(s), EPW);
       mbar_init(bar_store_free(s), 1);
       for (int c = 0; c < Cfg::MAXCH; ++c) mbar_init(bar_chunk(s, c), EPW);
@@ -438,7 +447,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
             }
             if (!ok) break;
           }
-          if (issuer) umma_commit(bar_acc_full(s));
+          if (issuer) umma_commit(bar_acc_full(s, (i * L + l) & 1));
           __syncwarp();
         }
       });
@@ -472,8 +481,8 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
       // hidden layers: softplus, fp16 activation published chunk by chunk
 #pragma unroll 1
       for (int l = 0; l < L - 1; ++l) {
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_acc_full(s), (i * L + l) & 1, abort_flag,
-                                               kDevTimeoutEpi));
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_acc_full(s, (i * L + l) & 1),
+                                               ((i * L + l) >> 1) & 1, abort_flag, kDevTimeoutEpi));
         if (!ok) break;
         tc_fence_after();
         if (l == 0 && i > 0) {
@@ -503,8 +512,8 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
       // output layer: fp16 result staged in obuf, written by TMA
       {
         constexpr int l = L - 1;
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_acc_full(s), (i * L + l) & 1, abort_flag,
-                                               kDevTimeoutEpi));
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_acc_full(s, (i * L + l) & 1),
+                                               ((i * L + l) >> 1) & 1, abort_flag, kDevTimeoutEpi));
         if (!ok) break;
         tc_fence_after();
         const uint32_t t_buf = t_lane + ((i * L + l) & 1) * Cfg::SLOT_COLS;

@@ -8,6 +8,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdint>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -36,16 +37,57 @@ struct DevInfo {
 DevInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
 
+// The CUDA failure behind this thread's most recent MLPK_ERR_CUDA (reported by
+// mlpk_last_cuda_error).
+thread_local char t_last_cuda_error[160] = "no error";
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return MLPK_OK;
+  std::snprintf(t_last_cuda_error, sizeof(t_last_cuda_error), "%s: %s", cudaGetErrorName(e),
+                cudaGetErrorString(e));
+  return MLPK_ERR_CUDA;
+}
+
+int driver_status(const char* what, int result) {
+  if (result == 0) return MLPK_OK;
+  std::snprintf(t_last_cuda_error, sizeof(t_last_cuda_error), "%s returned CUresult %d", what, result);
+  return MLPK_ERR_CUDA;
+}
+
+// Launch through cudaLaunchKernelEx so that the status returned is that of
+// THIS launch, not an error left earlier on the calling thread.
+template <typename... KArgs, typename... Args>
+int launch_kernel(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem,
+                  cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(block, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+}
+
 int current_device_info(DevInfo* out, int* dev_out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MLPK_ERR_CUDA;
+  int rc = cuda_status(cudaGetDevice(&dev));
+  if (rc != MLPK_OK) return rc;
+  if (dev < 0 || dev >= kMaxDevices) return MLPK_ERR_DEVICE;
+  // The tensor maps are encoded through the driver API, which needs the
+  // device's context current on THIS thread.  A thread that has only asked the
+  // runtime for its device (torch's autograd worker, for one) may have none
+  // bound yet; cudaSetDevice binds the primary context.
+  thread_local int t_bound_dev = -1;
+  if (t_bound_dev != dev) {
+    if ((rc = cuda_status(cudaSetDevice(dev))) != MLPK_OK) return rc;
+    t_bound_dev = dev;
+  }
   std::lock_guard<std::mutex> lk(g_dev_mu);
   DevInfo& d = g_dev[dev];
   if (!d.valid) {
-    if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
-      return MLPK_ERR_CUDA;
+    if ((rc = cuda_status(cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev))) ||
+        (rc = cuda_status(cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev))) ||
+        (rc = cuda_status(cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev))))
+      return rc;
     d.valid = true;
   }
   *out = d;
@@ -74,7 +116,7 @@ EncodeFn get_encode() {
 int make_map_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer,
                 uint32_t box_inner, uint32_t box_outer) {
   EncodeFn enc = get_encode();
-  if (!enc) return MLPK_ERR_CUDA;
+  if (!enc) return driver_status("cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)", -1);
   const uint32_t pitch = box_inner * 2;
   CUtensorMapSwizzle swz = pitch == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
                            : pitch == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
@@ -86,7 +128,7 @@ int make_map_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t oute
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), gdim, gstride,
                    box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? MLPK_OK : MLPK_ERR_CUDA;
+  return driver_status("cuTensorMapEncodeTiled", static_cast<int>(r));
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -99,7 +141,7 @@ bool set_smem_once(Kern kern, int bytes, int dev) {
   std::lock_guard<std::mutex> lk(mu);
   const auto key = std::make_pair(reinterpret_cast<const void*>(kern), dev);
   if (done.count(key)) return true;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+  if (cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes)))
     return false;
   done.insert(key);
   return true;
@@ -140,13 +182,11 @@ int launch_fwd(const void* x, const void* const* W, void* out, int64_t M, void* 
   if (hsave) {
     auto kern = mlpk::mlp_fwd_kernel<NetT, NS, EPW, true>;
     if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(maps, num_tiles);
-  } else {
-    auto kern = mlpk::mlp_fwd_kernel<NetT, NS, EPW, false>;
-    if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(maps, num_tiles);
+    return launch_kernel(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, st, maps, num_tiles);
   }
-  return cudaGetLastError() == cudaSuccess ? MLPK_OK : MLPK_ERR_CUDA;
+  auto kern = mlpk::mlp_fwd_kernel<NetT, NS, EPW, false>;
+  if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
+  return launch_kernel(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, st, maps, num_tiles);
 }
 
 // CTA-pair forward: clusters of 2 CTAs, one M=256 UMMA per pair tile.
@@ -184,8 +224,7 @@ int launch_fwd2(const void* x, const void* const* W, void* out, int64_t M, void*
   const int num_pairs = static_cast<int>((M + 2 * mlpk::kTileM - 1) / (2 * mlpk::kTileM));
   const int max_clusters = di.sm_count / 2;
   const int clusters = num_pairs < max_clusters ? num_pairs : max_clusters;
-  kern<<<2 * clusters, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(maps, num_pairs);
-  return cudaGetLastError() == cudaSuccess ? MLPK_OK : MLPK_ERR_CUDA;
+  return launch_kernel(kern, 2 * clusters, Cfg::THREADS, Cfg::SMEM_BYTES, st, maps, num_pairs);
 }
 
 // ------------------------------------------------------------------ backward
@@ -234,11 +273,11 @@ int launch_bwd(const void* x, const void* const* W, const void* const* h, const 
     auto kern = mlpk::mlp_bwd_kernel<NetT>;
     if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
     const int num_tiles = static_cast<int>((M + mlpk::kTileM - 1) / mlpk::kTileM);
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(maps, num_tiles);
-    if (cudaGetLastError() != cudaSuccess) return MLPK_ERR_CUDA;
+    if ((rc = launch_kernel(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, st, maps, num_tiles))) return rc;
   }
-  mlpk::mlp_reduce_kernel<<<(nfloats + 255) / 256, 256, 0, st>>>(ws, grid, nfloats, dw);
-  return cudaGetLastError() == cudaSuccess ? MLPK_OK : MLPK_ERR_CUDA;
+  return launch_kernel(mlpk::mlp_reduce_kernel, (nfloats + mlpk::kReduceElems - 1) / mlpk::kReduceElems,
+                       mlpk::kReduceElems * mlpk::kReduceSlices, 0, st,
+                       static_cast<const float*>(ws), grid, nfloats, dw);
 }
 
 // ------------------------------------------------------------------ dispatch
@@ -279,9 +318,15 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.bwd = &launch_bwd<N3>;
     o.bwd_ws = &bwd_workspace<N3>;
   } else if (shape_is<32, 64, 64, 64, 64, 16>(s)) {
-    o.fwd = &launch_fwd<Net<32, 64, 64, 64, 64, 16>, 2, 4>;
+    using N5 = Net<32, 64, 64, 64, 64, 16>;
+    o.fwd = &launch_fwd<N5, 2, 4>;
+    o.bwd = &launch_bwd<N5>;
+    o.bwd_ws = &bwd_workspace<N5>;
   } else if (shape_is<64, 64, 64, 64>(s)) {
-    o.fwd = &launch_fwd<Net<64, 64, 64, 64>, 2, 4>;
+    using N64 = Net<64, 64, 64, 64>;
+    o.fwd = &launch_fwd<N64, 2, 4>;
+    o.bwd = &launch_bwd<N64>;
+    o.bwd_ws = &bwd_workspace<N64>;
   }
   return o;
 }
@@ -425,9 +470,9 @@ int mlpk_wn_fwd(const mlpk_shape* shape, const float* v_all, const float* g_all,
   }
   DevInfo di;
   if ((rc = current_device_info(&di, nullptr)) != MLPK_OK) return rc;
-  mlpk::mlp_wn_fwd_kernel<<<(ws.total_cols + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      ws, v_all, g_all, out, inv_norm);
-  return cudaGetLastError() == cudaSuccess ? MLPK_OK : MLPK_ERR_CUDA;
+  return launch_kernel(mlpk::mlp_wn_fwd_kernel, mlpk::wn_num_blocks(ws),
+                       mlpk::kWnCols * mlpk::kWnRowGroups, 0, static_cast<cudaStream_t>(stream), ws,
+                       v_all, g_all, out, inv_norm);
 }
 
 int mlpk_wn_bwd(const mlpk_shape* shape, const float* dW_all, const float* v_all,
@@ -439,9 +484,9 @@ int mlpk_wn_bwd(const mlpk_shape* shape, const float* dW_all, const float* v_all
   if (!dW_all || !v_all || !g_all || !inv_norm || !dv_all || !dg_all) return MLPK_ERR_NULL;
   DevInfo di;
   if ((rc = current_device_info(&di, nullptr)) != MLPK_OK) return rc;
-  mlpk::mlp_wn_bwd_kernel<<<(ws.total_cols + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      ws, dW_all, v_all, g_all, inv_norm, dv_all, dg_all);
-  return cudaGetLastError() == cudaSuccess ? MLPK_OK : MLPK_ERR_CUDA;
+  return launch_kernel(mlpk::mlp_wn_bwd_kernel, mlpk::wn_num_blocks(ws),
+                       mlpk::kWnCols * mlpk::kWnRowGroups, 0, static_cast<cudaStream_t>(stream), ws,
+                       dW_all, v_all, g_all, inv_norm, dv_all, dg_all);
 }
 
 // ------------------------------------------------------------------ allocation-free backward
@@ -464,12 +509,15 @@ std::mutex g_noalloc_mu;
 // up once per device (with that device current) and cached.
 int noalloc_scratch(void** out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MLPK_ERR_CUDA;
+  const int drc = cuda_status(cudaGetDevice(&dev));
+  if (drc) return drc;
+  if (dev < 0 || dev >= kMaxDevices) return MLPK_ERR_DEVICE;
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (!g_noalloc_scratch_ptr[dev]) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_bwd_noalloc_scratch) != cudaSuccess || p == nullptr)
-      return MLPK_ERR_CUDA;
+    const int rc = cuda_status(cudaGetSymbolAddress(&p, g_bwd_noalloc_scratch));
+    if (rc) return rc;
+    if (p == nullptr) return driver_status("cudaGetSymbolAddress gave NULL", -1);
     g_noalloc_scratch_ptr[dev] = p;
   }
   *out = g_noalloc_scratch_ptr[dev];
@@ -497,15 +545,18 @@ int mlpk_bwd_noalloc(const mlpk_shape* shape, int64_t M, const void* x, const vo
 
 int mlpk_device_status(int clear, int* status_out) {
   int v = 0;
-  if (cudaMemcpyFromSymbol(&v, mlpk::g_device_status, sizeof(int)) != cudaSuccess)
-    return MLPK_ERR_CUDA;
+  int rc = cuda_status(cudaMemcpyFromSymbol(&v, mlpk::g_device_status, sizeof(int)));
+  if (rc) return rc;
   if (status_out) *status_out = v;
   if (clear) {
     const int z = 0;
-    if (cudaMemcpyToSymbol(mlpk::g_device_status, &z, sizeof(int)) != cudaSuccess)
-      return MLPK_ERR_CUDA;
+    if ((rc = cuda_status(cudaMemcpyToSymbol(mlpk::g_device_status, &z, sizeof(int))))) return rc;
   }
   return MLPK_OK;
+}
+
+const char* mlpk_last_cuda_error(void) {
+  return t_last_cuda_error;
 }
 
 }  // extern "C"

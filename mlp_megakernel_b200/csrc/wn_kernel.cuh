@@ -37,57 +37,102 @@ struct WnOut {
   __half* w[8];
 };
 
-__global__ void mlp_wn_fwd_kernel(WnShape s, const float* __restrict__ v_all,
-                                  const float* __restrict__ g_all, WnOut out,
-                                  float* __restrict__ inv_norm) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= s.total_cols) return;
-  int j;
-  const int l = wn_layer_of(s, c, j);
+// Block = one layer x 32 output columns; 256 threads = 32 columns x 8 row
+// groups.  Thread (c, r) handles column c and rows r, r+8, r+16, ...; the
+// per-column sums are combined through shared memory in a fixed order.
+constexpr int kWnCols = 32;
+constexpr int kWnRowGroups = 8;
+
+__device__ __forceinline__ int wn_block_layer(const WnShape& s, int b, int& col0) {
+  int l = 0, nb = 0;
+  while (true) {
+    const int blocks_l = (s.dout[l] + kWnCols - 1) / kWnCols;
+    if (b < nb + blocks_l || l + 1 == s.num_layers) {
+      col0 = (b - nb) * kWnCols;
+      return l;
+    }
+    nb += blocks_l;
+    ++l;
+  }
+}
+
+__device__ __forceinline__ float wn_col_sum(float v, float (*red)[kWnCols + 1], int c, int r) {
+  red[r][c] = v;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kWnRowGroups; ++k) t += red[k][c];  // fixed order
+  __syncthreads();
+  return t;
+}
+
+__global__ void __launch_bounds__(kWnCols * kWnRowGroups)
+    mlp_wn_fwd_kernel(WnShape s, const float* __restrict__ v_all, const float* __restrict__ g_all,
+                      WnOut out, float* __restrict__ inv_norm) {
+  __shared__ float red[kWnRowGroups][kWnCols + 1];
+  const int c = threadIdx.x % kWnCols, r = threadIdx.x / kWnCols;
+  int col0;
+  const int l = wn_block_layer(s, blockIdx.x, col0);
   const int K = s.din[l], N = s.dout[l];
+  const int j = col0 + c;
+  const bool valid = j < N;
   const float* v = v_all + s.voff[l];
   float ss = 0.0f;
-  for (int i = 0; i < K; ++i) {
-    const float a = v[static_cast<size_t>(i) * N + j];
-    ss = fmaf(a, a, ss);
-  }
+  if (valid)
+    for (int i = r; i < K; i += kWnRowGroups) {
+      const float a = v[static_cast<size_t>(i) * N + j];
+      ss = fmaf(a, a, ss);
+    }
+  ss = wn_col_sum(ss, red, c, r);
+  if (!valid) return;
   const float inv = 1.0f / sqrtf(ss);
-  const float scale = g_all[c] * inv;
+  const float scale = g_all[s.goff[l] + j] * inv;
   __half* w = out.w[l];
-  for (int i = 0; i < K; ++i)
+  for (int i = r; i < K; i += kWnRowGroups)
     w[static_cast<size_t>(i) * N + j] = __float2half_rn(v[static_cast<size_t>(i) * N + j] * scale);
-  inv_norm[c] = inv;
+  if (r == 0) inv_norm[s.goff[l] + j] = inv;
 }
 
 // dg_j = <dW_:j, v_:j> / ||v_:j||
 // dv_:j = (g_j / ||v_:j||) dW_:j - (g_j dg_j / ||v_:j||^2) v_:j
-__global__ void mlp_wn_bwd_kernel(WnShape s, const float* __restrict__ dw_all,
-                                  const float* __restrict__ v_all, const float* __restrict__ g_all,
-                                  const float* __restrict__ inv_norm, float* __restrict__ dv_all,
-                                  float* __restrict__ dg_all) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= s.total_cols) return;
-  int j;
-  const int l = wn_layer_of(s, c, j);
+__global__ void __launch_bounds__(kWnCols * kWnRowGroups)
+    mlp_wn_bwd_kernel(WnShape s, const float* __restrict__ dw_all, const float* __restrict__ v_all,
+                      const float* __restrict__ g_all, const float* __restrict__ inv_norm,
+                      float* __restrict__ dv_all, float* __restrict__ dg_all) {
+  __shared__ float red[kWnRowGroups][kWnCols + 1];
+  const int c = threadIdx.x % kWnCols, r = threadIdx.x / kWnCols;
+  int col0;
+  const int l = wn_block_layer(s, blockIdx.x, col0);
   const int K = s.din[l], N = s.dout[l];
+  const int j = col0 + c;
+  const bool valid = j < N;
   const float* v = v_all + s.voff[l];
   const float* dw = dw_all + s.voff[l];
   float* dv = dv_all + s.voff[l];
-  const float inv = inv_norm[c];
-  const float gj = g_all[c];
   float dot = 0.0f;
-  for (int i = 0; i < K; ++i) {
-    const size_t e = static_cast<size_t>(i) * N + j;
-    dot = fmaf(dw[e], v[e], dot);
-  }
+  if (valid)
+    for (int i = r; i < K; i += kWnRowGroups) {
+      const size_t e = static_cast<size_t>(i) * N + j;
+      dot = fmaf(dw[e], v[e], dot);
+    }
+  dot = wn_col_sum(dot, red, c, r);
+  if (!valid) return;
+  const float inv = inv_norm[s.goff[l] + j];
+  const float gj = g_all[s.goff[l] + j];
   const float dg = dot * inv;
   const float a = gj * inv;
   const float b = gj * dg * inv * inv;
-  for (int i = 0; i < K; ++i) {
+  for (int i = r; i < K; i += kWnRowGroups) {
     const size_t e = static_cast<size_t>(i) * N + j;
     dv[e] = fmaf(a, dw[e], -b * v[e]);
   }
-  dg_all[c] = dg;
+  if (r == 0) dg_all[s.goff[l] + j] = dg;
+}
+
+__host__ __device__ inline int wn_num_blocks(const WnShape& s) {
+  int n = 0;
+  for (int l = 0; l < s.num_layers; ++l) n += (s.dout[l] + kWnCols - 1) / kWnCols;
+  return n;
 }
 
 }  // namespace mlpk

@@ -32,6 +32,7 @@ import torch
 import torch.nn as nn
 
 from . import _lib
+from .dp import allreduce_weight_grads
 from .functional import _aligned
 
 
@@ -78,9 +79,7 @@ def _backward(x, ws, hs, grad_out, dims, process_group=None):
                       work.data_ptr(), int(work.numel()), dw.data_ptr(), _stream(x.device))
     _lib.check("mlpk_bwd", rc)
     if process_group is not None:
-        import torch.distributed as dist
-
-        dist.all_reduce(dw, op=dist.ReduceOp.SUM, group=process_group)
+        allreduce_weight_grads(dw, process_group)
     return dx, dw
 
 

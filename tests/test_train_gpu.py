@@ -42,20 +42,80 @@ def _status(built_lib):
     assert _lib.device_status() == 0, "a kernel recorded a device-side timeout"
 
 
-def _run(x, ws, g):
+def _run(x, ws, g, dims=DIMS):
     xg, wg, gg = x.cuda(), [w.cuda() for w in ws], g.cuda()
-    out, hs = _train_forward(xg, wg, DIMS)
-    dx, dw = _backward(xg, wg, hs, gg, DIMS)
+    out, hs = _train_forward(xg, wg, dims)
+    dx, dw = _backward(xg, wg, hs, gg, dims)
     torch.cuda.synchronize()
     return out, hs, dx, dw
 
 
-def _split(dw):
+def _split(dw, dims=DIMS):
     out, off = [], 0
-    for a, b in zip(DIMS[:-1], DIMS[1:]):
+    for a, b in zip(dims[:-1], dims[1:]):
         out.append(dw[off:off + a * b].reshape(a, b))
         off += a * b
     return out
+
+
+@pytest.mark.parametrize("config,M", [("5L", 1), ("5L", 300), ("5L", 65536), ("5L", 148 * 128 * 3 + 5)])
+def test_train_5layer_matches_oracle(config, M):
+    """BASELINE config 4 shape: 32 -> 64 -> 64 -> 64 -> 64 -> 16 (x ~ U(-1,1))."""
+    dims = (32, 64, 64, 64, 64, 16)
+    x, ws, g = make_inputs(config, M, with_grad=True)
+    out, hs, dx, dw = _run(x, ws, g, dims)
+    ref_out, ref_hs = oracle.mlp_forward_train(x.numpy(), [w.numpy() for w in ws])
+    assert rel_max(out.cpu().numpy(), ref_out) <= OUT_TOL
+    ref_dx, ref_dws = oracle.mlp_backward(x.numpy(), [w.numpy() for w in ws], ref_hs, g.numpy())
+    assert rel_l2(dx.cpu().numpy(), ref_dx) <= GRAD_TOL
+    for d, rd in zip(_split(dw.cpu().numpy(), dims), ref_dws):
+        assert rel_l2(d, rd) <= GRAD_TOL
+    dx2, dw2 = _backward(x.cuda(), [w.cuda() for w in ws], hs, g.cuda(), dims)
+    assert torch.equal(dw, dw2)
+
+
+def test_train_64wide_matches_oracle():
+    dims = (64, 64, 64, 64)
+    M = 3000
+    x = make_x(M, 64, "normal", 7)
+    ws = make_weights(dims)
+    g = make_grad(M, 64, seed=8)
+    out, hs, dx, dw = _run(x, ws, g, dims)
+    ref_out, ref_hs = oracle.mlp_forward_train(x.numpy(), [w.numpy() for w in ws])
+    ref_dx, ref_dws = oracle.mlp_backward(x.numpy(), [w.numpy() for w in ws], ref_hs, g.numpy())
+    assert rel_l2(dx.cpu().numpy(), ref_dx) <= GRAD_TOL
+    for d, rd in zip(_split(dw.cpu().numpy(), dims), ref_dws):
+        assert rel_l2(d, rd) <= GRAD_TOL
+
+
+def test_module_5layer_wn_autograd():
+    """FusedMLPSoftplusWN with 5 layers (D=32, H=64, OUT=16) through autograd."""
+    torch.manual_seed(3)
+    model = FusedMLPSoftplusWN(D=32, H=64, out_features=16, num_layers=5).cuda()
+    M = 20000
+    x, _, g = make_inputs("5L", M, with_grad=True)
+    x, g = x.cuda(), g.cuda()
+    out = model(x)
+    torch.cuda.synchronize()
+    out.backward(g)
+    torch.cuda.synchronize()
+    v = model.v_all.detach().double().cpu().requires_grad_(True)
+    gg = model.g_all.detach().double().cpu().requires_grad_(True)
+    ws, off, goff = [], 0, 0
+    for a, b in zip(model.dims[:-1], model.dims[1:]):
+        vl = v[off:off + a * b].view(a, b)
+        ws.append(gg[goff:goff + b] * vl / vl.norm(dim=0, keepdim=True))
+        off += a * b
+        goff += b
+    ref = x.cpu().double()
+    for i, w in enumerate(ws):
+        ref = ref @ w
+        if i < len(ws) - 1:
+            ref = torch.nn.functional.softplus(ref)
+    ref.backward(g.cpu().double())
+    assert rel_max(out.detach().cpu().numpy(), ref.detach().numpy()) <= OUT_TOL
+    assert rel_l2(model.v_all.grad.cpu().numpy(), v.grad.numpy()) <= GRAD_TOL
+    assert rel_l2(model.g_all.grad.cpu().numpy(), gg.grad.numpy()) <= GRAD_TOL
 
 
 @pytest.mark.parametrize("M", [1, 127, 129, 1000, 16384, 148 * 128 + 1])
@@ -210,3 +270,25 @@ def test_module_under_autocast_and_fp32_params():
     assert out.dtype == torch.float16
     assert x.grad is not None and x.grad.dtype == torch.float32
     assert all(w.grad.dtype == torch.float32 for w in model.weights)
+
+
+@pytest.mark.parametrize("config,dims,M", [("5L", (32, 64, 64, 64, 64, 16), 1048576),
+                                           ("3L128", DIMS, 1048576)])
+def test_repeated_launches_are_stable(config, dims, M):
+    """Many back-to-back inference and training forwards and backwards: every
+    repetition bitwise equal to the first and no bounded wait expired (the
+    fixture checks the device status word).  Catches hand-off races between
+    the warp roles that a single launch may not hit."""
+    x, ws, g = make_inputs(config, M, with_grad=True)
+    x, ws, g = x.cuda(), [w.cuda() for w in ws], g.cuda()
+    ref = fused_mlp_fwd(x, *ws)
+    ref_t, hs = _train_forward(x, ws, dims)
+    dx0, dw0 = _backward(x, ws, hs, g, dims)
+    assert torch.equal(ref, ref_t)
+    for _ in range(20):
+        out = fused_mlp_fwd(x, *ws)
+        out_t, hs2 = _train_forward(x, ws, dims)
+        dx, dw = _backward(x, ws, hs2, g, dims)
+        assert torch.equal(out, ref) and torch.equal(out_t, ref)
+        assert torch.equal(dx, dx0) and torch.equal(dw, dw0)
+    assert _lib.device_status() == 0
