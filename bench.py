@@ -40,8 +40,7 @@ FLOP_PER_ROW = 2 * sum(a * b for a, b in zip(DIMS[:-1], DIMS[1:]))
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 FWD_KERNEL = "mlp_fwd_kernel"
 TRAIN_ROWS = 262144                                           # BASELINE config 3 (split-K regime)
-TRAIN_BYTES_PER_ROW = 2 * (2 * DIMS[0] + 2 * DIMS[-1])        # x, out, grad_out, dx (fp16)
-TRAIN_FLOP_PER_ROW = 3 * FLOP_PER_ROW                         # forward, dgrad, wgrad
+TRAIN5_ROWS = 1024 * 1024                                     # BASELINE config 4 (global)
 
 
 def parse_args():
@@ -55,6 +54,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--train-rows", type=int, default=TRAIN_ROWS, help="training rows per GPU")
+    ap.add_argument("--train5-rows", type=int, default=TRAIN5_ROWS,
+                    help="global rows of the 5-layer training step (split over the GPUs)")
     ap.add_argument("--train-steps", type=int, default=50)
     ap.add_argument("--no-train", action="store_true")
     return ap.parse_args()
@@ -296,7 +297,13 @@ def run_mlpk(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
-    train = None if args.no_train else run_training(args, world, rank, dist, barrier)
+    train = train5 = None
+    if not args.no_train:
+        from mlp_megakernel_b200.dp import shard_rows
+
+        train = run_training(args, world, rank, dist, barrier, "3L128", args.train_rows)
+        a, b = shard_rows(args.train5_rows, rank, world)
+        train5 = run_training(args, world, rank, dist, barrier, "5L", b - a)
 
     clocks = clk.summary()
     if dist is not None:
@@ -355,6 +362,8 @@ def run_mlpk(args):
     }
     if train is not None:
         line["fwd_bwd"] = train
+    if train5 is not None:
+        line["fwd_bwd_5l"] = train5
     if world == 1 and not args.no_cpu_baseline:
         rows = 65536
         rps, cores, calls, dt = cpu_forward_rows_per_s(rows, args.cpu_seconds)
@@ -366,11 +375,26 @@ def run_mlpk(args):
     print(json.dumps(line), flush=True)
 
 
-def run_training(args, world, rank, dist, barrier):
-    """one 3L128 training step with weight norm per GPU on
-    `train_rows` rows -- weight-norm forward, training forward, fused backward
+TRAIN_SPECS = {
+    # 3L128 with weight norm, split-K regime, rows per GPU fixed
+    "3L128": {"dims": (128, 128, 128, 128), "x_dist": "normal", "x_seed": 0, "strong": False,
+              "metric": "fused MLP fwd+bwd rows/s (3L128 with weight norm)",
+              "workload": "BASELINE config 3: 3L D=H=OUT=128 training step with weight norm, "
+                          "M={M} rows per GPU"},
+    # 5L 32-64-64-64-64-16 with weight norm, global M = 1,048,576
+    # split over the ranks (strong scaling, NCCL all-reduce of dW)
+    "5L": {"dims": (32, 64, 64, 64, 64, 16), "x_dist": "uniform", "x_seed": 3, "strong": True,
+           "metric": "fused MLP fwd+bwd rows/s (5L 32-64-64-64-64-16 with weight norm)",
+           "workload": "BASELINE config 4: 5L D=32 H=64 OUT=16 training step with weight norm, "
+                       "global M={G} rows, {M} per GPU"},
+}
+
+
+def run_training(args, world, rank, dist, barrier, name, rows):
+    """One training step with weight norm per GPU through the C ABI on
+    preallocated buffers: weight-norm forward, training forward, fused backward
     + fixed-order dW reduction, (N > 1: NCCL all-reduce of dW), weight-norm
-    backward -- all through the C ABI on preallocated buffers."""
+    backward.  `rows` is the per-GPU batch."""
     import ctypes
 
     import torch
@@ -378,20 +402,24 @@ def run_training(args, world, rank, dist, barrier):
     from mlp_megakernel_b200 import _lib
     from mlp_megakernel_b200.synthetic import make_grad, make_weights, make_x
 
-    M = args.train_rows
+    spec = TRAIN_SPECS[name]
+    dims = spec["dims"]
+    flop_per_row = 3 * 2 * sum(a * b for a, b in zip(dims[:-1], dims[1:]))  # fwd, dgrad, wgrad
+    bytes_per_row = 2 * (2 * dims[0] + 2 * dims[-1])                       # x, out, grad_out, dx
+    M = rows
     dev = torch.device("cuda", torch.cuda.current_device())
     lib = _lib.lib()
-    shape = ctypes.byref(_lib.shape_struct(DIMS))
+    shape = ctypes.byref(_lib.shape_struct(dims))
     st = torch.cuda.current_stream().cuda_stream
-    x = make_x(M, DIMS[0], "normal", rank, device=dev)
-    g = make_grad(M, DIMS[-1], seed=2 + rank, device=dev)
-    ws0 = make_weights(DIMS, device=dev)
+    x = make_x(M, dims[0], spec["x_dist"], spec["x_seed"] + rank, device=dev)
+    g = make_grad(M, dims[-1], seed=2 + rank, device=dev)
+    ws0 = make_weights(dims, device=dev)
     v_all = torch.cat([w.float().reshape(-1) for w in ws0]).contiguous()
     g_all = torch.cat([w.float().norm(dim=0) for w in ws0]).contiguous()
     W = [torch.empty_like(w) for w in ws0]
     inv = torch.empty_like(g_all)
-    out = torch.empty((M, DIMS[-1]), dtype=torch.float16, device=dev)
-    hs = [torch.empty((M, d), dtype=torch.float16, device=dev) for d in DIMS[1:-1]]
+    out = torch.empty((M, dims[-1]), dtype=torch.float16, device=dev)
+    hs = [torch.empty((M, d), dtype=torch.float16, device=dev) for d in dims[1:-1]]
     dx = torch.empty_like(x)
     dw = torch.empty_like(v_all)
     dv = torch.empty_like(v_all)
@@ -463,30 +491,32 @@ def run_training(args, world, rank, dist, barrier):
 
     peaks = load_peaks()
     per_step = ms / 1e3 / args.train_steps
-    tflops = TRAIN_FLOP_PER_ROW * M / per_step / 1e12
-    gbs = TRAIN_BYTES_PER_ROW * M / per_step / 1e9
-    roof_rows = min(peaks["bf16_tflops"] * 1e12 / TRAIN_FLOP_PER_ROW,
-                    peaks["hbm_gbs"] * 1e9 / TRAIN_BYTES_PER_ROW)
+    tflops = flop_per_row * M / per_step / 1e12
+    gbs = bytes_per_row * M / per_step / 1e9
+    tensor_rows = peaks["bf16_tflops"] * 1e12 / flop_per_row
+    hbm_rows = peaks["hbm_gbs"] * 1e9 / bytes_per_row
+    roof_rows = min(tensor_rows, hbm_rows)
     return {
-        "metric": "fused MLP fwd+bwd rows/s (3L128 with weight norm)",
+        "metric": spec["metric"],
         "value": world * M * args.train_steps / (ms / 1e3),
         "unit": "rows/s",
         "steps": args.train_steps,
         "ms_per_step": ms / args.train_steps,
-        "config": {"workload": f"BASELINE config 3: 3L D=H=OUT=128 training step with weight "
-                               f"norm, M={M} rows per GPU",
-                   "rows_per_gpu": M, "parallelism": f"dp{world}" + (" (NCCL all-reduce of fp32 dW)"
-                                                                       if world > 1 else ""),
-                   "l2": "inputs larger than L2 (x, grad_out, saved h: 64 MiB each)"},
-        "roofline": {"bound": "tensor" if roof_rows < peaks["hbm_gbs"] * 1e9 / TRAIN_BYTES_PER_ROW
-                     else "hbm",
+        "scaling": "strong" if spec["strong"] else "weak",
+        "config": {"workload": spec["workload"].format(M=M, G=world * M),
+                   "dims": list(dims), "rows_per_gpu": M, "global_rows": world * M,
+                   "parallelism": f"dp{world}" + (" (NCCL all-reduce of fp32 dW)" if world > 1 else ""),
+                   "l2": "per-step inputs and saved activations larger than L2"
+                         if M * dims[1] * 2 * (len(dims) - 2) > 126e6 else
+                         "working set partly L2-resident (no flush between steps)"},
+        "roofline": {"bound": "tensor" if tensor_rows <= hbm_rows else "hbm",
                      "achieved": tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": tflops / peaks["bf16_tflops"],
                      "rows_frac_of_roofline": (M / per_step) / roof_rows,
                      "achieved_algorithmic_gbs": gbs, "traffic": None,
-                     "flop_per_row": TRAIN_FLOP_PER_ROW, "algorithmic_bytes_per_row": TRAIN_BYTES_PER_ROW},
+                     "flop_per_row": flop_per_row, "algorithmic_bytes_per_row": bytes_per_row},
         "e2e": {"value": world * M * n_e2e / (e2e_ms / 1e3), "unit": "rows/s",
-                "h2d_bytes_per_step": 2 * M * DIMS[0] * 2,
+                "h2d_bytes_per_step": M * (dims[0] + dims[-1]) * 2,
                 "d2h_bytes_per_step": (dv.numel() + dg.numel()) * 4,
                 "api": "C ABI (mlpk_wn_fwd, mlpk_train_fwd, mlpk_bwd, mlpk_wn_bwd) with pinned host buffers"},
         "gpu_launches": 5 * args.train_steps,
