@@ -464,7 +464,9 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
 // Level-2 reduction of the per-CTA partials: a block covers kReduceElems
 // elements with kReduceSlices threads each; slice s sums partials p = s,
 // s + kReduceSlices, ... in increasing p, and the slices are added in slice
-// order.  The order is fixed, so dW is bitwise reproducible.
+// order.  The order is fixed, so dW is bitwise reproducible.  blockIdx.y
+// selects an independent group (nparts partials of nfloats each, written to
+// dw + y * nfloats), e.g. one group per layer of the split-K wgrad kernel.
 constexpr int kReduceElems = 64;
 constexpr int kReduceSlices = 4;
 
@@ -472,6 +474,8 @@ __global__ void __launch_bounds__(kReduceElems * kReduceSlices)
     mlp_reduce_kernel(const float* __restrict__ partials, int nparts, int nfloats,
                       float* __restrict__ dw) {
   __shared__ float red[kReduceSlices][kReduceElems];
+  partials += static_cast<size_t>(blockIdx.y) * nparts * nfloats;
+  dw += static_cast<size_t>(blockIdx.y) * nfloats;
   const int le = threadIdx.x % kReduceElems, sl = threadIdx.x / kReduceElems;
   const int e = blockIdx.x * kReduceElems + le;
   float acc = 0.0f;

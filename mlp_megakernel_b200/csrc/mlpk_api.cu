@@ -18,6 +18,8 @@
 #include "../../include/mlpk.h"
 #include "bwd_kernel.cuh"
 #include "fwd2_kernel.cuh"
+#include "stream_kernel.cuh"
+#include "wgrad_kernel.cuh"
 #include "wn_kernel.cuh"
 
 namespace {
@@ -57,10 +59,10 @@ int driver_status(const char* what, int result) {
 // Launch through cudaLaunchKernelEx so that the status returned is that of
 // THIS launch, not an error left earlier on the calling thread.
 template <typename... KArgs, typename... Args>
-int launch_kernel(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem,
+int launch_kernel(void (*kern)(KArgs...), dim3 grid, unsigned block, size_t smem,
                   cudaStream_t st, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.gridDim = grid;
   cfg.blockDim = dim3(block, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -280,6 +282,147 @@ int launch_bwd(const void* x, const void* const* W, const void* const* h, const 
                        static_cast<const float*>(ws), grid, nfloats, dw);
 }
 
+// ------------------------------------------------------------------ streamed weights
+// Networks whose weights do not fit in shared memory (D = H = OUT = 256).
+constexpr int kStreamEpw = 8;
+
+template <class NetT>
+int launch_stream_fwd(const void* x, const void* const* W, void* out, int64_t M, void* const* hsave,
+                      cudaStream_t st) {
+  using Cfg = mlpk::StreamCfg<NetT, kStreamEpw>;
+  constexpr int L = NetT::L;
+  DevInfo di;
+  int dev = 0;
+  int rc = current_device_info(&di, &dev);
+  if (rc != MLPK_OK) return rc;
+  if (M == 0) return MLPK_OK;
+  if (M > (int64_t(1) << 31) - 256) return MLPK_ERR_SHAPE;
+  mlpk::StreamMaps<L> maps;
+  std::memset(&maps, 0, sizeof(maps));
+  if ((rc = make_map_2d(&maps.in, x, Cfg::D0, M, 64, mlpk::kTileM))) return rc;
+  if ((rc = make_map_2d(&maps.out, out, Cfg::DL, M, 64, mlpk::kTileM))) return rc;
+  int wrc = MLPK_OK;
+  mlpk::static_for<0, L>([&](auto lc) {
+    constexpr int l = decltype(lc)::value;
+    // W_l [d_l][d_{l+1}]: K-chunks of 64 rows read as {64 columns, 64 rows} boxes
+    if (wrc == MLPK_OK)
+      wrc = make_map_2d(&maps.w[l], W[l], NetT::template D<l + 1>(), NetT::template D<l>(), 64,
+                        mlpk::kStreamK);
+  });
+  if (wrc) return wrc;
+  for (int l = 0; l + 1 < L; ++l) maps.save[l] = hsave ? hsave[l] : nullptr;
+  maps.M = static_cast<int>(M);
+  const int64_t tiles = (M + mlpk::kTileM - 1) / mlpk::kTileM;
+  const int grid = static_cast<int>(tiles < di.sm_count ? tiles : di.sm_count);
+  if (hsave) {
+    auto kern = mlpk::mlp_stream_kernel<NetT, kStreamEpw, mlpk::kStreamFwd, true>;
+    if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
+    return launch_kernel(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, st, maps, static_cast<int>(tiles));
+  }
+  auto kern = mlpk::mlp_stream_kernel<NetT, kStreamEpw, mlpk::kStreamFwd, false>;
+  if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
+  return launch_kernel(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, st, maps, static_cast<int>(tiles));
+}
+
+// Workspace of the streamed backward: the data-gradient chain's dz_1..dz_{L-1}
+// (fp16 [M, H] each, read back by the weight-gradient kernel), then the fp32
+// partials of the weight-gradient CTAs.
+template <class NetT>
+struct StreamBwdLayout {
+  static constexpr int L = NetT::L;
+  static constexpr int DA = NetT::template D<0>();
+  static constexpr int DB = NetT::template D<1>();
+  static_assert(NetT::all_dims_are(DA), "streamed backward serves equal widths");
+  static int ctas_per_layer(int sm_count) { return sm_count / L > 0 ? sm_count / L : 1; }
+  static size_t dz_bytes(int64_t M) { return static_cast<size_t>(M) * DB * 2; }
+  static size_t partial_offset(int64_t M) {
+    return (static_cast<size_t>(L - 1) * dz_bytes(M) + 255) / 256 * 256;
+  }
+  static size_t total(int64_t M, int sm_count) {
+    return partial_offset(M) +
+           static_cast<size_t>(ctas_per_layer(sm_count)) * L * DA * DB * sizeof(float);
+  }
+};
+
+template <class NetT>
+size_t stream_bwd_workspace(int64_t M, int sm_count) {
+  return StreamBwdLayout<NetT>::total(M, sm_count);
+}
+
+template <class NetT>
+int launch_stream_bwd(const void* x, const void* const* W, const void* const* h, const void* g,
+                      void* dx, float* ws, size_t ws_bytes, float* dw, int64_t M, cudaStream_t st) {
+  using Lay = StreamBwdLayout<NetT>;
+  using Chain = mlpk::NetReverse<NetT>;
+  using Cfg = mlpk::StreamCfg<Chain, kStreamEpw>;
+  using WCfg = mlpk::WgradCfg<Lay::DA, Lay::DB>;
+  constexpr int L = NetT::L;
+  DevInfo di;
+  int dev = 0;
+  int rc = current_device_info(&di, &dev);
+  if (rc != MLPK_OK) return rc;
+  if (M > (int64_t(1) << 31) - 256) return MLPK_ERR_SHAPE;
+  if (ws_bytes < Lay::total(M, di.sm_count)) return MLPK_ERR_SHAPE;
+  uint8_t* wsb = reinterpret_cast<uint8_t*>(ws);
+  void* dz[L > 1 ? L - 1 : 1];  // dz[l - 1] = dz_l, l = 1 .. L-1
+  for (int l = 1; l < L; ++l) dz[l - 1] = wsb + static_cast<size_t>(l - 1) * Lay::dz_bytes(M);
+  float* partials = reinterpret_cast<float*>(wsb + Lay::partial_offset(M));
+  const int P = Lay::ctas_per_layer(di.sm_count);
+  if (M > 0) {
+    // 1. data-gradient chain: stage s handles layer l = L-1-s
+    mlpk::StreamMaps<L> maps;
+    std::memset(&maps, 0, sizeof(maps));
+    if ((rc = make_map_2d(&maps.in, g, Cfg::D0, M, 64, mlpk::kTileM))) return rc;
+    if ((rc = make_map_2d(&maps.out, dx, Cfg::DL, M, 64, mlpk::kTileM))) return rc;
+    int wrc = MLPK_OK;
+    mlpk::static_for<0, L>([&](auto sc) {
+      constexpr int s = decltype(sc)::value;
+      constexpr int l = L - 1 - s;
+      // W_l [d_l][d_{l+1}] read as W_l^T K-chunks: boxes {64 columns, all d_l rows}
+      if (wrc == MLPK_OK)
+        wrc = make_map_2d(&maps.w[s], W[l], NetT::template D<l + 1>(), NetT::template D<l>(), 64,
+                          NetT::template D<l>());
+    });
+    if (wrc) return wrc;
+    for (int s = 0; s + 1 < L; ++s) {
+      const int l = L - 1 - s;
+      maps.hact[s] = h[l - 1];
+      maps.save[s] = dz[l - 1];
+    }
+    maps.M = static_cast<int>(M);
+    const int64_t tiles = (M + mlpk::kTileM - 1) / mlpk::kTileM;
+    const int grid = static_cast<int>(tiles < di.sm_count ? tiles : di.sm_count);
+    auto kern = mlpk::mlp_stream_kernel<Chain, kStreamEpw, mlpk::kStreamDgrad, true>;
+    if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
+    if ((rc = launch_kernel(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, st, maps, static_cast<int>(tiles))))
+      return rc;
+  }
+  // 2. split-K weight gradients: P CTAs per layer (an empty share writes zeros)
+  {
+    mlpk::WgradMaps<L> wm;
+    std::memset(&wm, 0, sizeof(wm));
+    const int64_t rows = M > 0 ? M : 1;  // a map needs a non-empty tensor; no stage reads it at M = 0
+    for (int l = 0; l < L; ++l) {
+      const void* a = l == 0 ? x : h[l - 1];
+      const void* b = l == L - 1 ? g : dz[l];
+      if (M == 0) a = b = ws;  // never read
+      if ((rc = make_map_2d(&wm.a[l], a, Lay::DA, rows, 64, mlpk::kWgStageRows))) return rc;
+      if ((rc = make_map_2d(&wm.b[l], b, Lay::DB, rows, 64, mlpk::kWgStageRows))) return rc;
+    }
+    wm.partials = partials;
+    auto kern = mlpk::mlp_wgrad_kernel<L, Lay::DA, Lay::DB>;
+    if (!set_smem_once(kern, WCfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
+    if ((rc = launch_kernel(kern, P * L, WCfg::THREADS, WCfg::SMEM_BYTES, st, wm, static_cast<int>(M), P)))
+      return rc;
+  }
+  // 3. fixed-order sum of each layer's P partials
+  constexpr int nfloats = Lay::DA * Lay::DB;
+  return launch_kernel(mlpk::mlp_reduce_kernel,
+                       dim3((nfloats + mlpk::kReduceElems - 1) / mlpk::kReduceElems, L, 1),
+                       mlpk::kReduceElems * mlpk::kReduceSlices, 0, st,
+                       static_cast<const float*>(partials), P, nfloats, dw);
+}
+
 // ------------------------------------------------------------------ dispatch
 template <int... Ds>
 bool shape_is(const mlpk_shape* s) {
@@ -327,6 +470,11 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.fwd = &launch_fwd<N64, 2, 4>;
     o.bwd = &launch_bwd<N64>;
     o.bwd_ws = &bwd_workspace<N64>;
+  } else if (shape_is<256, 256, 256, 256>(s)) {
+    using N256 = Net<256, 256, 256, 256>;
+    o.fwd = &launch_stream_fwd<N256>;
+    o.bwd = &launch_stream_bwd<N256>;
+    o.bwd_ws = &stream_bwd_workspace<N256>;
   }
   return o;
 }

@@ -50,7 +50,9 @@ def test_fwd_matches_reference_kernel_golden(name):
     assert err <= TIGHT, f"{name}: {err:.3e} (parity ok, implementation bar missed)"
 
 
-@pytest.mark.parametrize("config,M", [("3L128", 4096), ("5L", 8192), ("3L128", 148 * 128 * 3 + 77)])
+@pytest.mark.parametrize("config,M", [("3L128", 4096), ("5L", 8192), ("3L128", 148 * 128 * 3 + 77),
+                                      ("W256", 1), ("W256", 129), ("W256", 5000),
+                                      ("W256", 148 * 128 * 2 + 3)])
 def test_fwd_matches_oracle(config, M):
     x, ws = make_inputs(config, M)
     out = fused_mlp_fwd(x.cuda(), *_gpu(ws)).cpu().numpy()

@@ -74,6 +74,55 @@ def test_train_5layer_matches_oracle(config, M):
     assert torch.equal(dw, dw2)
 
 
+@pytest.mark.parametrize("M", [1, 300, 40000])
+def test_train_w256_matches_oracle(M):
+    """BASELINE config 5 shape (D = H = OUT = 256): streamed-weight training
+    forward, data-gradient chain, split-K weight gradients."""
+    dims = (256, 256, 256, 256)
+    x, ws, g = make_inputs("W256", M, with_grad=True)
+    out, hs, dx, dw = _run(x, ws, g, dims)
+    assert torch.equal(out, fused_mlp_fwd(x.cuda(), *[w.cuda() for w in ws]))
+    ref_out, ref_hs = oracle.mlp_forward_train(x.numpy(), [w.numpy() for w in ws])
+    assert rel_max(out.cpu().numpy(), ref_out) <= OUT_TOL
+    for h, rh in zip(hs, ref_hs):
+        assert rel_max(h.cpu().numpy(), rh) <= 2e-3
+    ref_dx, ref_dws = oracle.mlp_backward(x.numpy(), [w.numpy() for w in ws], ref_hs, g.numpy())
+    assert rel_l2(dx.cpu().numpy(), ref_dx) <= GRAD_TOL
+    for d, rd in zip(_split(dw.cpu().numpy(), dims), ref_dws):
+        assert rel_l2(d, rd) <= GRAD_TOL
+    dx2, dw2 = _backward(x.cuda(), [w.cuda() for w in ws], hs, g.cuda(), dims)
+    assert torch.equal(dw, dw2) and torch.equal(dx, dx2)
+
+
+def test_module_w256_wn_autograd():
+    """FusedMLPSoftplusWN(D=H=OUT=256) through autograd (BASELINE config 5 shape)."""
+    torch.manual_seed(5)
+    model = FusedMLPSoftplusWN(D=256, H=256, out_features=256).cuda()
+    M = 3000
+    x, _, g = make_inputs("W256", M, with_grad=True)
+    x, g = x.cuda(), g.cuda()
+    out = model(x)
+    out.backward(g)
+    torch.cuda.synchronize()
+    v = model.v_all.detach().double().cpu().requires_grad_(True)
+    gg = model.g_all.detach().double().cpu().requires_grad_(True)
+    ws, off, goff = [], 0, 0
+    for a, b in zip(model.dims[:-1], model.dims[1:]):
+        vl = v[off:off + a * b].view(a, b)
+        ws.append(gg[goff:goff + b] * vl / vl.norm(dim=0, keepdim=True))
+        off += a * b
+        goff += b
+    ref = x.cpu().double()
+    for i, w in enumerate(ws):
+        ref = ref @ w
+        if i < len(ws) - 1:
+            ref = torch.nn.functional.softplus(ref)
+    ref.backward(g.cpu().double())
+    assert rel_max(out.detach().cpu().numpy(), ref.detach().numpy()) <= OUT_TOL
+    assert rel_l2(model.v_all.grad.cpu().numpy(), v.grad.numpy()) <= GRAD_TOL
+    assert rel_l2(model.g_all.grad.cpu().numpy(), gg.grad.numpy()) <= GRAD_TOL
+
+
 def test_train_64wide_matches_oracle():
     dims = (64, 64, 64, 64)
     M = 3000
@@ -273,7 +322,8 @@ def test_module_under_autocast_and_fp32_params():
 
 
 @pytest.mark.parametrize("config,dims,M", [("5L", (32, 64, 64, 64, 64, 16), 1048576),
-                                           ("3L128", DIMS, 1048576)])
+                                           ("3L128", DIMS, 1048576),
+                                           ("W256", (256, 256, 256, 256), 262144)])
 def test_repeated_launches_are_stable(config, dims, M):
     """Many back-to-back inference and training forwards and backwards: every
     repetition bitwise equal to the first and no bounded wait expired (the
