@@ -41,6 +41,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"
 FWD_KERNEL = "mlp_fwd_kernel"
 TRAIN_ROWS = 262144                                           # BASELINE config 3 (split-K regime)
 TRAIN5_ROWS = 1024 * 1024                                     # BASELINE config 4 (global)
+TRAIN256_ROWS = 1024 * 1024                                   # BASELINE config 5 (global)
 
 
 def parse_args():
@@ -56,6 +57,8 @@ def parse_args():
     ap.add_argument("--train-rows", type=int, default=TRAIN_ROWS, help="training rows per GPU")
     ap.add_argument("--train5-rows", type=int, default=TRAIN5_ROWS,
                     help="global rows of the 5-layer training step (split over the GPUs)")
+    ap.add_argument("--train256-rows", type=int, default=TRAIN256_ROWS,
+                    help="global rows of the wide (256) training step (split over the GPUs)")
     ap.add_argument("--train-steps", type=int, default=50)
     ap.add_argument("--no-train", action="store_true")
     return ap.parse_args()
@@ -297,13 +300,15 @@ def run_mlpk(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
-    train = train5 = None
+    train = train5 = train256 = None
     if not args.no_train:
         from mlp_megakernel_b200.dp import shard_rows
 
         train = run_training(args, world, rank, dist, barrier, "3L128", args.train_rows)
         a, b = shard_rows(args.train5_rows, rank, world)
         train5 = run_training(args, world, rank, dist, barrier, "5L", b - a)
+        a, b = shard_rows(args.train256_rows, rank, world)
+        train256 = run_training(args, world, rank, dist, barrier, "W256", b - a)
 
     clocks = clk.summary()
     if dist is not None:
@@ -364,6 +369,8 @@ def run_mlpk(args):
         line["fwd_bwd"] = train
     if train5 is not None:
         line["fwd_bwd_5l"] = train5
+    if train256 is not None:
+        line["fwd_bwd_w256"] = train256
     if world == 1 and not args.no_cpu_baseline:
         rows = 65536
         rps, cores, calls, dt = cpu_forward_rows_per_s(rows, args.cpu_seconds)
@@ -387,6 +394,12 @@ TRAIN_SPECS = {
            "metric": "fused MLP fwd+bwd rows/s (5L 32-64-64-64-64-16 with weight norm)",
            "workload": "BASELINE config 4: 5L D=32 H=64 OUT=16 training step with weight norm, "
                        "global M={G} rows, {M} per GPU"},
+    # wide 3L D=H=OUT=256 (weights streamed), plain weights,
+    # global M = 1,048,576 split over the ranks
+    "W256": {"dims": (256, 256, 256, 256), "x_dist": "normal", "x_seed": 4, "strong": True, "wn": False,
+             "metric": "fused MLP fwd+bwd rows/s (wide 3L D=H=OUT=256)",
+             "workload": "BASELINE config 5: 3L D=H=OUT=256 training step (streamed weights), "
+                         "global M={G} rows, {M} per GPU"},
 }
 
 
@@ -428,16 +441,23 @@ def run_training(args, world, rank, dist, barrier, name, rows):
     Wp = _lib.ptr_array([w.data_ptr() for w in W])
     Hp = _lib.ptr_array([h.data_ptr() for h in hs])
 
+    wn = spec.get("wn", True)
+    if not wn:  # plain weights: the step is training forward + backward (+ all-reduce)
+        for w, w0 in zip(W, ws0):
+            w.copy_(w0)
+
     def step():
-        _lib.check("wn_fwd", lib.mlpk_wn_fwd(shape, v_all.data_ptr(), g_all.data_ptr(), Wp,
-                                             inv.data_ptr(), st))
+        if wn:
+            _lib.check("wn_fwd", lib.mlpk_wn_fwd(shape, v_all.data_ptr(), g_all.data_ptr(), Wp,
+                                                 inv.data_ptr(), st))
         _lib.check("train_fwd", lib.mlpk_train_fwd(shape, M, x.data_ptr(), Wp, out.data_ptr(), Hp, st))
         _lib.check("bwd", lib.mlpk_bwd(shape, M, x.data_ptr(), Wp, Hp, g.data_ptr(), dx.data_ptr(),
                                        work.data_ptr(), work.numel(), dw.data_ptr(), st))
         if dist is not None:
             dist.all_reduce(dw)
-        _lib.check("wn_bwd", lib.mlpk_wn_bwd(shape, dw.data_ptr(), v_all.data_ptr(), g_all.data_ptr(),
-                                             inv.data_ptr(), dv.data_ptr(), dg.data_ptr(), st))
+        if wn:
+            _lib.check("wn_bwd", lib.mlpk_wn_bwd(shape, dw.data_ptr(), v_all.data_ptr(), g_all.data_ptr(),
+                                                 inv.data_ptr(), dv.data_ptr(), dg.data_ptr(), st))
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -464,12 +484,17 @@ def run_training(args, world, rank, dist, barrier, name, rows):
     dvh = torch.empty(dv.shape, dtype=dv.dtype, pin_memory=True)
     dgh = torch.empty(dg.shape, dtype=dg.dtype, pin_memory=True)
 
+    dwh = torch.empty(dw.shape, dtype=dw.dtype, pin_memory=True)
+
     def e2e_step():
         x.copy_(xh, non_blocking=True)
         g.copy_(gh, non_blocking=True)
         step()
-        dvh.copy_(dv, non_blocking=True)
-        dgh.copy_(dg, non_blocking=True)
+        if wn:
+            dvh.copy_(dv, non_blocking=True)
+            dgh.copy_(dg, non_blocking=True)
+        else:
+            dwh.copy_(dw, non_blocking=True)
 
     e2e_step()
     torch.cuda.synchronize()
@@ -489,6 +514,9 @@ def run_training(args, world, rank, dist, barrier, name, rows):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
+    # kernels of ours per step: [wn_fwd], train_fwd, backward (fused kernel + reduce, or for the
+    # streamed network data-gradient chain + weight-gradient kernel + reduce), [wn_bwd]
+    launches_per_step = (2 if wn else 0) + 1 + (3 if dims == (256, 256, 256, 256) else 2)
     peaks = load_peaks()
     per_step = ms / 1e3 / args.train_steps
     tflops = flop_per_row * M / per_step / 1e12
@@ -517,9 +545,10 @@ def run_training(args, world, rank, dist, barrier, name, rows):
                      "flop_per_row": flop_per_row, "algorithmic_bytes_per_row": bytes_per_row},
         "e2e": {"value": world * M * n_e2e / (e2e_ms / 1e3), "unit": "rows/s",
                 "h2d_bytes_per_step": M * (dims[0] + dims[-1]) * 2,
-                "d2h_bytes_per_step": (dv.numel() + dg.numel()) * 4,
-                "api": "C ABI (mlpk_wn_fwd, mlpk_train_fwd, mlpk_bwd, mlpk_wn_bwd) with pinned host buffers"},
-        "gpu_launches": 5 * args.train_steps,
+                "d2h_bytes_per_step": ((dv.numel() + dg.numel()) if wn else dw.numel()) * 4,
+                "api": "C ABI (" + ("mlpk_wn_fwd, " if wn else "") + "mlpk_train_fwd, mlpk_bwd"
+                       + (", mlpk_wn_bwd" if wn else "") + ") with pinned host buffers"},
+        "gpu_launches": launches_per_step * args.train_steps,
     }
 
 

@@ -18,14 +18,20 @@
 // fp32 partial per CTA; mlpk_reduce sums the partials in a fixed order (level
 // 2), so weight gradients are bitwise deterministic.
 //
-// Roles: warp 0 = TMA producer (weights once, then per tile g, h_l, x with
-// prefetch as buffers free up), warp 1 = TMEM owner + MMA issuer (one lane),
-// warps 2..5 = epilogue (thread = tile row; sigmoid multiply in registers,
-// dz written straight into the swizzled smem tile that the next layer's two
+// Roles: warp 0 = TMA producer (weights once; then, per tile, g, h_{L-1} ..
+// h_1 and x through a ring of generic tile slots, as far ahead as the ring
+// allows), warp 1 = TMEM owner + MMA issuer (one lane), 4*NG epilogue warps
+// (thread = tile row, NG column groups; sigmoid multiply in registers, dz
+// written straight into the swizzled smem tile "G" that the next layer's two
 // UMMAs read as K-major A (dgrad) and MN-major B (wgrad)).
 //
-// Shared memory: all weights (read as K-major B = W^T for dgrad), one buffer
-// per h_l, x, and one "G" buffer that holds g, then each dz, then dx staging.
+// Per layer the MMA warp issues the dgrad first and commits it, then the
+// wgrad: the epilogue's sigmoid multiply of layer l overlaps the wgrad of
+// layer l, and only its stores into G wait for the wgrad to have read G.
+//
+// Shared memory: all weights (read as K-major B = W^T for dgrad), G (each dz),
+// the ring of tile slots (dx is staged in x's slot for its TMA store) and,
+// for 64-wide layers, a zeroed chunk that pads a weight-gradient M to 128.
 // TMEM: one fp32 accumulator per dW_l plus one dgrad accumulator.
 #pragma once
 #include "fwd_kernel.cuh"
@@ -80,17 +86,35 @@ struct BwdCfg {
     for (int i = 0; i < l; ++i) c += wg_n(i);
     return c;
   }
+  // widest dgrad output (d_0 .. d_{L-1}); the epilogue has NG column groups of
+  // 4 warps so that a thread handles at most 32 columns of a layer
+  __host__ __device__ static constexpr int dgmax() {
+    int m = 0;
+    for (int l = 0; l < L; ++l) m = NetT::dim(l) > m ? NetT::dim(l) : m;
+    return m;
+  }
+  static constexpr int NG = dgmax() >= 128 ? 4 : dgmax() >= 64 ? 2 : 1;
+  static constexpr int EPI_WARPS = 4 * NG;
+  static constexpr int THREADS = (2 + EPI_WARPS) * 32;
+  __host__ __device__ static constexpr bool groups_ok() {
+    for (int l = 0; l < L; ++l) {
+      const int cw = NetT::dim(l) / NG;
+      if (NetT::dim(l) % NG != 0 || (cw != 8 && cw != 16 && cw != 32 && cw != 64)) return false;
+    }
+    return true;
+  }
   static constexpr int TILE_BYTES = align_up(tile_bytes(kTileM, DMAX), 1024);
   static constexpr int W_TOTAL = NetT::w_total();
   static constexpr int OFF_G = W_TOTAL;
-  static constexpr int OFF_X = OFF_G + TILE_BYTES;
-  static constexpr int OFF_H = OFF_X + TILE_BYTES;                 // h_1 .. h_{L-1}
-  static constexpr int OFF_ZERO = OFF_H + (L - 1) * TILE_BYTES;    // zero chunk (M padding)
-  static constexpr int ZERO_BYTES = any_pad() ? 16384 : 0;         // 128 rows x 128 B
+  static constexpr int OFF_RING = OFF_G + TILE_BYTES;
+  static constexpr int ZERO_BYTES = any_pad() ? 16384 : 0;  // 128 rows x 128 B
+  // barriers: w_full, slot_full[RING], slot_empty[RING], acc_full, acc_free,
+  //           wg_done, dz_full, out_ready, mma_done
+  static constexpr int RING_FIT = (232448 - 1024 - 16 - 8 * (1 + 2 * 8 + 6) - OFF_RING - ZERO_BYTES) / TILE_BYTES;
+  static constexpr int RING = RING_FIT > 8 ? 8 : RING_FIT;
+  static constexpr int OFF_ZERO = OFF_RING + RING * TILE_BYTES;
   static constexpr int OFF_BAR = OFF_ZERO + ZERO_BYTES;
-  // barriers: w_full, g_full, g_empty, x_full, x_empty, acc_full, dz_full,
-  //           acc_free, out_ready, mma_done, h_full[L-1], h_empty[L-1]
-  static constexpr int NUM_BARS = 10 + 2 * (L - 1);
+  static constexpr int NUM_BARS = 1 + 2 * RING + 6;
   static constexpr int OFF_MISC = OFF_BAR + 8 * NUM_BARS;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static constexpr int ACC_COL = dw_col(L);
@@ -101,9 +125,10 @@ struct BwdCfg {
     for (int i = 0; i < L; ++i) n += NetT::dim(i) * NetT::dim(i + 1);
     return n;
   }();
-  static constexpr int THREADS = 6 * 32;
   static_assert(plans_ok(), "weight-gradient GEMM shapes not supported");
+  static_assert(groups_ok(), "layer widths vs epilogue column groups");
   static_assert(NetT::hidden_uniform(), "all hidden layers must have the same width");
+  static_assert(RING >= 2, "the tile ring needs at least two slots");
   static_assert(TMEM_COLS_RAW <= 512, "dW + dgrad accumulators exceed TMEM");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
 };
@@ -139,11 +164,24 @@ __device__ __forceinline__ float2 dsoftplus_mul_x2(float2 dh, float2 h) {
   return __ffma2_rn(make_float2(-e.x, -e.y), dh, dh);              // dh - dh*e
 }
 
+// CW consecutive fp32 TMEM columns of this warp's lanes, loaded and waited.
+template <int CW>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[CW]) {
+  if constexpr (CW == 8) tmem_ld_wait_x8(taddr, r);
+  else if constexpr (CW == 16) tmem_ld_wait_x16(taddr, r);
+  else if constexpr (CW == 32) tmem_ld_wait_x32(taddr, r);
+  else tmem_ld_wait_x64(taddr, r);
+}
+
 template <class NetT>
 __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
     mlp_bwd_kernel(const __grid_constant__ BwdMaps<NetT::L> maps, int num_tiles) {
   using Cfg = BwdCfg<NetT>;
   constexpr int L = Cfg::L;
+  constexpr int R = Cfg::RING;
+  constexpr int NLD = L + 1;  // loads per tile: k = 0 g, k = 1..L-1 h_{L-k}, k = L x
+  constexpr int NG = Cfg::NG;
+  constexpr int EW = Cfg::EPI_WARPS;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t sbase = (raw + 1023u) & ~1023u;
@@ -151,21 +189,18 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
 
   const uint32_t s_w = sbase;
   const uint32_t s_g = sbase + Cfg::OFF_G;
-  const uint32_t s_xb = sbase + Cfg::OFF_X;
-  auto s_h = [&](int l) { return sbase + Cfg::OFF_H + (l - 1) * Cfg::TILE_BYTES; };  // l >= 1
+  auto slot_addr = [&](int r) { return sbase + Cfg::OFF_RING + static_cast<uint32_t>(r) * Cfg::TILE_BYTES; };
+  const uint32_t s_zero = sbase + Cfg::OFF_ZERO;
   const uint32_t s_bar = sbase + Cfg::OFF_BAR;
   const uint32_t bar_w_full = s_bar;
-  const uint32_t bar_g_full = s_bar + 8;
-  const uint32_t bar_g_empty = s_bar + 16;
-  const uint32_t bar_x_full = s_bar + 24;
-  const uint32_t bar_x_empty = s_bar + 32;
-  const uint32_t bar_acc_full = s_bar + 40;
-  const uint32_t bar_dz_full = s_bar + 48;
-  const uint32_t bar_acc_free = s_bar + 56;
-  const uint32_t bar_out_ready = s_bar + 64;
-  const uint32_t bar_mma_done = s_bar + 72;
-  auto bar_h_full = [&](int l) { return s_bar + 80 + 8u * (l - 1); };
-  auto bar_h_empty = [&](int l) { return s_bar + 80 + 8u * (L - 1) + 8u * (l - 1); };
+  auto bar_slot_full = [&](int r) { return s_bar + 8u + 8u * r; };
+  auto bar_slot_empty = [&](int r) { return s_bar + 8u + 8u * (R + r); };
+  const uint32_t bar_acc_full = s_bar + 8u + 16u * R;  // dgrad accumulator written
+  const uint32_t bar_acc_free = bar_acc_full + 8;      // ... and read (once per tile)
+  const uint32_t bar_wg_done = bar_acc_full + 16;      // this layer's wgrad has read its operands
+  const uint32_t bar_dz_full = bar_acc_full + 24;      // G holds the next layer's dz
+  const uint32_t bar_out_ready = bar_acc_full + 32;    // dx staged
+  const uint32_t bar_mma_done = bar_acc_full + 40;
   const uint32_t s_tmem_slot = sbase + Cfg::OFF_MISC;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + Cfg::OFF_MISC + 4);
 
@@ -174,19 +209,16 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar_w_full, 1);
-    mbar_init(bar_g_full, 1);
-    mbar_init(bar_g_empty, 1);
-    mbar_init(bar_x_full, 1);
-    mbar_init(bar_x_empty, 1);
-    mbar_init(bar_acc_full, 1);
-    mbar_init(bar_dz_full, 4);
-    mbar_init(bar_acc_free, 4);
-    mbar_init(bar_out_ready, 4);
-    mbar_init(bar_mma_done, 1);
-    for (int l = 1; l < L; ++l) {
-      mbar_init(bar_h_full(l), 1);
-      mbar_init(bar_h_empty(l), 4);
+    for (int r = 0; r < R; ++r) {
+      mbar_init(bar_slot_full(r), 1);
+      mbar_init(bar_slot_empty(r), 1 + EW);  // MMA commit + every epilogue warp
     }
+    mbar_init(bar_acc_full, 1);
+    mbar_init(bar_acc_free, EW);
+    mbar_init(bar_wg_done, 1);
+    mbar_init(bar_dz_full, EW);
+    mbar_init(bar_out_ready, EW);
+    mbar_init(bar_mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -196,7 +228,7 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
   }
   if constexpr (Cfg::ZERO_BYTES > 0) {  // zero chunk that pads a 64-wide wgrad M to 128
     for (int i = threadIdx.x; i < Cfg::ZERO_BYTES / 16; i += blockDim.x)
-      st_shared_v4(sbase + Cfg::OFF_ZERO + 16 * i, 0u, 0u, 0u, 0u);
+      st_shared_v4(s_zero + 16 * i, 0u, 0u, 0u, 0u);
     fence_proxy_async_smem();
   }
   tc_fence_before();
@@ -227,21 +259,29 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
         for (int c = 0; c < d / C; ++c) tma_load_2d(dst + c * kTileM * P, map, bar, c * C, t * kTileM);
       };
       bool ok = true;
+      int issued = 0;
       for (int i = 0; ok; ++i) {
         const int t = tile_of(i);
         if (t >= num_tiles) break;
-        const uint32_t par = (i & 1) ^ 1;
-        // in the order the buffers free up: h_{L-1} .. h_1, x, g
-        static_for<1, L>([&](auto lc) {
-          constexpr int l = L - decltype(lc)::value;  // L-1 .. 1
+        static_for<0, NLD>([&](auto kc) {
+          constexpr int k = decltype(kc)::value;
           if (!ok) return;
-          ok = mbar_wait(bar_h_empty(l), par, abort_flag, kDevTimeoutEmpty);
-          if (ok) load_tile(&maps.h[l - 1], s_h(l), bar_h_full(l), NetT::template D<l>(), t);
+          const int n = i * NLD + k;
+          const int r = n % R;
+          ok = mbar_wait(bar_slot_empty(r), ((n / R) & 1) ^ 1, abort_flag, kDevTimeoutEmpty);
+          if (!ok) return;
+          if constexpr (k == 0) load_tile(&maps.g, slot_addr(r), bar_slot_full(r), Cfg::DL, t);
+          else if constexpr (k == L) load_tile(&maps.x, slot_addr(r), bar_slot_full(r), Cfg::D0, t);
+          else load_tile(&maps.h[L - k - 1], slot_addr(r), bar_slot_full(r), NetT::template D<L - k>(), t);
+          ++issued;
         });
-        if (ok) ok = mbar_wait(bar_x_empty, par, abort_flag, kDevTimeoutEmpty);
-        if (ok) load_tile(&maps.x, s_xb, bar_x_full, Cfg::D0, t);
-        if (ok) ok = mbar_wait(bar_g_empty, par, abort_flag, kDevTimeoutEmpty);
-        if (ok) load_tile(&maps.g, s_g, bar_g_full, Cfg::DL, t);
+      }
+      // Drain: never leave the CTA with a TMA load still writing shared memory.
+      volatile int no_abort = 0;
+      mbar_wait(bar_w_full, 0, &no_abort, kDevTimeoutFull);
+      for (int r = 0; r < R; ++r) {
+        const int uses = issued > r ? (issued - r + R - 1) / R : 0;
+        if (uses > 0) mbar_wait(bar_slot_full(r), (uses - 1) & 1, &no_abort, kDevTimeoutFull);
       }
     }
     __syncwarp();
@@ -258,58 +298,58 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
         constexpr int DI = NetT::template D<l>();      // d_l
         constexpr int DO = NetT::template D<l + 1>();  // d_{l+1}
         if (!ok) return;
-        // G holds dz_{l+1}: g for the last layer (TMA), else written by the epilogue
+        const int ng = i * NLD;            // g
+        const int na = i * NLD + (L - l);  // h_l (x for l == 0)
+        // dz_{l+1}: g (a ring slot) for the last layer, else G written by the epilogue
+        uint32_t zsrc = s_g;
         if constexpr (l == L - 1) {
-          ok = __all_sync(0xffffffffu, mbar_wait(bar_g_full, i & 1, abort_flag, kDevTimeoutMma)) &&
-               __all_sync(0xffffffffu,
-                          mbar_wait(bar_acc_free, (i & 1) ^ 1, abort_flag, kDevTimeoutMma));
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_slot_full(ng % R), (ng / R) & 1, abort_flag,
+                                                 kDevTimeoutMma)) &&
+               __all_sync(0xffffffffu, mbar_wait(bar_acc_free, (i & 1) ^ 1, abort_flag, kDevTimeoutMma));
+          zsrc = slot_addr(ng % R);
         } else {
           ok = __all_sync(0xffffffffu, mbar_wait(bar_dz_full, (i * (L - 1) + (L - 2 - l)) & 1,
                                                  abort_flag, kDevTimeoutMma));
         }
         if (!ok) return;
-        // A operand of the wgrad: h_l (x for l == 0)
-        if constexpr (l == 0) {
-          ok = __all_sync(0xffffffffu, mbar_wait(bar_x_full, i & 1, abort_flag, kDevTimeoutMma));
-        } else {
-          ok = __all_sync(0xffffffffu, mbar_wait(bar_h_full(l), i & 1, abort_flag, kDevTimeoutMma));
-        }
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(bar_slot_full(na % R), (na / R) & 1, abort_flag, kDevTimeoutMma));
         if (!ok) return;
         tc_fence_after();
-        const uint32_t a_h = (l == 0) ? s_xb : s_h(l);
+        const uint32_t a_h = slot_addr(na % R);
         if (issuer) {
-          // wgrad over the 128 tile rows (K): dW_l += h_l^T dz (A = h_l, B = dz) or,
-          // transposed, dW_l^T += dz^T h_l (A = dz, B = h_l); both operands
-          // MN-major from shared memory; a 64-wide A is padded to M = 128 by
-          // pointing its second 64-column chunk (LBO) at the zero chunk.
-          {
-            constexpr bool TR = Cfg::wg_trans(l);
-            constexpr int MW = Cfg::wg_m(l);
-            constexpr int NW = Cfg::wg_n(l);
-            constexpr uint32_t idesc_w = make_idesc_f16(kTileM, NW, 1, 1);
-            const uint32_t a_base = TR ? s_g : a_h;
-            const uint32_t b_base = TR ? a_h : s_g;
-            constexpr int PA = pitch_bytes(MW);
-            const uint32_t lbo = (MW < 128) ? (sbase + Cfg::OFF_ZERO - a_base) : kTileM * PA;
-            const uint64_t aw0 = make_sdesc(a_base, lbo, 8 * PA, umma_layout_code(PA));
-            const uint64_t bw0 = mnmajor_base_desc<kTileM, NW>(b_base);
-            const uint32_t dw = tmem_base + Cfg::dw_col(l);
-#pragma unroll
-            for (int k = 0; k < kTileM / 16; ++k)
-              umma_f16(dw, aw0 + (mnmajor_koff<MW>(k) >> 4), bw0 + (mnmajor_koff<NW>(k) >> 4),
-                       idesc_w, (i > 0 || k > 0) ? 1u : 0u);
-          }
           // dgrad: dh_l[128 x d_l] = dz W_l^T: A = dz (K-major, K = d_{l+1}),
           // B = W_l as stored ([d_l rows][d_{l+1}] = K-major W_l^T)
           constexpr uint32_t idesc_d = make_idesc_f16(kTileM, DI, 0, 0);
-          const uint64_t ad0 = kmajor_base_desc<DO>(s_g);
+          const uint64_t ad0 = kmajor_base_desc<DO>(zsrc);
           const uint64_t bd0 = kmajor_base_desc<DO>(s_w + NetT::template w_off<l>());
 #pragma unroll
           for (int k = 0; k < DO / 16; ++k)
             umma_f16(acc, ad0 + (kmajor_koff<kTileM, DO>(k) >> 4),
                      bd0 + (kmajor_koff<DI, DO>(k) >> 4), idesc_d, k > 0 ? 1u : 0u);
           umma_commit(bar_acc_full);
-          if constexpr (l == 0) umma_commit(bar_x_empty);
+          // wgrad over the 128 tile rows (K): dW_l += h_l^T dz (A = h_l, B = dz) or,
+          // transposed, dW_l^T += dz^T h_l (A = dz, B = h_l); both operands
+          // MN-major from shared memory; a 64-wide A is padded to M = 128 by
+          // pointing its second 64-column chunk (LBO) at the zero chunk.
+          constexpr bool TR = Cfg::wg_trans(l);
+          constexpr int MW = Cfg::wg_m(l);
+          constexpr int NW = Cfg::wg_n(l);
+          constexpr uint32_t idesc_w = make_idesc_f16(kTileM, NW, 1, 1);
+          const uint32_t a_base = TR ? zsrc : a_h;
+          const uint32_t b_base = TR ? a_h : zsrc;
+          constexpr int PA = pitch_bytes(MW);
+          const uint32_t lbo = (MW < 128) ? (s_zero - a_base) : kTileM * PA;
+          const uint64_t aw0 = make_sdesc(a_base, lbo, 8 * PA, umma_layout_code(PA));
+          const uint64_t bw0 = mnmajor_base_desc<kTileM, NW>(b_base);
+          const uint32_t dw = tmem_base + Cfg::dw_col(l);
+#pragma unroll
+          for (int k = 0; k < kTileM / 16; ++k)
+            umma_f16(dw, aw0 + (mnmajor_koff<MW>(k) >> 4), bw0 + (mnmajor_koff<NW>(k) >> 4), idesc_w,
+                     (i > 0 || k > 0) ? 1u : 0u);
+          umma_commit(bar_wg_done);
+          umma_commit(bar_slot_empty(na % R));
+          if constexpr (l == L - 1) umma_commit(bar_slot_empty(ng % R));
         }
         __syncwarp();
       });
@@ -323,11 +363,13 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;
+    const int e = warp - 2;
+    const int q = warp & 3;     // TMEM lane quarter this warp may access
+    const int grp = e >> 2;     // column group
     const uint32_t row = q * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t acc = tmem_base + lane_off + Cfg::ACC_COL;
-    const bool store_leader = (warp == 2 && lane == 0);
+    const bool store_leader = (e == 0 && lane == 0);
     bool ok = true;
     for (int i = 0; ok; ++i) {
       const int t = tile_of(i);
@@ -335,60 +377,67 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
       static_for<0, L>([&](auto lc) {
         constexpr int l = L - 1 - decltype(lc)::value;  // dgrad result dh_l
         constexpr int DI = NetT::template D<l>();
+        constexpr int CW = DI / NG;                      // this group's columns
         if (!ok) return;
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait(bar_acc_full, (i * L + (L - 1 - l)) & 1, abort_flag, kDevTimeoutEpi));
+        const int step = i * L + (L - 1 - l);
+        const int c0 = grp * CW;
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_acc_full, step & 1, abort_flag, kDevTimeoutEpi));
         if (!ok) return;
         tc_fence_after();
+        // the g slot is only read by the MMAs: release this warp's share now
+        if constexpr (l == L - 1)
+          if (lane == 0) mbar_arrive(bar_slot_empty((i * NLD) % R));
+        uint32_t r[CW];
+        tmem_ld_cols<CW>(acc + c0, r);
+        uint32_t o[CW / 2];
         if constexpr (l > 0) {
-          // dz_l = dh_l * softplus'(z_l) = dh_l * (1 - e^{-h_l}) -> G (fp16)
-          const uint32_t hb = s_h(l);
-#pragma unroll 1
-          for (int c = 0; c < DI; c += 32) {
-            uint32_t r[32];
-            tmem_ld_wait_x32(acc + c, r);
+          // dz_l = dh_l * softplus'(z_l) = dh_l * (1 - e^{-h_l}), h_l from its slot
+          const int nh = i * NLD + (L - l);
+          const uint32_t hb = slot_addr(nh % R);
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(bar_slot_full(nh % R), (nh / R) & 1, abort_flag, kDevTimeoutEpi));
+          if (!ok) return;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const uint4 hv = ld_tile_row8<DI>(hb, row, c + 8 * u);
-              const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
-              uint32_t o[4];
+          for (int u = 0; u < CW / 8; ++u) {
+            const uint4 hv = ld_tile_row8<DI>(hb, row, c0 + 8 * u);
+            const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float2 dz = dsoftplus_mul_x2(
-                    make_float2(__uint_as_float(r[8 * u + 2 * j]), __uint_as_float(r[8 * u + 2 * j + 1])),
-                    half2_to_float2(hw[j]));
-                o[j] = pack_half2(dz.x, dz.y);
-              }
-              st_tile_row8<DI>(s_g, row, c + 8 * u, o[0], o[1], o[2], o[3]);
+            for (int j = 0; j < 4; ++j) {
+              const float2 dz = dsoftplus_mul_x2(
+                  make_float2(__uint_as_float(r[8 * u + 2 * j]), __uint_as_float(r[8 * u + 2 * j + 1])),
+                  half2_to_float2(hw[j]));
+              o[4 * u + j] = pack_half2(dz.x, dz.y);
             }
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_slot_empty(nh % R));  // h_l read
+          // G still holds dz_{l+1} until this layer's wgrad has read it
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_wg_done, step & 1, abort_flag, kDevTimeoutEpi));
+          if (!ok) return;
+#pragma unroll
+          for (int u = 0; u < CW / 8; ++u)
+            st_tile_row8<DI>(s_g, row, c0 + 8 * u, o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
           fence_proxy_async_smem();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(bar_dz_full);
-            mbar_arrive(bar_h_empty(l));
-          }
+          if (lane == 0) mbar_arrive(bar_dz_full);
         } else {
-          // dx = dh_0 -> fp16 staged in G -> TMA store
-#pragma unroll 1
-          for (int c = 0; c < DI; c += 32) {
-            uint32_t r[32];
-            tmem_ld_wait_x32(acc + c, r);
+          // dx = dh_0 -> fp16, staged in x's slot (free once the wgrad read x) -> TMA store
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              uint32_t o[4];
-              pack_cols<4, false>(r + 8 * u, o);
-              st_tile_row8<DI>(s_g, row, c + 8 * u, o[0], o[1], o[2], o[3]);
-            }
-          }
-          fence_proxy_async_smem();
+          for (int u = 0; u < CW / 8; ++u) pack_cols<4, false>(r + 8 * u, o + 4 * u);
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(bar_acc_free);
-            mbar_arrive(bar_out_ready);
-          }
+          if (lane == 0) mbar_arrive(bar_acc_free);  // accumulator read
+          const int nx = i * NLD + L;
+          const uint32_t xb = slot_addr(nx % R);
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_wg_done, step & 1, abort_flag, kDevTimeoutEpi));
+          if (!ok) return;
+#pragma unroll
+          for (int u = 0; u < CW / 8; ++u)
+            st_tile_row8<DI>(xb, row, c0 + 8 * u, o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_out_ready);
           if (store_leader) {
             ok = mbar_wait(bar_out_ready, i & 1, abort_flag, kDevTimeoutEpi);
             if (ok) {
@@ -396,17 +445,18 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
               constexpr int P = pitch_bytes(DI);
 #pragma unroll
               for (int cc = 0; cc < DI / C; ++cc)
-                tma_store_2d(&maps.dx, s_g + cc * kTileM * P, cc * C, t * kTileM);
+                tma_store_2d(&maps.dx, xb + cc * kTileM * P, cc * C, t * kTileM);
               bulk_commit_group();
               bulk_wait_group_read<0>();
-              mbar_arrive(bar_g_empty);  // G may take the next tile's g
+              mbar_arrive_cnt(bar_slot_empty(nx % R), EW);  // x's slot may take a new tile
             }
           }
           ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         }
       });
     }
-    // dump this CTA's dW partials: lane (row of dW_l) x d_{l+1} fp32
+    // dump this CTA's dW partials: accumulator lane = row of dW_l (or, transposed,
+    // column); 16-column pieces are shared round-robin by the column groups
     if (ok) {
       ok = __all_sync(0xffffffffu, mbar_wait(bar_mma_done, 0, abort_flag, kDevTimeoutEpi));
       tc_fence_after();
@@ -421,12 +471,11 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
         constexpr int MW = Cfg::wg_m(l);
         constexpr int NW = Cfg::wg_n(l);
         const uint32_t dw = tmem_base + lane_off + Cfg::dw_col(l);
-        // lane `row` of the accumulator: row of dW_l, or (transposed) column
-        if (row < static_cast<uint32_t>(MW)) {
 #pragma unroll 1
-          for (int c = 0; c < NW; c += 16) {
-            uint32_t r[16];
-            tmem_ld_wait_x16(dw + c, r);
+        for (int c = 16 * grp; c < NW; c += 16 * NG) {
+          uint32_t r[16];
+          tmem_ld_wait_x16(dw + c, r);  // every lane takes part in the warp-wide load
+          if (row < static_cast<uint32_t>(MW)) {
             if constexpr (!TR) {
               float4* dst = reinterpret_cast<float4*>(part + off + row * DO + c);
 #pragma unroll
@@ -437,13 +486,6 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
 #pragma unroll
               for (int v = 0; v < 16; ++v) part[off + (c + v) * DO + row] = __uint_as_float(r[v]);
             }
-          }
-        } else {
-          // lanes past M still take part in the warp-wide TMEM loads
-#pragma unroll 1
-          for (int c = 0; c < NW; c += 16) {
-            uint32_t r[16];
-            tmem_ld_wait_x16(dw + c, r);
           }
         }
         off += NetT::dim(l) * DO;
