@@ -94,8 +94,13 @@ struct BwdCfg {
     return m;
   }
   static constexpr int NG = dgmax() >= 128 ? 4 : dgmax() >= 64 ? 2 : 1;
-  static constexpr int EPI_WARPS = 4 * NG;
-  static constexpr int THREADS = (2 + EPI_WARPS) * 32;
+  static constexpr int EPI_WARPS = 4 * NG;  // per slot
+  // Tiles in flight ("slots"): two when TMEM holds a second dgrad accumulator
+  // next to the dW accumulators; the MMA warp then alternates the slots' layer
+  // steps so one slot's epilogue overlaps the other slot's MMAs.
+  static constexpr int ACC_W = align_up(DMAX, 32);
+  static constexpr int NS = dw_col(L) + 2 * ACC_W <= 512 ? 2 : 1;
+  static constexpr int THREADS = (2 + NS * EPI_WARPS) * 32;
   __host__ __device__ static constexpr bool groups_ok() {
     for (int l = 0; l < L; ++l) {
       const int cw = NetT::dim(l) / NG;
@@ -105,20 +110,21 @@ struct BwdCfg {
   }
   static constexpr int TILE_BYTES = align_up(tile_bytes(kTileM, DMAX), 1024);
   static constexpr int W_TOTAL = NetT::w_total();
-  static constexpr int OFF_G = W_TOTAL;
-  static constexpr int OFF_RING = OFF_G + TILE_BYTES;
+  static constexpr int OFF_G = W_TOTAL;                  // G of slot s at OFF_G + s * TILE_BYTES
+  static constexpr int OFF_RING = OFF_G + NS * TILE_BYTES;
   static constexpr int ZERO_BYTES = any_pad() ? 16384 : 0;  // 128 rows x 128 B
-  // barriers: w_full, slot_full[RING], slot_empty[RING], acc_full, acc_free,
-  //           wg_done, dz_full, out_ready, mma_done
-  static constexpr int RING_FIT = (232448 - 1024 - 16 - 8 * (1 + 2 * 8 + 6) - OFF_RING - ZERO_BYTES) / TILE_BYTES;
+  // barriers: w_full, slot_full[RING], slot_empty[RING], then per tile slot
+  //           acc_full, acc_free, wg_done, dz_full, out_ready; mma_done
+  static constexpr int RING_FIT =
+      (232448 - 1024 - 16 - 8 * (2 + 2 * 8 + 5 * NS) - OFF_RING - ZERO_BYTES) / TILE_BYTES;
   static constexpr int RING = RING_FIT > 8 ? 8 : RING_FIT;
   static constexpr int OFF_ZERO = OFF_RING + RING * TILE_BYTES;
   static constexpr int OFF_BAR = OFF_ZERO + ZERO_BYTES;
-  static constexpr int NUM_BARS = 1 + 2 * RING + 6;
+  static constexpr int NUM_BARS = 2 + 2 * RING + 5 * NS;
   static constexpr int OFF_MISC = OFF_BAR + 8 * NUM_BARS;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static constexpr int ACC_COL = dw_col(L);
-  static constexpr int TMEM_COLS_RAW = ACC_COL + align_up(DMAX, 32);
+  static constexpr int TMEM_COLS_RAW = ACC_COL + NS * ACC_W;
   static constexpr int TMEM_COLS = TMEM_COLS_RAW <= 128 ? 128 : TMEM_COLS_RAW <= 256 ? 256 : 512;
   static constexpr int PARTIAL_FLOATS = [] {
     int n = 0;
@@ -129,6 +135,9 @@ struct BwdCfg {
   static_assert(groups_ok(), "layer widths vs epilogue column groups");
   static_assert(NetT::hidden_uniform(), "all hidden layers must have the same width");
   static_assert(RING >= 2, "the tile ring needs at least two slots");
+  // with two tiles in flight the ring must hold one tile's loads plus the
+  // first two of the next (see the producer)
+  static_assert(NS == 1 || RING >= L + 3, "ring too shallow for two tiles in flight");
   static_assert(TMEM_COLS_RAW <= 512, "dW + dgrad accumulators exceed TMEM");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
 };
@@ -181,26 +190,28 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
   constexpr int R = Cfg::RING;
   constexpr int NLD = L + 1;  // loads per tile: k = 0 g, k = 1..L-1 h_{L-k}, k = L x
   constexpr int NG = Cfg::NG;
-  constexpr int EW = Cfg::EPI_WARPS;
+  constexpr int EW = Cfg::EPI_WARPS;  // epilogue warps per slot
+  constexpr int NS = Cfg::NS;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t sbase = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (sbase - raw);
 
   const uint32_t s_w = sbase;
-  const uint32_t s_g = sbase + Cfg::OFF_G;
+  auto s_g = [&](int s) { return sbase + Cfg::OFF_G + static_cast<uint32_t>(s) * Cfg::TILE_BYTES; };
   auto slot_addr = [&](int r) { return sbase + Cfg::OFF_RING + static_cast<uint32_t>(r) * Cfg::TILE_BYTES; };
   const uint32_t s_zero = sbase + Cfg::OFF_ZERO;
   const uint32_t s_bar = sbase + Cfg::OFF_BAR;
   const uint32_t bar_w_full = s_bar;
   auto bar_slot_full = [&](int r) { return s_bar + 8u + 8u * r; };
   auto bar_slot_empty = [&](int r) { return s_bar + 8u + 8u * (R + r); };
-  const uint32_t bar_acc_full = s_bar + 8u + 16u * R;  // dgrad accumulator written
-  const uint32_t bar_acc_free = bar_acc_full + 8;      // ... and read (once per tile)
-  const uint32_t bar_wg_done = bar_acc_full + 16;      // this layer's wgrad has read its operands
-  const uint32_t bar_dz_full = bar_acc_full + 24;      // G holds the next layer's dz
-  const uint32_t bar_out_ready = bar_acc_full + 32;    // dx staged
-  const uint32_t bar_mma_done = bar_acc_full + 40;
+  // per tile slot s
+  auto bar_acc_full = [&](int s) { return s_bar + 8u + 16u * R + 40u * s; };  // dgrad accumulator written
+  auto bar_acc_free = [&](int s) { return bar_acc_full(s) + 8; };   // ... and read (once per tile)
+  auto bar_wg_done = [&](int s) { return bar_acc_full(s) + 16; };   // this layer's wgrad read its operands
+  auto bar_dz_full = [&](int s) { return bar_acc_full(s) + 24; };   // G holds the next layer's dz
+  auto bar_out_ready = [&](int s) { return bar_acc_full(s) + 32; }; // dx staged
+  const uint32_t bar_mma_done = bar_acc_full(NS);
   const uint32_t s_tmem_slot = sbase + Cfg::OFF_MISC;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + Cfg::OFF_MISC + 4);
 
@@ -213,11 +224,13 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
       mbar_init(bar_slot_full(r), 1);
       mbar_init(bar_slot_empty(r), 1 + EW);  // MMA commit + every epilogue warp
     }
-    mbar_init(bar_acc_full, 1);
-    mbar_init(bar_acc_free, EW);
-    mbar_init(bar_wg_done, 1);
-    mbar_init(bar_dz_full, EW);
-    mbar_init(bar_out_ready, EW);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(bar_acc_full(s), 1);
+      mbar_init(bar_acc_free(s), EW);
+      mbar_init(bar_wg_done(s), 1);
+      mbar_init(bar_dz_full(s), EW);
+      mbar_init(bar_out_ready(s), EW);
+    }
     mbar_init(bar_mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -287,71 +300,77 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Tiles i = p*NS + s of round p; per layer, every slot's step in turn.
     const bool issuer = (lane == 0);
     bool ok = __all_sync(0xffffffffu, mbar_wait(bar_w_full, 0, abort_flag, kDevTimeoutMma));
     tc_fence_after();
-    const uint32_t acc = tmem_base + Cfg::ACC_COL;
-    for (int i = 0; ok; ++i) {
-      if (tile_of(i) >= num_tiles) break;
+    for (int p = 0; ok; ++p) {
+      if (tile_of(p * NS) >= num_tiles) break;
       static_for<0, L>([&](auto lc) {
         constexpr int l = L - 1 - decltype(lc)::value;  // L-1 .. 0
         constexpr int DI = NetT::template D<l>();      // d_l
         constexpr int DO = NetT::template D<l + 1>();  // d_{l+1}
-        if (!ok) return;
-        const int ng = i * NLD;            // g
-        const int na = i * NLD + (L - l);  // h_l (x for l == 0)
-        // dz_{l+1}: g (a ring slot) for the last layer, else G written by the epilogue
-        uint32_t zsrc = s_g;
-        if constexpr (l == L - 1) {
-          ok = __all_sync(0xffffffffu, mbar_wait(bar_slot_full(ng % R), (ng / R) & 1, abort_flag,
-                                                 kDevTimeoutMma)) &&
-               __all_sync(0xffffffffu, mbar_wait(bar_acc_free, (i & 1) ^ 1, abort_flag, kDevTimeoutMma));
-          zsrc = slot_addr(ng % R);
-        } else {
-          ok = __all_sync(0xffffffffu, mbar_wait(bar_dz_full, (i * (L - 1) + (L - 2 - l)) & 1,
-                                                 abort_flag, kDevTimeoutMma));
-        }
-        if (!ok) return;
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait(bar_slot_full(na % R), (na / R) & 1, abort_flag, kDevTimeoutMma));
-        if (!ok) return;
-        tc_fence_after();
-        const uint32_t a_h = slot_addr(na % R);
-        if (issuer) {
-          // dgrad: dh_l[128 x d_l] = dz W_l^T: A = dz (K-major, K = d_{l+1}),
-          // B = W_l as stored ([d_l rows][d_{l+1}] = K-major W_l^T)
-          constexpr uint32_t idesc_d = make_idesc_f16(kTileM, DI, 0, 0);
-          const uint64_t ad0 = kmajor_base_desc<DO>(zsrc);
-          const uint64_t bd0 = kmajor_base_desc<DO>(s_w + NetT::template w_off<l>());
 #pragma unroll
-          for (int k = 0; k < DO / 16; ++k)
-            umma_f16(acc, ad0 + (kmajor_koff<kTileM, DO>(k) >> 4),
-                     bd0 + (kmajor_koff<DI, DO>(k) >> 4), idesc_d, k > 0 ? 1u : 0u);
-          umma_commit(bar_acc_full);
-          // wgrad over the 128 tile rows (K): dW_l += h_l^T dz (A = h_l, B = dz) or,
-          // transposed, dW_l^T += dz^T h_l (A = dz, B = h_l); both operands
-          // MN-major from shared memory; a 64-wide A is padded to M = 128 by
-          // pointing its second 64-column chunk (LBO) at the zero chunk.
-          constexpr bool TR = Cfg::wg_trans(l);
-          constexpr int MW = Cfg::wg_m(l);
-          constexpr int NW = Cfg::wg_n(l);
-          constexpr uint32_t idesc_w = make_idesc_f16(kTileM, NW, 1, 1);
-          const uint32_t a_base = TR ? zsrc : a_h;
-          const uint32_t b_base = TR ? a_h : zsrc;
-          constexpr int PA = pitch_bytes(MW);
-          const uint32_t lbo = (MW < 128) ? (s_zero - a_base) : kTileM * PA;
-          const uint64_t aw0 = make_sdesc(a_base, lbo, 8 * PA, umma_layout_code(PA));
-          const uint64_t bw0 = mnmajor_base_desc<kTileM, NW>(b_base);
-          const uint32_t dw = tmem_base + Cfg::dw_col(l);
+        for (int s = 0; s < NS; ++s) {
+          const int i = p * NS + s;
+          if (!ok || tile_of(i) >= num_tiles) break;
+          const uint32_t acc = tmem_base + Cfg::ACC_COL + s * Cfg::ACC_W;
+          const int ng = i * NLD;            // g
+          const int na = i * NLD + (L - l);  // h_l (x for l == 0)
+          // dz_{l+1}: g (a ring slot) for the last layer, else the slot's G
+          uint32_t zsrc = s_g(s);
+          if constexpr (l == L - 1) {
+            ok = __all_sync(0xffffffffu, mbar_wait(bar_slot_full(ng % R), (ng / R) & 1, abort_flag,
+                                                   kDevTimeoutMma)) &&
+                 __all_sync(0xffffffffu,
+                            mbar_wait(bar_acc_free(s), (p & 1) ^ 1, abort_flag, kDevTimeoutMma));
+            zsrc = slot_addr(ng % R);
+          } else {
+            ok = __all_sync(0xffffffffu, mbar_wait(bar_dz_full(s), (p * (L - 1) + (L - 2 - l)) & 1,
+                                                   abort_flag, kDevTimeoutMma));
+          }
+          if (!ok) break;
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(bar_slot_full(na % R), (na / R) & 1, abort_flag, kDevTimeoutMma));
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t a_h = slot_addr(na % R);
+          if (issuer) {
+            // dgrad: dh_l[128 x d_l] = dz W_l^T: A = dz (K-major, K = d_{l+1}),
+            // B = W_l as stored ([d_l rows][d_{l+1}] = K-major W_l^T)
+            constexpr uint32_t idesc_d = make_idesc_f16(kTileM, DI, 0, 0);
+            const uint64_t ad0 = kmajor_base_desc<DO>(zsrc);
+            const uint64_t bd0 = kmajor_base_desc<DO>(s_w + NetT::template w_off<l>());
 #pragma unroll
-          for (int k = 0; k < kTileM / 16; ++k)
-            umma_f16(dw, aw0 + (mnmajor_koff<MW>(k) >> 4), bw0 + (mnmajor_koff<NW>(k) >> 4), idesc_w,
-                     (i > 0 || k > 0) ? 1u : 0u);
-          umma_commit(bar_wg_done);
-          umma_commit(bar_slot_empty(na % R));
-          if constexpr (l == L - 1) umma_commit(bar_slot_empty(ng % R));
+            for (int k = 0; k < DO / 16; ++k)
+              umma_f16(acc, ad0 + (kmajor_koff<kTileM, DO>(k) >> 4),
+                       bd0 + (kmajor_koff<DI, DO>(k) >> 4), idesc_d, k > 0 ? 1u : 0u);
+            umma_commit(bar_acc_full(s));
+            // wgrad over the 128 tile rows (K): dW_l += h_l^T dz (A = h_l, B = dz) or,
+            // transposed, dW_l^T += dz^T h_l (A = dz, B = h_l); both operands
+            // MN-major from shared memory; a 64-wide A is padded to M = 128 by
+            // pointing its second 64-column chunk (LBO) at the zero chunk.
+            constexpr bool TR = Cfg::wg_trans(l);
+            constexpr int MW = Cfg::wg_m(l);
+            constexpr int NW = Cfg::wg_n(l);
+            constexpr uint32_t idesc_w = make_idesc_f16(kTileM, NW, 1, 1);
+            const uint32_t a_base = TR ? zsrc : a_h;
+            const uint32_t b_base = TR ? a_h : zsrc;
+            constexpr int PA = pitch_bytes(MW);
+            const uint32_t lbo = (MW < 128) ? (s_zero - a_base) : kTileM * PA;
+            const uint64_t aw0 = make_sdesc(a_base, lbo, 8 * PA, umma_layout_code(PA));
+            const uint64_t bw0 = mnmajor_base_desc<kTileM, NW>(b_base);
+            const uint32_t dw = tmem_base + Cfg::dw_col(l);
+#pragma unroll
+            for (int k = 0; k < kTileM / 16; ++k)
+              umma_f16(dw, aw0 + (mnmajor_koff<MW>(k) >> 4), bw0 + (mnmajor_koff<NW>(k) >> 4), idesc_w,
+                       (i > 0 || k > 0) ? 1u : 0u);
+            umma_commit(bar_wg_done(s));
+            umma_commit(bar_slot_empty(na % R));
+            if constexpr (l == L - 1) umma_commit(bar_slot_empty(ng % R));
+          }
+          __syncwarp();
         }
-        __syncwarp();
       });
     }
     if (issuer) umma_commit(bar_mma_done);
@@ -364,14 +383,18 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int e = warp - 2;
+    const int s = e / EW;       // tile slot served by this warp
+    const int ew = e % EW;
     const int q = warp & 3;     // TMEM lane quarter this warp may access
-    const int grp = e >> 2;     // column group
+    const int grp = ew >> 2;    // column group
     const uint32_t row = q * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    const uint32_t acc = tmem_base + lane_off + Cfg::ACC_COL;
-    const bool store_leader = (e == 0 && lane == 0);
+    const uint32_t acc = tmem_base + lane_off + Cfg::ACC_COL + s * Cfg::ACC_W;
+    const uint32_t sg = s_g(s);
+    const bool store_leader = (ew == 0 && lane == 0);
     bool ok = true;
-    for (int i = 0; ok; ++i) {
+    for (int j = 0; ok; ++j) {
+      const int i = j * NS + s;  // this slot's j-th tile
       const int t = tile_of(i);
       if (t >= num_tiles) break;
       static_for<0, L>([&](auto lc) {
@@ -379,9 +402,9 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
         constexpr int DI = NetT::template D<l>();
         constexpr int CW = DI / NG;                      // this group's columns
         if (!ok) return;
-        const int step = i * L + (L - 1 - l);
+        const int step = j * L + (L - 1 - l);  // this slot's step count
         const int c0 = grp * CW;
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_acc_full, step & 1, abort_flag, kDevTimeoutEpi));
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_acc_full(s), step & 1, abort_flag, kDevTimeoutEpi));
         if (!ok) return;
         tc_fence_after();
         // the g slot is only read by the MMAs: release this warp's share now
@@ -412,34 +435,34 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(bar_slot_empty(nh % R));  // h_l read
           // G still holds dz_{l+1} until this layer's wgrad has read it
-          ok = __all_sync(0xffffffffu, mbar_wait(bar_wg_done, step & 1, abort_flag, kDevTimeoutEpi));
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_wg_done(s), step & 1, abort_flag, kDevTimeoutEpi));
           if (!ok) return;
 #pragma unroll
           for (int u = 0; u < CW / 8; ++u)
-            st_tile_row8<DI>(s_g, row, c0 + 8 * u, o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
+            st_tile_row8<DI>(sg, row, c0 + 8 * u, o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
           fence_proxy_async_smem();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar_dz_full);
+          if (lane == 0) mbar_arrive(bar_dz_full(s));
         } else {
           // dx = dh_0 -> fp16, staged in x's slot (free once the wgrad read x) -> TMA store
 #pragma unroll
           for (int u = 0; u < CW / 8; ++u) pack_cols<4, false>(r + 8 * u, o + 4 * u);
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar_acc_free);  // accumulator read
+          if (lane == 0) mbar_arrive(bar_acc_free(s));  // accumulator read
           const int nx = i * NLD + L;
           const uint32_t xb = slot_addr(nx % R);
-          ok = __all_sync(0xffffffffu, mbar_wait(bar_wg_done, step & 1, abort_flag, kDevTimeoutEpi));
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_wg_done(s), step & 1, abort_flag, kDevTimeoutEpi));
           if (!ok) return;
 #pragma unroll
           for (int u = 0; u < CW / 8; ++u)
             st_tile_row8<DI>(xb, row, c0 + 8 * u, o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar_out_ready);
+          if (lane == 0) mbar_arrive(bar_out_ready(s));
           if (store_leader) {
-            ok = mbar_wait(bar_out_ready, i & 1, abort_flag, kDevTimeoutEpi);
+            ok = mbar_wait(bar_out_ready(s), j & 1, abort_flag, kDevTimeoutEpi);
             if (ok) {
               constexpr int C = chunk_elems(DI);
               constexpr int P = pitch_bytes(DI);
@@ -472,7 +495,7 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
         constexpr int NW = Cfg::wg_n(l);
         const uint32_t dw = tmem_base + lane_off + Cfg::dw_col(l);
 #pragma unroll 1
-        for (int c = 16 * grp; c < NW; c += 16 * NG) {
+        for (int c = 16 * (s * NG + grp); c < NW; c += 16 * NS * NG) {
           uint32_t r[16];
           tmem_ld_wait_x16(dw + c, r);  // every lane takes part in the warp-wide load
           if (row < static_cast<uint32_t>(MW)) {
