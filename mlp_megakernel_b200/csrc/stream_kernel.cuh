@@ -106,30 +106,26 @@ struct StreamCfg {
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
 };
 
-// Loads this thread's saved activations for one data-gradient stage: stripe j
-// of column group grp covers columns 32*(j*NG + grp) .. +31 (64 bytes).  Rows
-// past M (hrow == nullptr) get zeros.  Issued before the accumulator wait so
-// the loads overlap the stage's MMAs.
-template <int N, int NG>
-__device__ __forceinline__ void dgrad_load_h(uint4 (&hv)[N / (32 * NG)][4], const uint8_t* hrow,
-                                             int grp) {
-  constexpr int SUBS = N / (32 * NG);
+// Loads this thread's saved activations of stripe j of one data-gradient
+// stage: stripe j of column group grp covers columns 32*(j*NG + grp) .. +31
+// (64 bytes).  Rows past M (hrow == nullptr) get zeros.
+template <int NG>
+__device__ __forceinline__ void dgrad_load_h(uint4 (&hv)[4], const uint8_t* hrow, int grp, int j) {
+  const int col = 32 * (j * NG + grp);
 #pragma unroll
-  for (int j = 0; j < SUBS; ++j) {
-    const int col = 32 * (j * NG + grp);
-#pragma unroll
-    for (int v = 0; v < 4; ++v)
-      hv[j][v] = hrow ? __ldg(reinterpret_cast<const uint4*>(hrow + 2 * col) + v) : make_uint4(0, 0, 0, 0);
-  }
+  for (int v = 0; v < 4; ++v)
+    hv[v] = hrow ? __ldg(reinterpret_cast<const uint4*>(hrow + 2 * col) + v) : make_uint4(0, 0, 0, 0);
 }
 
 // Data-gradient stage epilogue of one warp (mirrors hidden_job): dz = dh *
 // (1 - e^{-h}) for the thread's row over the group's stripes, fp16 result
 // packed into TMEM at h_tmem_col() for the next stage's A operand, optionally
-// saved to global memory, chunks published as in hidden_job.
+// saved to global memory, chunks published as in hidden_job.  hv holds the
+// first two stripes' h (loaded before the accumulator wait); each later
+// stripe's h is loaded two stripes ahead, into the registers just consumed.
 template <int N, int NG, int SPC, bool SAVE>
-__device__ __forceinline__ void dgrad_job(uint32_t tbuf, int grp, uint32_t chunk_bar0,
-                                          const uint4 (&hv)[N / (32 * NG)][4], uint8_t* dzrow) {
+__device__ __forceinline__ void dgrad_job(uint32_t tbuf, int grp, uint32_t chunk_bar0, uint4 (&hv)[2][4],
+                                          const uint8_t* hrow, uint8_t* dzrow) {
   constexpr int SUBS = N / (32 * NG);
   static_assert(SUBS % SPC == 0, "stripes per chunk must divide the stripes per group");
   uint32_t a[32];
@@ -139,10 +135,10 @@ __device__ __forceinline__ void dgrad_job(uint32_t tbuf, int grp, uint32_t chunk
     const int col = 32 * (j * NG + grp);
     uint32_t b[32];
     if (j + 1 < SUBS) tmem_ld_async_x32(tbuf + col + 32 * NG, b);
-    const uint32_t hw[16] = {hv[j][0].x, hv[j][0].y, hv[j][0].z, hv[j][0].w,
-                             hv[j][1].x, hv[j][1].y, hv[j][1].z, hv[j][1].w,
-                             hv[j][2].x, hv[j][2].y, hv[j][2].z, hv[j][2].w,
-                             hv[j][3].x, hv[j][3].y, hv[j][3].z, hv[j][3].w};
+    uint4(&hc)[4] = hv[j & 1];
+    const uint32_t hw[16] = {hc[0].x, hc[0].y, hc[0].z, hc[0].w, hc[1].x, hc[1].y, hc[1].z, hc[1].w,
+                             hc[2].x, hc[2].y, hc[2].z, hc[2].w, hc[3].x, hc[3].y, hc[3].z, hc[3].w};
+    if (j + 2 < SUBS) dgrad_load_h<NG>(hc, hrow, grp, j + 2);
     uint32_t w[16];
 #pragma unroll
     for (int p = 0; p < 16; ++p) {
@@ -246,6 +242,18 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
         for (int c = 0; c < Cfg::D0 / 64; ++c)
           tma_load_2d(s_x + c * kTileM * 128, &maps.in, bar_x_full, c * 64, t * kTileM);
         ++xs;
+        if constexpr (MODE == kStreamDgrad) {
+          // the epilogue reads the saved activations with plain loads: bring
+          // this tile's (first tile) and the next tile's rows into L2 early
+          for (int tt = (i == 0 ? t : t + G); tt <= t + G && tt < num_tiles; tt += G) {
+            const int rows = maps.M - tt * kTileM < kTileM ? maps.M - tt * kTileM : kTileM;
+#pragma unroll 1
+            for (int s = 0; s + 1 < L; ++s)
+              prefetch_l2_bulk(static_cast<const uint8_t*>(maps.hact[s]) +
+                                   static_cast<size_t>(tt) * kTileM * Cfg::H * 2,
+                               static_cast<uint32_t>(rows) * Cfg::H * 2);
+          }
+        }
         static_for<0, L>([&](auto sc) {
           constexpr int s = decltype(sc)::value;
           constexpr int K = ChainT::template D<s>();
@@ -373,12 +381,14 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
 #pragma unroll 1
       for (int s = 0; s < L - 1; ++s) {
         const int g = i * L + s;
-        uint4 hv[MODE == kStreamDgrad ? H / (32 * NG) : 1][4];
-        if constexpr (MODE == kStreamDgrad)
-          dgrad_load_h<H, NG>(hv, valid ? static_cast<const uint8_t*>(maps.hact[s]) +
-                                              static_cast<size_t>(grow) * H * 2
-                                        : nullptr,
-                              grp);
+        uint4 hv[2][4];
+        const uint8_t* hrow = nullptr;
+        if constexpr (MODE == kStreamDgrad) {
+          hrow = valid ? static_cast<const uint8_t*>(maps.hact[s]) + static_cast<size_t>(grow) * H * 2
+                       : nullptr;
+          dgrad_load_h<NG>(hv[0], hrow, grp, 0);
+          if (H / (32 * NG) > 1) dgrad_load_h<NG>(hv[1], hrow, grp, 1);
+        }
         ok = __all_sync(0xffffffffu,
                         mbar_wait(bar_acc_full(g & 1), (g >> 1) & 1, abort_flag, kDevTimeoutEpi));
         if (!ok) break;
@@ -402,7 +412,7 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
         if constexpr (MODE == kStreamFwd)
           hidden_job<H, NG, Cfg::SPC, false, SAVE>(t_buf, grp, bar_chunk(0), srow);
         else
-          dgrad_job<H, NG, Cfg::SPC, SAVE>(t_buf, grp, bar_chunk(0), hv, srow);
+          dgrad_job<H, NG, Cfg::SPC, SAVE>(t_buf, grp, bar_chunk(0), hv, hrow, srow);
       }
       if (!ok) break;
       {
