@@ -271,11 +271,26 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
         mbar_arrive_expect_tx(bar, kTileM * d * 2);
         for (int c = 0; c < d / C; ++c) tma_load_2d(dst + c * kTileM * P, map, bar, c * C, t * kTileM);
       };
+      auto prefetch_tile = [&](const CUtensorMap* map, int d, int t) {
+        const int C = d < 64 ? d : 64;
+        for (int c = 0; c < d / C; ++c) tma_prefetch_l2_2d(map, c * C, t * kTileM);
+      };
       bool ok = true;
       int issued = 0;
       for (int i = 0; ok; ++i) {
         const int t = tile_of(i);
         if (t >= num_tiles) break;
+        // the ring holds about one tile: bring the NEXT tile's rows into L2 now,
+        // so its ring loads later hit L2 (more bytes in flight per SM)
+        if (tile_of(i + 1) < num_tiles) {
+          const int tn = tile_of(i + 1);
+          prefetch_tile(&maps.g, Cfg::DL, tn);
+          static_for<1, L>([&](auto hc) {
+            constexpr int l = decltype(hc)::value;
+            prefetch_tile(&maps.h[l - 1], NetT::template D<l>(), tn);
+          });
+          prefetch_tile(&maps.x, Cfg::D0, tn);
+        }
         static_for<0, NLD>([&](auto kc) {
           constexpr int k = decltype(kc)::value;
           if (!ok) return;
@@ -448,13 +463,16 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
           // dx = dh_0 -> fp16, staged in x's slot (free once the wgrad read x) -> TMA store
 #pragma unroll
           for (int u = 0; u < CW / 8; ++u) pack_cols<4, false>(r + 8 * u, o + 4 * u);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar_acc_free(s));  // accumulator read
           const int nx = i * NLD + L;
           const uint32_t xb = slot_addr(nx % R);
           ok = __all_sync(0xffffffffu, mbar_wait(bar_wg_done(s), step & 1, abort_flag, kDevTimeoutEpi));
           if (!ok) return;
+          // accumulator read.  Released only after the wg_done wait: the next
+          // tile's first step (which needs acc_free) commits wg_done again, and
+          // a parity wait cannot tell that phase from this one.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_acc_free(s));
 #pragma unroll
           for (int u = 0; u < CW / 8; ++u)
             st_tile_row8<DI>(xb, row, c0 + 8 * u, o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);

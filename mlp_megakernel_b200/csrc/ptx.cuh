@@ -123,6 +123,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
                "r"(src), "r"(c0), "r"(c1)
                : "memory");
 }
+// L2 prefetch of one TMA box (the box a tma_load_2d at these coordinates
+// would load); no shared memory or barrier involved.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
 // Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) of global
 // memory into L2.
 __device__ __forceinline__ void prefetch_l2_bulk(const void* gptr, uint32_t bytes) {
