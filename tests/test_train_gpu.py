@@ -342,3 +342,61 @@ def test_repeated_launches_are_stable(config, dims, M):
         assert torch.equal(out, ref) and torch.equal(out_t, ref)
         assert torch.equal(dx, dx0) and torch.equal(dw, dw0)
     assert _lib.device_status() == 0
+
+
+def test_module_under_autocast():
+    """AMP (mlp_fused.md:168-172): fp32 parameters and input under torch.autocast
+    run the fp16 kernels (custom_fwd casts the inputs); gradients come back in
+    the parameters' dtype."""
+    torch.manual_seed(11)
+    model = FusedMLPSoftplus(D=128, H=128, out_features=128).cuda()  # fp32 parameters
+    M = 5000
+    x, _, g = make_inputs("3L128", M, with_grad=True)
+    xf = x.float().cuda()
+    with torch.autocast("cuda", dtype=torch.float16):
+        out = model(xf)
+    assert out.dtype == torch.float16
+    out.backward(g.cuda())
+    assert all(w.grad.dtype == torch.float32 for w in model.weights)
+    ws = [w.detach().half().float().cpu() for w in model.weights]
+    ref_out, ref_hs = oracle.mlp_forward_train(x.numpy(), [w.numpy() for w in ws])
+    assert rel_max(out.detach().cpu().numpy(), ref_out) <= OUT_TOL
+    _, ref_dws = oracle.mlp_backward(x.numpy(), [w.numpy() for w in ws], ref_hs, g.numpy())
+    for w, rd in zip(model.weights, ref_dws):
+        assert rel_l2(w.grad.cpu().numpy(), rd) <= GRAD_TOL
+
+
+def test_training_step_in_cuda_graph():
+    """A whole training step (weight-normed module forward + backward) captured
+    in a CUDA graph after one eager warm-up step, replayed on new inputs copied
+    into the static buffers: same gradients as eager."""
+    torch.manual_seed(12)
+    model = FusedMLPSoftplusWN(D=32, H=64, out_features=16, num_layers=5).cuda()
+    M = 30000
+    x1, _, g1 = make_inputs("5L", M, with_grad=True)
+    sx, sg = x1.cuda().clone(), g1.cuda().clone()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):  # warm-up (sets kernel attributes, caches)
+        model(sx).backward(sg)
+    torch.cuda.current_stream().wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    model.v_all.grad.zero_()
+    model.g_all.grad.zero_()
+    with torch.cuda.graph(graph):
+        model(sx).backward(sg)
+    # new data through the static buffers
+    x2 = (x1.float() * 0.5).half()
+    g2 = (g1.float() * -1.5).half()
+    sx.copy_(x2.cuda())
+    sg.copy_(g2.cuda())
+    model.v_all.grad.zero_()
+    model.g_all.grad.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    gv, gg = model.v_all.grad.clone(), model.g_all.grad.clone()
+    model.v_all.grad = None
+    model.g_all.grad = None
+    model(x2.cuda()).backward(g2.cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(gv, model.v_all.grad) and torch.equal(gg, model.g_all.grad)
