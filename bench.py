@@ -440,6 +440,11 @@ def run_training(args, world, rank, dist, barrier, name, rows):
     work = torch.empty(int(lib.mlpk_bwd_workspace_size(shape, M)), dtype=torch.uint8, device=dev)
     Wp = _lib.ptr_array([w.data_ptr() for w in W])
     Hp = _lib.ptr_array([h.data_ptr() for h in hs])
+    red = None
+    if dist is not None:  # dW sum over the ranks: NVLink peer-memory kernel on one node
+        from mlp_megakernel_b200.dp import make_grad_reducer
+
+        red = make_grad_reducer(dw.numel())
 
     wn = spec.get("wn", True)
     if not wn:  # plain weights: the step is training forward + backward (+ all-reduce)
@@ -451,10 +456,11 @@ def run_training(args, world, rank, dist, barrier, name, rows):
             _lib.check("wn_fwd", lib.mlpk_wn_fwd(shape, v_all.data_ptr(), g_all.data_ptr(), Wp,
                                                  inv.data_ptr(), st))
         _lib.check("train_fwd", lib.mlpk_train_fwd(shape, M, x.data_ptr(), Wp, out.data_ptr(), Hp, st))
+        local = red.local_buffer(dw) if red is not None else dw
         _lib.check("bwd", lib.mlpk_bwd(shape, M, x.data_ptr(), Wp, Hp, g.data_ptr(), dx.data_ptr(),
-                                       work.data_ptr(), work.numel(), dw.data_ptr(), st))
-        if dist is not None:
-            dist.all_reduce(dw)
+                                       work.data_ptr(), work.numel(), local.data_ptr(), st))
+        if red is not None:
+            red.reduce(local, dw)
         if wn:
             _lib.check("wn_bwd", lib.mlpk_wn_bwd(shape, dw.data_ptr(), v_all.data_ptr(), g_all.data_ptr(),
                                                  inv.data_ptr(), dv.data_ptr(), dg.data_ptr(), st))
@@ -515,8 +521,12 @@ def run_training(args, world, rank, dist, barrier, name, rows):
         e2e_ms = float(t.item())
 
     # kernels of ours per step: [wn_fwd], train_fwd, backward (fused kernel + reduce, or for the
-    # streamed network data-gradient chain + weight-gradient kernel + reduce), [wn_bwd]
-    launches_per_step = (2 if wn else 0) + 1 + (3 if dims == (256, 256, 256, 256) else 2)
+    # streamed network data-gradient chain + weight-gradient kernel + reduce), [peer dW sum], [wn_bwd]
+    peer = red is not None and type(red).__name__ == "PeerGradReducer"
+    launches_per_step = ((2 if wn else 0) + 1 + (3 if dims == (256, 256, 256, 256) else 2)
+                         + (1 if peer else 0))
+    if red is not None:
+        red.close()
     peaks = load_peaks()
     per_step = ms / 1e3 / args.train_steps
     tflops = flop_per_row * M / per_step / 1e12
@@ -533,7 +543,8 @@ def run_training(args, world, rank, dist, barrier, name, rows):
         "scaling": "strong" if spec["strong"] else "weak",
         "config": {"workload": spec["workload"].format(M=M, G=world * M),
                    "dims": list(dims), "rows_per_gpu": M, "global_rows": world * M,
-                   "parallelism": f"dp{world}" + (" (NCCL all-reduce of fp32 dW)" if world > 1 else ""),
+                   "parallelism": f"dp{world}" + ((" (fp32 dW summed by the NVLink peer-memory kernel)" if peer
+                                                   else " (NCCL all-reduce of fp32 dW)") if world > 1 else ""),
                    "l2": "per-step inputs and saved activations larger than L2"
                          if M * dims[1] * 2 * (len(dims) - 2) > 126e6 else
                          "working set partly L2-resident (no flush between steps)"},

@@ -122,6 +122,30 @@ int mlpk_bwd_noalloc(const mlpk_shape* shape, int64_t M, const void* x, const vo
  * device: bit flags set by bounded waits that expired.  Synchronises. */
 int mlpk_device_status(int clear, int* status_out);
 
+/* ---- Data-parallel weight-gradient sum over NVLink peer memory (one node).
+ * Replaces the all_reduce(SUM) of the fp32 dW buffer in the reference's
+ * data-parallel recipe (BASELINE: "training all-reduces the weight gradients
+ * over NVLink"); the reference itself calls NCCL through torch.distributed.
+ * Each rank allocates one peer buffer for n floats (n a multiple of 4), shares
+ * its IPC handle (MLPK_PEER_HANDLE_BYTES bytes) with the other ranks and opens
+ * theirs.  Per step with epoch = 1, 2, ...: the backward writes this rank's dW
+ * into mlpk_peer_slot(own buffer, n, epoch), then mlpk_peer_allreduce sums
+ * every rank's slot in rank order into dW_out (bitwise identical on all
+ * ranks).  Every rank must call it once per epoch, in the same order.  If a
+ * peer does not arrive within the bounded wait (1 s), the kernel sets bit 16
+ * (cross-GPU flag timeout) of the device status word (mlpk_device_status) and
+ * leaves dW_out unwritten.  At most 8 ranks; mlpk_peer_alloc and
+ * mlpk_peer_open allocate / map device memory (set-up calls, not per step). */
+#define MLPK_PEER_HANDLE_BYTES 64
+#define MLPK_PEER_MAX_RANKS 8
+int mlpk_peer_alloc(int64_t n, void** buf_out, void* handle_out);
+int mlpk_peer_open(const void* handle, void** buf_out);
+int mlpk_peer_close(void* peer_buf);
+int mlpk_peer_free(void* buf);
+float* mlpk_peer_slot(void* buf, int64_t n, uint32_t epoch);
+int mlpk_peer_allreduce(void* const* bufs, int world, int rank, int64_t n, uint32_t epoch, float* dW_out,
+                        mlpk_stream_t stream);
+
 /* Text of the CUDA runtime / driver failure behind the calling thread's most
  * recent MLPK_ERR_CUDA ("no error" if none).  The reference reports failures as
  * Python exceptions carrying the CUDA message (cutile_mlp.py:388); this is the

@@ -54,7 +54,16 @@ SIGNATURES = {
     "mlpk_wn_bwd": (ctypes.c_int, [_SHAPE_P, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "mlpk_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "mlpk_last_cuda_error": (ctypes.c_char_p, []),
+    "mlpk_peer_alloc": (ctypes.c_int, [ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]),
+    "mlpk_peer_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "mlpk_peer_close": (ctypes.c_int, [ctypes.c_void_p]),
+    "mlpk_peer_free": (ctypes.c_int, [ctypes.c_void_p]),
+    "mlpk_peer_slot": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_uint32]),
+    "mlpk_peer_allreduce": (ctypes.c_int, [_VPP, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_uint32,
+                                           _vp, _vp]),
 }
+PEER_HANDLE_BYTES = 64
+PEER_MAX_RANKS = 8
 
 _lock = threading.Lock()
 _lib = None

@@ -19,6 +19,7 @@
 #include "bwd_kernel.cuh"
 #include "fwd2_kernel.cuh"
 #include "stream_kernel.cuh"
+#include "peer_kernel.cuh"
 #include "wgrad_kernel.cuh"
 #include "wn_kernel.cuh"
 
@@ -701,6 +702,67 @@ int mlpk_device_status(int clear, int* status_out) {
     if ((rc = cuda_status(cudaMemcpyToSymbol(mlpk::g_device_status, &z, sizeof(int))))) return rc;
   }
   return MLPK_OK;
+}
+
+// ------------------------------------------------------------------ peer-memory dW sum
+int mlpk_peer_alloc(int64_t n, void** buf_out, void* handle_out) {
+  if (!buf_out || !handle_out) return MLPK_ERR_NULL;
+  if (n <= 0 || n % 4 != 0) return MLPK_ERR_SHAPE;
+  static_assert(sizeof(cudaIpcMemHandle_t) == MLPK_PEER_HANDLE_BYTES, "IPC handle size");
+  // two slots of n floats, then ready[8], done[8], count (32-bit words, padded)
+  const size_t bytes = (2 * static_cast<size_t>(n) + 4 * mlpk::kPeerMaxRanks) * sizeof(float);
+  void* p = nullptr;
+  int rc = cuda_status(cudaMalloc(&p, bytes));
+  if (rc) return rc;
+  if ((rc = cuda_status(cudaMemset(p, 0, bytes))) ||
+      (rc = cuda_status(cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle_out), p)))) {
+    cudaFree(p);
+    return rc;
+  }
+  *buf_out = p;
+  return MLPK_OK;
+}
+
+int mlpk_peer_open(const void* handle, void** buf_out) {
+  if (!handle || !buf_out) return MLPK_ERR_NULL;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(buf_out, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int mlpk_peer_close(void* peer_buf) {
+  if (!peer_buf) return MLPK_ERR_NULL;
+  return cuda_status(cudaIpcCloseMemHandle(peer_buf));
+}
+
+int mlpk_peer_free(void* buf) {
+  if (!buf) return MLPK_ERR_NULL;
+  return cuda_status(cudaFree(buf));
+}
+
+float* mlpk_peer_slot(void* buf, int64_t n, uint32_t epoch) {
+  return buf ? static_cast<float*>(buf) + static_cast<size_t>(epoch & 1u) * n : nullptr;
+}
+
+int mlpk_peer_allreduce(void* const* bufs, int world, int rank, int64_t n, uint32_t epoch, float* dW_out,
+                        mlpk_stream_t stream) {
+  if (!bufs || !dW_out) return MLPK_ERR_NULL;
+  if (world < 1 || world > mlpk::kPeerMaxRanks || rank < 0 || rank >= world) return MLPK_ERR_SHAPE;
+  if (n <= 0 || n % 4 != 0 || n > (int64_t(1) << 30)) return MLPK_ERR_SHAPE;
+  if (!aligned16(dW_out)) return MLPK_ERR_ALIGN;
+  mlpk::PeerPtrs peers;
+  std::memset(&peers, 0, sizeof(peers));
+  for (int q = 0; q < world; ++q) {
+    if (!bufs[q]) return MLPK_ERR_NULL;
+    peers.buf[q] = static_cast<float*>(bufs[q]);
+  }
+  DevInfo di;
+  int rc = current_device_info(&di, nullptr);
+  if (rc != MLPK_OK) return rc;
+  const int64_t blocks = (n / 4 + 255) / 256;
+  const int grid = static_cast<int>(blocks < di.sm_count ? blocks : di.sm_count);
+  return launch_kernel(mlpk::mlp_peer_allreduce_kernel, grid, 256, 0, static_cast<cudaStream_t>(stream),
+                       peers, world, rank, static_cast<int>(n), epoch, dW_out);
 }
 
 const char* mlpk_last_cuda_error(void) {

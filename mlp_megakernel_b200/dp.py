@@ -12,8 +12,18 @@ The split of a global batch follows the reference's benchmark recipe: rank r
 of W takes rows ``[r*M/W, (r+1)*M/W)`` (integer division spreads a remainder
 over the ranks).  ``torch.distributed`` supplies the process group: NCCL on the
 GPUs, gloo in the CPU tests of this host logic.
+
+The weight-gradient sum has two implementations behind ``make_grad_reducer``:
+
+* ``PeerGradReducer`` -- all ranks on one node (up to 8): this library's own
+  kernel sums the ranks' dW over NVLink peer memory (CUDA IPC buffers, bounded
+  flag hand-off), in rank order, so every rank gets bitwise the same dW;
+* ``NcclGradReducer`` -- anything else: ``all_reduce(SUM)`` over NCCL.
 """
 from __future__ import annotations
+
+import ctypes
+import os
 
 import torch
 
@@ -45,3 +55,135 @@ def broadcast_parameters(module: torch.nn.Module, process_group=None, src: int =
 
     for p in module.parameters():
         dist.broadcast(p.data, src=src, group=process_group)
+
+
+class NcclGradReducer:
+    """dW sum over ``torch.distributed`` (NCCL across nodes)."""
+
+    def __init__(self, n: int, process_group=None):
+        self.n = n
+        self.process_group = process_group
+
+    def local_buffer(self, like: torch.Tensor) -> torch.Tensor:
+        """Where the backward writes this rank's dW (here: the output itself)."""
+        return like
+
+    def reduce(self, local: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        if local.data_ptr() != out.data_ptr():
+            out.copy_(local)
+        return allreduce_weight_grads(out, self.process_group)
+
+    def close(self):
+        pass
+
+
+class _DevicePtr:
+    """A raw device pointer seen by torch as a float32 tensor (no copy)."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerGradReducer:
+    """Deterministic dW sum over NVLink peer memory for the ranks of one node.
+
+    Set-up (collective): every rank allocates a peer buffer through the C ABI
+    (``mlpk_peer_alloc``), the IPC handles are exchanged with
+    ``all_gather_object`` and every rank opens the others' buffers.  Per step:
+    the backward writes this rank's dW into ``local_buffer()`` (the slot of the
+    next epoch) and ``reduce()`` launches ``mlpk_peer_allreduce``, which sums
+    the ranks' slots in rank order on the current stream.  Every rank must run
+    the same steps in the same order.
+    """
+
+    def __init__(self, n: int, process_group=None):
+        import torch.distributed as dist
+
+        from . import _lib
+
+        if n % 4:
+            raise ValueError("the gradient length must be a multiple of 4")
+        self.n = n
+        self.world = dist.get_world_size(process_group)
+        self.rank = dist.get_rank(process_group)
+        if self.world > _lib.PEER_MAX_RANKS:
+            raise ValueError(f"peer-memory reduction serves at most {_lib.PEER_MAX_RANKS} ranks")
+        self._lib = _lib.lib()
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * _lib.PEER_HANDLE_BYTES)()
+        _lib.check("mlpk_peer_alloc", self._lib.mlpk_peer_alloc(n, ctypes.byref(own), handle))
+        self._own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=process_group)
+        self._opened = []
+        ptrs = []
+        for q, h in enumerate(handles):
+            if q == self.rank:
+                ptrs.append(self._own)
+                continue
+            p = ctypes.c_void_p()
+            hb = (ctypes.c_uint8 * _lib.PEER_HANDLE_BYTES).from_buffer_copy(h)
+            _lib.check("mlpk_peer_open", self._lib.mlpk_peer_open(hb, ctypes.byref(p)))
+            self._opened.append(p.value)
+            ptrs.append(p.value)
+        self._ptrs = _lib.ptr_array(ptrs)
+        self.epoch = 0
+        # every rank has opened every buffer before the first step
+        dist.barrier(group=process_group)
+
+    def local_buffer(self, like: torch.Tensor = None) -> torch.Tensor:
+        """This rank's slot for the next step (the backward writes dW here)."""
+        ptr = self._lib.mlpk_peer_slot(self._own, self.n, self.epoch + 1)
+        dev = like.device if like is not None else torch.device("cuda", torch.cuda.current_device())
+        return torch.as_tensor(_DevicePtr(ptr, self.n), device=dev)
+
+    def reduce(self, local: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        from . import _lib
+
+        self.epoch += 1
+        expect = self._lib.mlpk_peer_slot(self._own, self.n, self.epoch)
+        if local.data_ptr() != expect:
+            raise RuntimeError("local dW is not in this step's peer slot (call local_buffer() first)")
+        if out.dtype != torch.float32 or not out.is_contiguous() or out.numel() != self.n:
+            raise ValueError("output must be a contiguous fp32 buffer of the gradient length")
+        _lib.check("mlpk_peer_allreduce",
+                   self._lib.mlpk_peer_allreduce(self._ptrs, self.world, self.rank, self.n, self.epoch,
+                                                 out.data_ptr(), torch.cuda.current_stream(out.device).cuda_stream))
+        return out
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's.  Safe once this rank's
+        last reduction has completed: that kernel returns only after every rank
+        finished reading and writing this rank's buffer."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        for p in self._opened:
+            self._lib.mlpk_peer_close(ctypes.c_void_p(p))
+        self._opened = []
+        self._lib.mlpk_peer_free(ctypes.c_void_p(self._own))
+        self._own = None
+
+
+def single_node(process_group=None) -> bool:
+    """True when every rank of the group runs on this node (torchrun's
+    LOCAL_WORLD_SIZE equals the group size)."""
+    import torch.distributed as dist
+
+    local = int(os.environ.get("LOCAL_WORLD_SIZE", "-1"))
+    return local == dist.get_world_size(process_group)
+
+
+def make_grad_reducer(n: int, process_group=None, kind: str = "auto"):
+    """The dW reducer for ``process_group``: peer memory on one node (up to 8
+    ranks), NCCL otherwise.  ``kind`` = "auto", "peer" or "nccl"."""
+    import torch.distributed as dist
+
+    if kind not in ("auto", "peer", "nccl"):
+        raise ValueError(f"unknown reducer kind {kind!r}")
+    if kind == "peer" or (kind == "auto" and dist.get_backend(process_group) == "nccl"
+                          and single_node(process_group) and dist.get_world_size(process_group) <= 8
+                          and n % 4 == 0):
+        return PeerGradReducer(n, process_group)
+    return NcclGradReducer(n, process_group)

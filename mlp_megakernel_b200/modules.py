@@ -19,9 +19,11 @@ from mlp_fused.md:52-172 and mlp_fused.md:461-486, and is restated here:
 
 ``num_layers`` selects the depth (3 or 5 in the reference; README.md:9); all
 hidden layers have width H.  Data-parallel training: pass a
-``torch.distributed`` process group and the fp32 weight gradients are
-all-reduced (sum) on the current stream between the backward kernel and the
-weight-norm backward (so every rank applies the same update).
+``torch.distributed`` process group and the fp32 weight gradients are summed
+over the ranks on the current stream between the backward kernel and the
+weight-norm backward (so every rank applies the same update): on one node by
+this library's NVLink peer-memory kernel, otherwise by NCCL (``grad_reduce``
+= "auto", "peer" or "nccl"; see dp.make_grad_reducer).
 """
 from __future__ import annotations
 
@@ -32,7 +34,7 @@ import torch
 import torch.nn as nn
 
 from . import _lib
-from .dp import allreduce_weight_grads
+from .dp import make_grad_reducer
 from .functional import _aligned
 
 
@@ -60,8 +62,26 @@ def _train_forward(x: torch.Tensor, ws, dims):
     return out, hs
 
 
-def _backward(x, ws, hs, grad_out, dims, process_group=None):
-    """Launch mlpk_bwd: returns (dx fp16, dW_flat fp32)."""
+class _GradSum:
+    """Data-parallel weight-gradient sum of one module: the reducer is made on
+    the first backward (a collective set-up on every rank of the group)."""
+
+    def __init__(self, process_group, kind: str = "auto"):
+        self.process_group = process_group
+        self.kind = kind
+        self._reducer = None
+
+    def reducer(self, n: int):
+        if self._reducer is None or self._reducer.n != n:
+            if self._reducer is not None:
+                self._reducer.close()
+            self._reducer = make_grad_reducer(n, self.process_group, self.kind)
+        return self._reducer
+
+
+def _backward(x, ws, hs, grad_out, dims, grad_sum: _GradSum = None):
+    """Launch mlpk_bwd: returns (dx fp16, dW_flat fp32), dW summed over the
+    ranks when ``grad_sum`` is given."""
     M = x.shape[0]
     lib = _lib.lib()
     shape = _lib.shape_struct(dims)
@@ -69,6 +89,8 @@ def _backward(x, ws, hs, grad_out, dims, process_group=None):
     dx = torch.empty_like(x)
     nflat = sum(a * b for a, b in zip(dims[:-1], dims[1:]))
     dw = torch.empty(nflat, device=x.device, dtype=torch.float32)
+    red = grad_sum.reducer(nflat) if grad_sum is not None else None
+    local = red.local_buffer(dw) if red is not None else dw
     wsb = lib.mlpk_bwd_workspace_size(ctypes.byref(shape), M)
     if wsb < 0:
         raise _lib.MlpkError("mlpk_bwd_workspace_size", 2)
@@ -76,10 +98,10 @@ def _backward(x, ws, hs, grad_out, dims, process_group=None):
     rc = lib.mlpk_bwd(ctypes.byref(shape), M, x.data_ptr(),
                       _lib.ptr_array([w.data_ptr() for w in ws]),
                       _lib.ptr_array([h.data_ptr() for h in hs]), g.data_ptr(), dx.data_ptr(),
-                      work.data_ptr(), int(work.numel()), dw.data_ptr(), _stream(x.device))
+                      work.data_ptr(), int(work.numel()), local.data_ptr(), _stream(x.device))
     _lib.check("mlpk_bwd", rc)
-    if process_group is not None:
-        allreduce_weight_grads(dw, process_group)
+    if red is not None:
+        red.reduce(local, dw)
     return dx, dw
 
 
@@ -102,12 +124,12 @@ def _check_input(x: torch.Tensor, d0: int) -> torch.Tensor:
 class _FusedMLPFn(torch.autograd.Function):
     @staticmethod
     @torch.amp.custom_fwd(device_type="cuda", cast_inputs=torch.float16)
-    def forward(ctx, x, dims, process_group, *weights):
+    def forward(ctx, x, dims, grad_sum, *weights):
         x = _check_input(x, dims[0])
         ws = [_aligned(w.to(torch.float16)) for w in weights]
         out, hs = _train_forward(x, ws, dims)
         ctx.dims = dims
-        ctx.process_group = process_group
+        ctx.grad_sum = grad_sum
         ctx.w_dtypes = [w.dtype for w in weights]
         ctx.save_for_backward(x, *ws, *hs)
         return out
@@ -119,7 +141,7 @@ class _FusedMLPFn(torch.autograd.Function):
         L = len(dims) - 1
         saved = ctx.saved_tensors
         x, ws, hs = saved[0], list(saved[1:1 + L]), list(saved[1 + L:])
-        dx, dw = _backward(x, ws, hs, grad_out, dims, ctx.process_group)
+        dx, dw = _backward(x, ws, hs, grad_out, dims, ctx.grad_sum)
         dws = [d.to(t) for d, t in zip(_split_flat(dw, dims), ctx.w_dtypes)]
         return (dx if ctx.needs_input_grad[0] else None, None, None, *dws)
 
@@ -127,7 +149,7 @@ class _FusedMLPFn(torch.autograd.Function):
 class _FusedMLPWNFn(torch.autograd.Function):
     @staticmethod
     @torch.amp.custom_fwd(device_type="cuda", cast_inputs=torch.float16)
-    def forward(ctx, x, dims, process_group, v_all, g_all):
+    def forward(ctx, x, dims, grad_sum, v_all, g_all):
         x = _check_input(x, dims[0])
         lib = _lib.lib()
         shape = _lib.shape_struct(dims)
@@ -142,7 +164,7 @@ class _FusedMLPWNFn(torch.autograd.Function):
         _lib.check("mlpk_wn_fwd", rc)
         out, hs = _train_forward(x, ws, dims)
         ctx.dims = dims
-        ctx.process_group = process_group
+        ctx.grad_sum = grad_sum
         ctx.dtypes = (v_all.dtype, g_all.dtype)
         ctx.save_for_backward(x, v32, g32, inv, *ws, *hs)
         return out
@@ -155,7 +177,7 @@ class _FusedMLPWNFn(torch.autograd.Function):
         saved = ctx.saved_tensors
         x, v32, g32, inv = saved[:4]
         ws, hs = list(saved[4:4 + L]), list(saved[4 + L:])
-        dx, dw = _backward(x, ws, hs, grad_out, dims, ctx.process_group)
+        dx, dw = _backward(x, ws, hs, grad_out, dims, ctx.grad_sum)
         dv = torch.empty_like(v32)
         dg = torch.empty_like(g32)
         lib = _lib.lib()
@@ -175,10 +197,11 @@ class FusedMLPSoftplus(nn.Module):
     """
 
     def __init__(self, D: int = 128, H: int = 128, out_features: int = 128, num_layers: int = 3,
-                 process_group=None):
+                 process_group=None, grad_reduce: str = "auto"):
         super().__init__()
         self.dims = _dims(D, H, out_features, num_layers)
         self.process_group = process_group
+        self._grad_sum = _GradSum(process_group, grad_reduce) if process_group is not None else None
         for i, (a, b) in enumerate(zip(self.dims[:-1], self.dims[1:])):
             w = torch.empty(a, b)
             nn.init.uniform_(w, -1.0 / math.sqrt(a), 1.0 / math.sqrt(a))
@@ -189,7 +212,7 @@ class FusedMLPSoftplus(nn.Module):
         return [getattr(self, f"w{i + 1}") for i in range(len(self.dims) - 1)]
 
     def forward(self, x):
-        return _FusedMLPFn.apply(x, self.dims, self.process_group, *self.weights)
+        return _FusedMLPFn.apply(x, self.dims, self._grad_sum, *self.weights)
 
 
 class FusedMLPSoftplusWN(nn.Module):
@@ -202,10 +225,11 @@ class FusedMLPSoftplusWN(nn.Module):
     """
 
     def __init__(self, D: int = 128, H: int = 128, out_features: int = 128, num_layers: int = 3,
-                 process_group=None):
+                 process_group=None, grad_reduce: str = "auto"):
         super().__init__()
         self.dims = _dims(D, H, out_features, num_layers)
         self.process_group = process_group
+        self._grad_sum = _GradSum(process_group, grad_reduce) if process_group is not None else None
         vs, gs = [], []
         for a, b in zip(self.dims[:-1], self.dims[1:]):
             v = torch.empty(a, b)
@@ -236,4 +260,4 @@ class FusedMLPSoftplusWN(nn.Module):
             self.g(l).copy_(w.float().norm(dim=0))
 
     def forward(self, x):
-        return _FusedMLPWNFn.apply(x, self.dims, self.process_group, self.v_all, self.g_all)
+        return _FusedMLPWNFn.apply(x, self.dims, self._grad_sum, self.v_all, self.g_all)
