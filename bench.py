@@ -61,6 +61,7 @@ def parse_args():
                     help="global rows of the wide (256) training step (split over the GPUs)")
     ap.add_argument("--train-steps", type=int, default=50)
     ap.add_argument("--no-train", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="time training steps as eager launches")
     return ap.parse_args()
 
 
@@ -452,6 +453,7 @@ def run_training(args, world, rank, dist, barrier, name, rows):
             w.copy_(w0)
 
     def step():
+        st = torch.cuda.current_stream().cuda_stream  # the capture stream inside a graph capture
         if wn:
             _lib.check("wn_fwd", lib.mlpk_wn_fwd(shape, v_all.data_ptr(), g_all.data_ptr(), Wp,
                                                  inv.data_ptr(), st))
@@ -468,12 +470,27 @@ def run_training(args, world, rank, dist, barrier, name, rows):
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
+    # the timed steps replay the whole step (all kernels, and the dW sum across
+    # ranks) as one CUDA graph: no host launch gaps between the kernels
+    run = step
+    if not args.no_graph:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        run = graph.replay
+        run()
+        torch.cuda.synchronize()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.train_steps):
-        step()
+        run()
     e1.record()
     torch.cuda.synchronize()
     barrier()
@@ -545,6 +562,7 @@ def run_training(args, world, rank, dist, barrier, name, rows):
                    "dims": list(dims), "rows_per_gpu": M, "global_rows": world * M,
                    "parallelism": f"dp{world}" + ((" (fp32 dW summed by the NVLink peer-memory kernel)" if peer
                                                    else " (NCCL all-reduce of fp32 dW)") if world > 1 else ""),
+                   "launch": "eager" if args.no_graph else "CUDA graph of the whole step",
                    "l2": "per-step inputs and saved activations larger than L2"
                          if M * dims[1] * 2 * (len(dims) - 2) > 126e6 else
                          "working set partly L2-resident (no flush between steps)"},

@@ -128,22 +128,23 @@ int mlpk_device_status(int clear, int* status_out);
  * over NVLink"); the reference itself calls NCCL through torch.distributed.
  * Each rank allocates one peer buffer for n floats (n a multiple of 4), shares
  * its IPC handle (MLPK_PEER_HANDLE_BYTES bytes) with the other ranks and opens
- * theirs.  Per step with epoch = 1, 2, ...: the backward writes this rank's dW
- * into mlpk_peer_slot(own buffer, n, epoch), then mlpk_peer_allreduce sums
- * every rank's slot in rank order into dW_out (bitwise identical on all
- * ranks).  Every rank must call it once per epoch, in the same order.  If a
- * peer does not arrive within the bounded wait (1 s), the kernel sets bit 16
- * (cross-GPU flag timeout) of the device status word (mlpk_device_status) and
- * leaves dW_out unwritten.  At most 8 ranks; mlpk_peer_alloc and
- * mlpk_peer_open allocate / map device memory (set-up calls, not per step). */
+ * theirs.  Per step: the backward writes this rank's dW into its own buffer
+ * (the first n floats), then mlpk_peer_allreduce sums every rank's dW in rank
+ * order into dW_out (bitwise identical on all ranks).  Every rank must call it
+ * once per step, in the same order; the step count lives in device memory, so
+ * the call can be captured in a CUDA graph.  When it returns (on the stream),
+ * every rank has finished reading this rank's buffer.  If a peer does not
+ * arrive within the bounded wait (1 s), the kernel sets bit 16 (cross-GPU flag
+ * timeout) of the device status word (mlpk_device_status).  At most 8 ranks;
+ * mlpk_peer_alloc and mlpk_peer_open allocate / map device memory (set-up
+ * calls, not per step). */
 #define MLPK_PEER_HANDLE_BYTES 64
 #define MLPK_PEER_MAX_RANKS 8
 int mlpk_peer_alloc(int64_t n, void** buf_out, void* handle_out);
 int mlpk_peer_open(const void* handle, void** buf_out);
 int mlpk_peer_close(void* peer_buf);
 int mlpk_peer_free(void* buf);
-float* mlpk_peer_slot(void* buf, int64_t n, uint32_t epoch);
-int mlpk_peer_allreduce(void* const* bufs, int world, int rank, int64_t n, uint32_t epoch, float* dW_out,
+int mlpk_peer_allreduce(void* const* bufs, int world, int rank, int64_t n, float* dW_out,
                         mlpk_stream_t stream);
 
 /* Text of the CUDA runtime / driver failure behind the calling thread's most

@@ -58,9 +58,7 @@ SIGNATURES = {
     "mlpk_peer_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
     "mlpk_peer_close": (ctypes.c_int, [ctypes.c_void_p]),
     "mlpk_peer_free": (ctypes.c_int, [ctypes.c_void_p]),
-    "mlpk_peer_slot": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_uint32]),
-    "mlpk_peer_allreduce": (ctypes.c_int, [_VPP, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_uint32,
-                                           _vp, _vp]),
+    "mlpk_peer_allreduce": (ctypes.c_int, [_VPP, ctypes.c_int, ctypes.c_int, ctypes.c_int64, _vp, _vp]),
 }
 PEER_HANDLE_BYTES = 64
 PEER_MAX_RANKS = 8

@@ -562,9 +562,19 @@ __global__ void __launch_bounds__(kReduceElems * kReduceSlices)
   const int le = threadIdx.x % kReduceElems, sl = threadIdx.x / kReduceElems;
   const int e = blockIdx.x * kReduceElems + le;
   float acc = 0.0f;
-  if (e < nfloats)
-    for (int p = sl; p < nparts; p += kReduceSlices)
-      acc += partials[static_cast<size_t>(p) * nfloats + e];
+  if (e < nfloats) {
+    // 8 loads in flight, added in increasing p (the fixed order)
+    constexpr int U = 8;
+    int p = sl;
+    for (; p + (U - 1) * kReduceSlices < nparts; p += U * kReduceSlices) {
+      float v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = partials[static_cast<size_t>(p + u * kReduceSlices) * nfloats + e];
+#pragma unroll
+      for (int u = 0; u < U; ++u) acc += v[u];
+    }
+    for (; p < nparts; p += kReduceSlices) acc += partials[static_cast<size_t>(p) * nfloats + e];
+  }
   red[sl][le] = acc;
   __syncthreads();
   if (sl == 0 && e < nfloats) {

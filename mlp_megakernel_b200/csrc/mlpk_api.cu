@@ -709,8 +709,8 @@ int mlpk_peer_alloc(int64_t n, void** buf_out, void* handle_out) {
   if (!buf_out || !handle_out) return MLPK_ERR_NULL;
   if (n <= 0 || n % 4 != 0) return MLPK_ERR_SHAPE;
   static_assert(sizeof(cudaIpcMemHandle_t) == MLPK_PEER_HANDLE_BYTES, "IPC handle size");
-  // two slots of n floats, then ready[8], done[8], count (32-bit words, padded)
-  const size_t bytes = (2 * static_cast<size_t>(n) + 4 * mlpk::kPeerMaxRanks) * sizeof(float);
+  // the slot of n floats, then ready[8], done[8], count, epoch (32-bit words, padded)
+  const size_t bytes = (static_cast<size_t>(n) + 4 * mlpk::kPeerMaxRanks) * sizeof(float);
   void* p = nullptr;
   int rc = cuda_status(cudaMalloc(&p, bytes));
   if (rc) return rc;
@@ -740,11 +740,7 @@ int mlpk_peer_free(void* buf) {
   return cuda_status(cudaFree(buf));
 }
 
-float* mlpk_peer_slot(void* buf, int64_t n, uint32_t epoch) {
-  return buf ? static_cast<float*>(buf) + static_cast<size_t>(epoch & 1u) * n : nullptr;
-}
-
-int mlpk_peer_allreduce(void* const* bufs, int world, int rank, int64_t n, uint32_t epoch, float* dW_out,
+int mlpk_peer_allreduce(void* const* bufs, int world, int rank, int64_t n, float* dW_out,
                         mlpk_stream_t stream) {
   if (!bufs || !dW_out) return MLPK_ERR_NULL;
   if (world < 1 || world > mlpk::kPeerMaxRanks || rank < 0 || rank >= world) return MLPK_ERR_SHAPE;
@@ -762,7 +758,7 @@ int mlpk_peer_allreduce(void* const* bufs, int world, int rank, int64_t n, uint3
   const int64_t blocks = (n / 4 + 255) / 256;
   const int grid = static_cast<int>(blocks < di.sm_count ? blocks : di.sm_count);
   return launch_kernel(mlpk::mlp_peer_allreduce_kernel, grid, 256, 0, static_cast<cudaStream_t>(stream),
-                       peers, world, rank, static_cast<int>(n), epoch, dW_out);
+                       peers, world, rank, static_cast<int>(n), dW_out);
 }
 
 const char* mlpk_last_cuda_error(void) {

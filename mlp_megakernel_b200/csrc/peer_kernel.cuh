@@ -3,29 +3,27 @@
 // reference's DP recipe, done without NCCL).
 //
 // Every rank owns one exported ("peer") buffer of
-//   [slot 0: n floats][slot 1: n floats][ready[8]][done[8]][count] (uint32 words)
-// opened by every other rank through CUDA IPC.  In step `epoch` (1, 2, ...):
-//   1. the backward's reduction writes this rank's dW into its own slot
-//      (epoch & 1);
-//   2. mlp_peer_allreduce_kernel: thread 0 of CTA 0 stores `epoch` into
+//   [slot: n floats][ready[8]][done[8]][count][epoch] (uint32 words)
+// opened by every other rank through CUDA IPC.  In each step:
+//   1. the backward's reduction writes this rank's dW into its slot;
+//   2. mlp_peer_allreduce_kernel: every CTA reads the step number
+//      e = epoch + 1 from its own buffer; thread 0 of CTA 0 stores e into
 //      ready[rank] of every rank's buffer (release, system scope); every CTA
-//      waits until its own buffer's ready[q] >= epoch for all q (acquire,
-//      bounded), then its threads sum slot (epoch & 1) of ranks 0 .. W-1 in
-//      rank order and write the result.  Every rank adds the same values in
-//      the same order, so the sum is bitwise identical on all ranks (NCCL's
-//      ring / tree orders do not promise that).
+//      waits until its own ready[q] >= e for all q (acquire, bounded), then its
+//      threads sum the slots of ranks 0 .. W-1 in rank order and write the
+//      result.  Every rank adds the same values in the same order, so the sum
+//      is bitwise identical on all ranks (NCCL's ring / tree orders do not
+//      promise that);
 //   3. completion: every CTA counts itself done in `count`; CTA 0 then stores
-//      `epoch` into done[rank] of every rank's buffer and waits for its own
-//      done[q] >= epoch.  So when the kernel returns on any rank, no rank reads
-//      or writes that rank's buffer again in this step: a rank may free its
-//      buffer or exit right after its last step.
-// Slots alternate by epoch parity: a rank can write its slot for epoch e only
-// after its step e-1 returned, i.e. after every rank finished reading epoch
-// e-1 -- and, one step earlier, epoch e-2 (the same slot).
-//
-// Plain peer loads and stores only (no multicast objects, no TMA).  Every wait
-// is bounded: on expiry the kernel records kDevTimeoutFlag in the device
-// status word and returns (without writing the result if the data never
+//      e into done[rank] of every rank's buffer, waits for its own done[q] >= e
+//      and finally sets epoch = e.  So when the kernel returns on a rank, every
+//      rank has finished reading that rank's slot (it may be rewritten by the
+//      next backward, freed, or the process may exit) and no rank will write
+//      into that rank's buffer again in this step.
+// The step number lives in device memory, so the kernel can be replayed from
+// a CUDA graph.  Plain peer loads and stores only (no multicast objects, no
+// TMA).  Every wait is bounded: on expiry the kernel records kDevTimeoutFlag in
+// the device status word and returns (without the result if the data never
 // became ready).
 #pragma once
 #include "ptx.cuh"
@@ -62,30 +60,34 @@ __device__ __forceinline__ bool peer_wait_all(const uint32_t* flags, int world, 
 }
 
 __global__ void __launch_bounds__(256)
-    mlp_peer_allreduce_kernel(PeerPtrs peers, int world, int rank, int n, uint32_t epoch,
-                              float* __restrict__ out) {
-  const size_t slot_off = static_cast<size_t>(epoch & 1u) * n;
-  auto words = [&](int q) { return reinterpret_cast<uint32_t*>(peers.buf[q] + 2 * static_cast<size_t>(n)); };
+    mlp_peer_allreduce_kernel(PeerPtrs peers, int world, int rank, int n, float* __restrict__ out) {
+  auto words = [&](int q) { return reinterpret_cast<uint32_t*>(peers.buf[q] + static_cast<size_t>(n)); };
   uint32_t* const ready = words(rank);                  // ready[kPeerMaxRanks]
   uint32_t* const done = ready + kPeerMaxRanks;         // done[kPeerMaxRanks]
   uint32_t* const count = ready + 2 * kPeerMaxRanks;    // CTAs finished, all steps
+  uint32_t* const epoch_word = count + 1;               // steps completed
   __shared__ int s_ok;
+  __shared__ uint32_t s_epoch;
   if (threadIdx.x == 0) {
+    // epoch only changes at the very end of CTA 0, after every CTA counted itself
+    const uint32_t e = *reinterpret_cast<volatile uint32_t*>(epoch_word) + 1u;
+    s_epoch = e;
     if (blockIdx.x == 0) {
       // this rank's slot was completed by the previous kernel on this stream
       asm volatile("fence.acq_rel.sys;" ::: "memory");
-      for (int q = 0; q < world; ++q) st_release_sys(words(q) + rank, epoch);
+      for (int q = 0; q < world; ++q) st_release_sys(words(q) + rank, e);
     }
-    s_ok = peer_wait_all(ready, world, epoch) ? 1 : 0;
+    s_ok = peer_wait_all(ready, world, e) ? 1 : 0;
   }
   __syncthreads();
+  const uint32_t e = s_epoch;
   if (s_ok) {
     // n is a multiple of 4 (checked by the host); grid-stride over float4s
     // (the host keeps the grid at most one CTA per SM: every CTA is resident)
     for (int i4 = blockIdx.x * blockDim.x + threadIdx.x; 4 * i4 < n; i4 += gridDim.x * blockDim.x) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int q = 0; q < world; ++q) {  // fixed rank order: identical sums on every rank
-        const float4 v = __ldcv(reinterpret_cast<const float4*>(peers.buf[q] + slot_off) + i4);
+        const float4 v = __ldcv(reinterpret_cast<const float4*>(peers.buf[q]) + i4);
         acc.x += v.x;
         acc.y += v.y;
         acc.z += v.z;
@@ -98,24 +100,24 @@ __global__ void __launch_bounds__(256)
   if (threadIdx.x == 0) {
     __threadfence();
     atomicAdd(count, 1u);
-    if (blockIdx.x == 0 && s_ok) {
+    if (blockIdx.x == 0) {
       // every CTA of this kernel (count is cumulative over steps) ...
-      const uint32_t target = epoch * gridDim.x;
+      const uint32_t target = e * gridDim.x;
       const uint64_t t0 = globaltimer_ns();
-      bool ok = true;
-      while (static_cast<int32_t>(ld_acquire_sys(count) - target) < 0) {
+      bool ok = s_ok != 0;
+      while (ok && static_cast<int32_t>(ld_acquire_sys(count) - target) < 0) {
         if (globaltimer_ns() - t0 > MLPK_WAIT_TIMEOUT_NS) {
           atomicOr(&g_device_status, kDevTimeoutFlag);
           ok = false;
-          break;
         }
       }
       // ... then every rank is done with the others' buffers for this step
       if (ok) {
         asm volatile("fence.acq_rel.sys;" ::: "memory");
-        for (int q = 0; q < world; ++q) st_release_sys(words(q) + kPeerMaxRanks + rank, epoch);
-        peer_wait_all(done, world, epoch);
+        for (int q = 0; q < world; ++q) st_release_sys(words(q) + kPeerMaxRanks + rank, e);
+        peer_wait_all(done, world, e);
       }
+      *reinterpret_cast<volatile uint32_t*>(epoch_word) = e;
     }
   }
 }

@@ -78,11 +78,13 @@ __global__ void __launch_bounds__(kWnCols * kWnRowGroups)
   const bool valid = j < N;
   const float* v = v_all + s.voff[l];
   float ss = 0.0f;
-  if (valid)
+  if (valid) {
+#pragma unroll 4
     for (int i = r; i < K; i += kWnRowGroups) {
       const float a = v[static_cast<size_t>(i) * N + j];
       ss = fmaf(a, a, ss);
     }
+  }
   ss = wn_col_sum(ss, red, c, r);
   if (!valid) return;
   const float inv = 1.0f / sqrtf(ss);
@@ -110,11 +112,13 @@ __global__ void __launch_bounds__(kWnCols * kWnRowGroups)
   const float* dw = dw_all + s.voff[l];
   float* dv = dv_all + s.voff[l];
   float dot = 0.0f;
-  if (valid)
+  if (valid) {
+#pragma unroll 4
     for (int i = r; i < K; i += kWnRowGroups) {
       const size_t e = static_cast<size_t>(i) * N + j;
       dot = fmaf(dw[e], v[e], dot);
     }
+  }
   dot = wn_col_sum(dot, red, c, r);
   if (!valid) return;
   const float inv = inv_norm[s.goff[l] + j];

@@ -91,10 +91,11 @@ class PeerGradReducer:
     Set-up (collective): every rank allocates a peer buffer through the C ABI
     (``mlpk_peer_alloc``), the IPC handles are exchanged with
     ``all_gather_object`` and every rank opens the others' buffers.  Per step:
-    the backward writes this rank's dW into ``local_buffer()`` (the slot of the
-    next epoch) and ``reduce()`` launches ``mlpk_peer_allreduce``, which sums
-    the ranks' slots in rank order on the current stream.  Every rank must run
-    the same steps in the same order.
+    the backward writes this rank's dW into ``local_buffer()`` and
+    ``reduce()`` launches ``mlpk_peer_allreduce``, which sums the ranks' dW in
+    rank order on the current stream.  Every rank must run the same steps in
+    the same order; the step count is kept on the device, so steps may be
+    replayed from a CUDA graph.
     """
 
     def __init__(self, n: int, process_group=None):
@@ -128,28 +129,25 @@ class PeerGradReducer:
             self._opened.append(p.value)
             ptrs.append(p.value)
         self._ptrs = _lib.ptr_array(ptrs)
-        self.epoch = 0
+        self._local = torch.as_tensor(_DevicePtr(self._own, n),
+                                      device=torch.device("cuda", torch.cuda.current_device()))
         # every rank has opened every buffer before the first step
         dist.barrier(group=process_group)
 
     def local_buffer(self, like: torch.Tensor = None) -> torch.Tensor:
-        """This rank's slot for the next step (the backward writes dW here)."""
-        ptr = self._lib.mlpk_peer_slot(self._own, self.n, self.epoch + 1)
-        dev = like.device if like is not None else torch.device("cuda", torch.cuda.current_device())
-        return torch.as_tensor(_DevicePtr(ptr, self.n), device=dev)
+        """This rank's dW slot (the backward writes dW here)."""
+        return self._local
 
     def reduce(self, local: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         from . import _lib
 
-        self.epoch += 1
-        expect = self._lib.mlpk_peer_slot(self._own, self.n, self.epoch)
-        if local.data_ptr() != expect:
-            raise RuntimeError("local dW is not in this step's peer slot (call local_buffer() first)")
+        if local.data_ptr() != self._own:
+            raise RuntimeError("local dW is not in this rank's peer slot (use local_buffer())")
         if out.dtype != torch.float32 or not out.is_contiguous() or out.numel() != self.n:
             raise ValueError("output must be a contiguous fp32 buffer of the gradient length")
         _lib.check("mlpk_peer_allreduce",
-                   self._lib.mlpk_peer_allreduce(self._ptrs, self.world, self.rank, self.n, self.epoch,
-                                                 out.data_ptr(), torch.cuda.current_stream(out.device).cuda_stream))
+                   self._lib.mlpk_peer_allreduce(self._ptrs, self.world, self.rank, self.n, out.data_ptr(),
+                                                 torch.cuda.current_stream(out.device).cuda_stream))
         return out
 
     def close(self):
@@ -159,6 +157,7 @@ class PeerGradReducer:
         if self._own is None:
             return
         torch.cuda.synchronize()
+        self._local = None
         for p in self._opened:
             self._lib.mlpk_peer_close(ctypes.c_void_p(p))
         self._opened = []
