@@ -122,6 +122,14 @@ int mlpk_bwd_noalloc(const mlpk_shape* shape, int64_t M, const void* x, const vo
  * device: bit flags set by bounded waits that expired.  Synchronises. */
 int mlpk_device_status(int clear, int* status_out);
 
+/* ---- fp32 <-> fp16 casts (round to nearest even), for the fp32-input
+ * forward: the reference's kernel.py accepts fp32 x and W (kernel.py:37-43,
+ * 134-138) and stores its fp16-rounded result into an fp32 output; the
+ * library casts x and W to fp16, runs mlpk_fwd and widens the result.  n
+ * elements; pointers 16-byte aligned. */
+int mlpk_cast_f32_f16(const float* src, void* dst_f16, int64_t n, mlpk_stream_t stream);
+int mlpk_cast_f16_f32(const void* src_f16, float* dst, int64_t n, mlpk_stream_t stream);
+
 /* ---- Data-parallel weight-gradient sum over NVLink peer memory (one node).
  * Replaces the all_reduce(SUM) of the fp32 dW buffer in the reference's
  * data-parallel recipe (BASELINE: "training all-reduces the weight gradients

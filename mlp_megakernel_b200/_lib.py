@@ -54,6 +54,8 @@ SIGNATURES = {
     "mlpk_wn_bwd": (ctypes.c_int, [_SHAPE_P, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "mlpk_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "mlpk_last_cuda_error": (ctypes.c_char_p, []),
+    "mlpk_cast_f32_f16": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, _vp]),
+    "mlpk_cast_f16_f32": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, _vp]),
     "mlpk_peer_alloc": (ctypes.c_int, [ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]),
     "mlpk_peer_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
     "mlpk_peer_close": (ctypes.c_int, [ctypes.c_void_p]),

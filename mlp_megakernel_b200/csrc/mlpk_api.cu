@@ -17,6 +17,7 @@
 
 #include "../../include/mlpk.h"
 #include "bwd_kernel.cuh"
+#include "cast_kernel.cuh"
 #include "fwd2_kernel.cuh"
 #include "stream_kernel.cuh"
 #include "peer_kernel.cuh"
@@ -702,6 +703,41 @@ int mlpk_device_status(int clear, int* status_out) {
     if ((rc = cuda_status(cudaMemcpyToSymbol(mlpk::g_device_status, &z, sizeof(int))))) return rc;
   }
   return MLPK_OK;
+}
+
+// ------------------------------------------------------------------ fp32 <-> fp16 casts
+namespace {
+int cast_grid(int64_t n) {
+  DevInfo di;
+  if (current_device_info(&di, nullptr) != MLPK_OK) return 0;
+  const int64_t want = (n / 8 + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(di.sm_count) * 8;
+  return static_cast<int>(want < 1 ? 1 : want < cap ? want : cap);
+}
+}  // namespace
+
+int mlpk_cast_f32_f16(const float* src, void* dst, int64_t n, mlpk_stream_t stream) {
+  if (n < 0) return MLPK_ERR_SHAPE;
+  if (n == 0) return MLPK_OK;
+  if (!src || !dst) return MLPK_ERR_NULL;
+  if (!aligned16(src) || !aligned16(dst)) return MLPK_ERR_ALIGN;
+  DevInfo di;
+  int rc = current_device_info(&di, nullptr);
+  if (rc != MLPK_OK) return rc;
+  return launch_kernel(mlpk::mlp_cast_f32_f16_kernel, cast_grid(n), 256, 0, static_cast<cudaStream_t>(stream),
+                       src, static_cast<__half*>(dst), n);
+}
+
+int mlpk_cast_f16_f32(const void* src, float* dst, int64_t n, mlpk_stream_t stream) {
+  if (n < 0) return MLPK_ERR_SHAPE;
+  if (n == 0) return MLPK_OK;
+  if (!src || !dst) return MLPK_ERR_NULL;
+  if (!aligned16(src) || !aligned16(dst)) return MLPK_ERR_ALIGN;
+  DevInfo di;
+  int rc = current_device_info(&di, nullptr);
+  if (rc != MLPK_OK) return rc;
+  return launch_kernel(mlpk::mlp_cast_f16_f32_kernel, cast_grid(n), 256, 0, static_cast<cudaStream_t>(stream),
+                       static_cast<const __half*>(src), dst, n);
 }
 
 // ------------------------------------------------------------------ peer-memory dW sum

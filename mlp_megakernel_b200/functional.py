@@ -10,8 +10,13 @@ Mirrors the reference's functional surface:
 * ``ModelNew`` -- the nn.Module shim of kernel.py:174-180.
 
 Every call runs the sm_100a kernel in libmlpk through its C ABI on the current
-CUDA stream.  There is no CPU or PyTorch fallback: CPU tensors, unsupported
-dtypes or shapes raise.
+CUDA stream.  x and the weights are fp16, or fp32 as the reference also
+accepts (kernel.py:37-43, 134-138): fp32 operands are rounded to fp16 by the
+library's cast kernel, the fused fp16 kernel runs, and its fp16-rounded result
+is widened into the fp32 output -- the reference's own rounding points for the
+hidden activations (kernel.py:110, 117) and the output (kernel.py:121-124).
+There is no CPU or PyTorch fallback: CPU tensors, other dtypes or unsupported
+shapes raise.
 """
 from __future__ import annotations
 
@@ -35,8 +40,9 @@ def _check_operands(x: torch.Tensor, weights) -> list:
         raise ValueError("x must be a 2-D tensor [M, in_features]")
     if not x.is_cuda:
         raise RuntimeError("fused MLP runs on CUDA (sm_100) only; got a CPU tensor")
-    if x.dtype != torch.float16:
-        raise TypeError(f"fused MLP computes in fp16 (fp32 accumulate); got x.dtype={x.dtype}")
+    if x.dtype not in (torch.float16, torch.float32):
+        raise TypeError(f"fused MLP takes fp16 or fp32 inputs (fp16 operands, fp32 accumulate); "
+                        f"got x.dtype={x.dtype}")
     if len(weights) < 1:
         raise ValueError("need at least one weight matrix")
     dims = [x.shape[1]]
@@ -52,6 +58,7 @@ def _check_operands(x: torch.Tensor, weights) -> list:
     return dims
 
 
+@torch.compiler.disable  # launches through ctypes: opaque to torch.compile (runs at a graph break)
 def fused_mlp_fwd(x: torch.Tensor, *weights: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
     """``softplus(...softplus(x @ W_0)...) @ W_{L-1}`` in one kernel launch.
 
@@ -75,12 +82,31 @@ def fused_mlp_fwd(x: torch.Tensor, *weights: torch.Tensor, out: torch.Tensor = N
         return out
     lib = _lib.lib()
     shape = _lib.shape_struct(dims)
-    wptr = _lib.ptr_array([w.data_ptr() for w in ws])
     with torch.cuda.device(x.device):
         stream = torch.cuda.current_stream(x.device).cuda_stream
+        if x.dtype == torch.float32:
+            if not lib.mlpk_shape_supported(ctypes.byref(shape)):
+                _lib.check("mlpk_fwd", 2)
+            x16 = _cast(lib, x, torch.float16, stream)
+            ws = [_cast(lib, w, torch.float16, stream) for w in ws]
+            out16 = torch.empty((M, dims[-1]), device=x.device, dtype=torch.float16)
+            wptr = _lib.ptr_array([w.data_ptr() for w in ws])
+            _lib.check("mlpk_fwd", lib.mlpk_fwd(ctypes.byref(shape), M, x16.data_ptr(), wptr, out16.data_ptr(),
+                                                stream))
+            _lib.check("mlpk_cast_f16_f32", lib.mlpk_cast_f16_f32(out16.data_ptr(), out.data_ptr(),
+                                                                  out.numel(), stream))
+            return out
+        wptr = _lib.ptr_array([w.data_ptr() for w in ws])
         rc = lib.mlpk_fwd(ctypes.byref(shape), M, x.data_ptr(), wptr, out.data_ptr(), stream)
     _lib.check("mlpk_fwd", rc)
     return out
+
+
+def _cast(lib, t: torch.Tensor, dtype, stream) -> torch.Tensor:
+    """fp32 -> fp16 copy of a contiguous tensor with the library's cast kernel."""
+    dst = torch.empty(t.shape, device=t.device, dtype=dtype)
+    _lib.check("mlpk_cast_f32_f16", lib.mlpk_cast_f32_f16(t.data_ptr(), dst.data_ptr(), t.numel(), stream))
+    return dst
 
 
 def _fused_mlp_fwd(x, w1, w2, w3):

@@ -189,6 +189,19 @@ class _FusedMLPWNFn(torch.autograd.Function):
                 dv.to(ctx.dtypes[0]), dg.to(ctx.dtypes[1]))
 
 
+# The autograd Functions launch kernels through ctypes: torch.compile must not
+# trace into them.  Marked opaque, they run eagerly at a graph break and their
+# backward is recorded by autograd as usual.
+@torch.compiler.disable
+def _apply_fused(x, dims, grad_sum, *weights):
+    return _FusedMLPFn.apply(x, dims, grad_sum, *weights)
+
+
+@torch.compiler.disable
+def _apply_fused_wn(x, dims, grad_sum, v_all, g_all):
+    return _FusedMLPWNFn.apply(x, dims, grad_sum, v_all, g_all)
+
+
 class FusedMLPSoftplus(nn.Module):
     """``softplus(...softplus(x @ W_1)...) @ W_L`` with fused training kernels.
 
@@ -212,7 +225,7 @@ class FusedMLPSoftplus(nn.Module):
         return [getattr(self, f"w{i + 1}") for i in range(len(self.dims) - 1)]
 
     def forward(self, x):
-        return _FusedMLPFn.apply(x, self.dims, self._grad_sum, *self.weights)
+        return _apply_fused(x, self.dims, self._grad_sum, *self.weights)
 
 
 class FusedMLPSoftplusWN(nn.Module):
@@ -260,4 +273,4 @@ class FusedMLPSoftplusWN(nn.Module):
             self.g(l).copy_(w.float().norm(dim=0))
 
     def forward(self, x):
-        return _FusedMLPWNFn.apply(x, self.dims, self._grad_sum, self.v_all, self.g_all)
+        return _apply_fused_wn(x, self.dims, self._grad_sum, self.v_all, self.g_all)

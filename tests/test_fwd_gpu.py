@@ -189,10 +189,36 @@ def test_fwd_errors_are_loud():
     with pytest.raises(RuntimeError):
         fused_mlp_fwd(x, *ws)  # CPU tensors: no fallback
     with pytest.raises(TypeError):
-        fused_mlp_fwd(x.float().cuda(), *[w.float().cuda() for w in ws])
+        fused_mlp_fwd(x.double().cuda(), *[w.double().cuda() for w in ws])
+    with pytest.raises(ValueError):  # fp32 x with fp16 weights: dtypes must agree
+        fused_mlp_fwd(x.float().cuda(), *[w.cuda() for w in ws])
     with pytest.raises(ValueError):
         fused_mlp_fwd(x.cuda(), ws[0].cuda(), ws[1][:64].cuda(), ws[2].cuda())
     bad = [torch.zeros(128, 96, dtype=torch.float16, device="cuda"),
            torch.zeros(96, 128, dtype=torch.float16, device="cuda")]
     with pytest.raises(_lib.MlpkError):
         fused_mlp_fwd(x.cuda(), *bad)
+
+
+@pytest.mark.parametrize("config,M", [("3L128", 4096), ("3L128", 300), ("5L", 5000)])
+def test_fwd_fp32_inputs(config, M):
+    """fp32 x and W (the reference accepts them, kernel.py:134-138): the result
+    is fp32, equals the fp16 path on the fp16-rounded operands exactly, and
+    matches the oracle on the fp32 operands."""
+    x, ws = make_inputs(config, M)
+    x32 = (x.float() + 1e-4 * torch.randn(x.shape, generator=torch.Generator().manual_seed(3))).cuda()
+    w32 = [(w.float() * 1.0003).cuda() for w in ws]
+    out = fused_mlp_fwd(x32, *w32)
+    assert out.dtype == torch.float32 and out.shape == (M, ws[-1].shape[1])
+    ref16 = fused_mlp_fwd(x32.half(), *[w.half() for w in w32]).float()
+    assert torch.equal(out, ref16)
+    ref = oracle.mlp_forward(x32.cpu().numpy(), [w.cpu().numpy() for w in w32])
+    assert _rel_max(out.cpu().numpy(), ref) <= TIGHT
+    buf = torch.empty_like(out)
+    assert fused_mlp_fwd(x32, *w32, out=buf) is buf and torch.equal(buf, out)
+
+
+def test_fwd_rejects_other_dtypes():
+    x, ws = make_inputs("3L128", 64)
+    with pytest.raises(TypeError):
+        fused_mlp_fwd(x.cuda().bfloat16(), *[w.cuda().bfloat16() for w in ws])

@@ -400,3 +400,25 @@ def test_training_step_in_cuda_graph():
     model(x2.cuda()).backward(g2.cuda())
     torch.cuda.synchronize()
     assert torch.equal(gv, model.v_all.grad) and torch.equal(gg, model.g_all.grad)
+
+
+def test_module_under_torch_compile():
+    """torch.compile of a model holding the fused module (the custom
+    autograd.Function calls the C ABI, which dynamo runs eagerly): same
+    outputs and gradients as eager."""
+    torch.manual_seed(13)
+    model = FusedMLPSoftplus(D=128, H=128, out_features=128).cuda().half()
+    x, _, g = make_inputs("3L128", 4000, with_grad=True)
+    x, g = x.cuda(), g.cuda()
+    out_e = model(x)
+    out_e.backward(g)
+    grads_e = [w.grad.clone() for w in model.weights]
+    for w in model.weights:
+        w.grad = None
+    compiled = torch.compile(model)
+    out_c = compiled(x)
+    out_c.backward(g)
+    torch.cuda.synchronize()
+    assert torch.equal(out_c, out_e)
+    for w, ge in zip(model.weights, grads_e):
+        assert torch.equal(w.grad, ge)
