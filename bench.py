@@ -15,6 +15,15 @@ launching stream, bracketed by a barrier and a device synchronize; inputs
 (1 GiB x, 1 GiB out) are larger than L2, so no flush is needed.  SM clocks and
 throttle reasons are sampled through NVML during the timed region.
 
+The same JSON line carries the training steps (forward + backward through
+the C ABI on preallocated buffers, replayed as one CUDA graph per step, dW
+summed over the ranks by the library's NVLink peer-memory kernel when N > 1):
+``fwd_bwd`` (3L128 with weight norm, 262,144 rows per GPU),
+``fwd_bwd_5l`` (config 4: 5-layer with weight norm, 1,048,576 rows in total,
+strong scaling), ``fwd_bwd_5l_weak`` (N > 1 only: the same with 1,048,576 rows
+per GPU) and ``fwd_bwd_w256`` (config 5: D = H = OUT = 256, 1,048,576 rows in
+total).  Each has its own roofline (tensor-bound) and e2e figure.
+
 ``--impl reference`` times the reference's own PyTorch path (kernel.py:163-171,
 restated in oracle/cpu_baseline.py because the reference tree does not exist
 on the GPU box) on the host cores, rank 0 only.
@@ -301,7 +310,7 @@ def run_mlpk(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
-    train = train5 = train256 = None
+    train = train5 = train256 = train5w = None
     if not args.no_train:
         from mlp_megakernel_b200.dp import shard_rows
 
@@ -310,6 +319,8 @@ def run_mlpk(args):
         train5 = run_training(args, world, rank, dist, barrier, "5L", b - a)
         a, b = shard_rows(args.train256_rows, rank, world)
         train256 = run_training(args, world, rank, dist, barrier, "W256", b - a)
+        train5w = (run_training(args, world, rank, dist, barrier, "5L_weak", args.train5_rows)
+                   if world > 1 else None)  # at N = 1 it is the fwd_bwd_5l run
 
     clocks = clk.summary()
     if dist is not None:
@@ -372,6 +383,8 @@ def run_mlpk(args):
         line["fwd_bwd_5l"] = train5
     if train256 is not None:
         line["fwd_bwd_w256"] = train256
+    if train5w is not None:
+        line["fwd_bwd_5l_weak"] = train5w
     if world == 1 and not args.no_cpu_baseline:
         rows = 65536
         rps, cores, calls, dt = cpu_forward_rows_per_s(rows, args.cpu_seconds)
@@ -395,6 +408,11 @@ TRAIN_SPECS = {
            "metric": "fused MLP fwd+bwd rows/s (5L 32-64-64-64-64-16 with weight norm)",
            "workload": "BASELINE config 4: 5L D=32 H=64 OUT=16 training step with weight norm, "
                        "global M={G} rows, {M} per GPU"},
+    # the same 5-layer step with the rows per GPU fixed (1,048,576 each): weak scaling
+    "5L_weak": {"dims": (32, 64, 64, 64, 64, 16), "x_dist": "uniform", "x_seed": 3, "strong": False,
+                "metric": "fused MLP fwd+bwd rows/s (5L 32-64-64-64-64-16 with weight norm)",
+                "workload": "BASELINE config 4 shape, rows per GPU fixed: 5L D=32 H=64 OUT=16 training "
+                            "step with weight norm, M={M} rows per GPU"},
     # wide 3L D=H=OUT=256 (weights streamed), plain weights,
     # global M = 1,048,576 split over the ranks
     "W256": {"dims": (256, 256, 256, 256), "x_dist": "normal", "x_seed": 4, "strong": True, "wn": False,
