@@ -200,10 +200,13 @@ def test_backward_split_k_regime_and_determinism():
     assert rel_l2(dx.cpu().numpy(), ref_dx) <= GRAD_TOL
 
 
-def test_backward_empty_batch():
-    x, ws, g = make_inputs("3L128", 0, with_grad=True)
-    out, hs, dx, dw = _run(x, ws, g)
-    assert dx.shape == (0, 128) and float(dw.abs().max()) == 0.0
+@pytest.mark.parametrize("config,dims", [("3L128", DIMS), ("5L", (32, 64, 64, 64, 64, 16)),
+                                         ("W256", (256, 256, 256, 256))])
+def test_backward_empty_batch(config, dims):
+    x, ws, g = make_inputs(config, 0, with_grad=True)
+    out, hs, dx, dw = _run(x, ws, g, dims)
+    assert out.shape == (0, dims[-1]) and dx.shape == (0, dims[0])
+    assert float(dw.abs().max()) == 0.0
 
 
 def test_weight_norm_kernels_match_oracle():
