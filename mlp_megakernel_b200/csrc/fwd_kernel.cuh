@@ -108,9 +108,9 @@ struct alignas(64) FwdMaps {
   CUtensorMap x;       // [M, d0] fp16, box {chunk(d0), 128}
   CUtensorMap out;     // [M, dL] fp16, box {chunk(dL), 128}
   CUtensorMap w[L];    // [d_l, d_{l+1}] fp16, box {chunk(d_{l+1}), d_l}
-  // training forward only: where to save the hidden activations h_1..h_{L-1}
-  // ([M, d_l] fp16 each, the exact values fed to the next GEMM), and M
-  void* hsave[L > 1 ? L - 1 : 1];
+  // training forward only: the saved hidden activations h_1..h_{L-1} ([M, d_l]
+  // fp16 each, the exact values fed to the next GEMM), box {chunk(d_l), 128}
+  CUtensorMap hsave[L > 1 ? L - 1 : 1];
   int M;
 };
 
@@ -129,7 +129,10 @@ struct FwdCfg {
   static constexpr int DL = NetT::template D<L>();
   static constexpr int HMAX = NetT::max_hidden_or_out();
   static constexpr int X_BYTES = align_up(tile_bytes(kTileM, D0), 1024);
-  static constexpr int O_BYTES = align_up(tile_bytes(kTileM, DL), 1024);  // out staging
+  static constexpr int H1 = NetT::template D<1>();
+  // staging tile of a slot: the output, and in the training forward also every
+  // hidden activation (both written to HBM by TMA stores)
+  static constexpr int O_BYTES = align_up(tile_bytes(kTileM, DL > H1 ? DL : H1), 1024);
   static constexpr int W_TOTAL = NetT::w_total();
   static constexpr int OFF_X = W_TOTAL;
   static constexpr int OFF_O = OFF_X + NS * X_BYTES;
@@ -198,13 +201,16 @@ __device__ __forceinline__ void publish_chunk(uint32_t bar) {
 // TMEM address tbuf (lane field = the warp's quarter) -> softplus -> fp16 back
 // into TMEM at h_tmem_col(); after every SPC stripes it arrives on the next
 // chunk barrier (chunk_bar0 + 8*(j/SPC)), which completes once all NG groups
-// finished those stripes.  A
+// finished those stripes.  SAVE = 1 also writes the fp16 activation to this
+// thread's row in global memory (hrow), SAVE = 2 into the swizzled staging
+// tile at stage_base (row `row`) for a TMA store.  A
 // column is always loaded before the packed activation overwrites it: a
 // stripe's packed columns lie in its own range, and the async load of the
 // next stripe is issued before this stripe's store.
-template <int N, int NG, int SPC, bool CLUSTER = false, bool SAVE = false>
+template <int N, int NG, int SPC, bool CLUSTER = false, int SAVE = 0>
 __device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chunk_bar0,
-                                           uint8_t* hrow = nullptr) {
+                                           uint8_t* hrow = nullptr, uint32_t stage_base = 0,
+                                           uint32_t row = 0) {
   static_assert(N % (32 * NG) == 0, "hidden width must be a multiple of 32 * column groups");
   constexpr int SUBS = N / (32 * NG);
   static_assert(SUBS % SPC == 0, "stripes per chunk must divide the stripes per group");
@@ -218,12 +224,21 @@ __device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chun
     uint32_t w[16];
     pack_cols<16, true>(a, w);
     tmem_st_x16(tbuf + h_tmem_col(col), w);
-    if constexpr (SAVE) {
+    if constexpr (SAVE == 1) {
       if (hrow != nullptr) {  // this thread's row exists (row < M): save h for backward
         uint4* dst = reinterpret_cast<uint4*>(hrow + 2 * col);
 #pragma unroll
         for (int v = 0; v < 4; ++v)
           dst[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+      }
+    } else if constexpr (SAVE == 2) {
+      constexpr int C = chunk_elems(N);
+      constexpr int P = pitch_bytes(N);
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const int cc = col + 8 * v;
+        st_shared_v4(stage_base + (cc / C) * (kTileM * P) + swz_off<P>(row, (cc % C) / 8), w[4 * v],
+                     w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
       }
     }
     if ((j + 1) % SPC == 0) publish_chunk<CLUSTER>(chunk_bar0 + 8 * (j / SPC));
@@ -485,25 +500,41 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
                                                ((i * L + l) >> 1) & 1, abort_flag, kDevTimeoutEpi));
         if (!ok) break;
         tc_fence_after();
-        if (l == 0 && i > 0) {
-          // obuf may still be the source of this slot's previous TMA store:
-          // the leader waits for that store to finish reading, then frees it.
+        // obuf may still be the source of this slot's previous TMA store: the
+        // leader waits for that store to finish reading, then frees it.  Uses
+        // of obuf: one per tile (the output) or, in the training forward, one
+        // per layer (every h_l, then the output).
+        const int use = TRAIN ? i * L + l : i;
+        if ((TRAIN || l == 0) && use > 0) {
           if (leader) {
             bulk_wait_group_read<0>();
             mbar_arrive(bar_store_free(s));
           }
           __syncwarp();
           ok = __all_sync(0xffffffffu,
-                          mbar_wait(bar_store_free(s), (i - 1) & 1, abort_flag, kDevTimeoutEpi));
+                          mbar_wait(bar_store_free(s), (use - 1) & 1, abort_flag, kDevTimeoutEpi));
           if (!ok) break;
         }
         const uint32_t t_buf = t_lane + ((i * L + l) & 1) * Cfg::SLOT_COLS;
         if constexpr (TRAIN) {
-          const int grow = t * kTileM + static_cast<int>(row);
-          uint8_t* hrow = grow < maps.M ? static_cast<uint8_t*>(maps.hsave[l]) +
-                                              static_cast<size_t>(grow) * H * 2
-                                        : nullptr;
-          hidden_job<H, Cfg::NG, Cfg::SPC, false, true>(t_buf, grp, bar_chunk(s, 0), hrow);
+          // h_l -> TMEM (next layer's A) and the staging tile -> TMA store
+          hidden_job<H, Cfg::NG, Cfg::SPC, false, 2>(t_buf, grp, bar_chunk(s, 0), nullptr, obuf, row);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_out_ready(s));
+          if (leader) {
+            ok = mbar_wait(bar_out_ready(s), use & 1, abort_flag, kDevTimeoutEpi);
+            if (ok) {
+              constexpr int C = chunk_elems(H);
+              constexpr int P = pitch_bytes(H);
+#pragma unroll
+              for (int c = 0; c < H / C; ++c)
+                tma_store_2d(&maps.hsave[l], obuf + c * kTileM * P, c * C, t * kTileM);
+              bulk_commit_group();
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          if (!ok) break;
         } else {
           hidden_job<H, Cfg::NG, Cfg::SPC>(t_buf, grp, bar_chunk(s, 0));
         }
@@ -516,13 +547,24 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
                                                ((i * L + l) >> 1) & 1, abort_flag, kDevTimeoutEpi));
         if (!ok) break;
         tc_fence_after();
+        const int use = TRAIN ? i * L + l : i;
+        if constexpr (TRAIN) {  // obuf held h_{L-1}: wait until its store has read it
+          if (leader) {
+            bulk_wait_group_read<0>();
+            mbar_arrive(bar_store_free(s));
+          }
+          __syncwarp();
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(bar_store_free(s), (use - 1) & 1, abort_flag, kDevTimeoutEpi));
+          if (!ok) break;
+        }
         const uint32_t t_buf = t_lane + ((i * L + l) & 1) * Cfg::SLOT_COLS;
         out_job<Cfg::DL, NCOL_O>(t_buf, obuf, row, grp * NCOL_O);
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_out_ready(s));
-        if (leader) ok = mbar_wait(bar_out_ready(s), i & 1, abort_flag, kDevTimeoutEpi);
+        if (leader) ok = mbar_wait(bar_out_ready(s), use & 1, abort_flag, kDevTimeoutEpi);
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (leader && ok) {
           constexpr int C = chunk_elems(Cfg::DL);

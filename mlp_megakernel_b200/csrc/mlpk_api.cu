@@ -179,7 +179,13 @@ int launch_fwd(const void* x, const void* const* W, void* out, int64_t M, void* 
   });
   if (wrc) return wrc;
   maps.M = static_cast<int>(M);
-  for (int l = 0; l + 1 < L; ++l) maps.hsave[l] = hsave ? hsave[l] : nullptr;
+  if (hsave) {
+    for (int l = 0; l + 1 < L; ++l) {
+      if (!hsave[l]) return MLPK_ERR_NULL;
+      if ((rc = make_map_2d(&maps.hsave[l], hsave[l], Cfg::H, M, mlpk::chunk_elems(Cfg::H), mlpk::kTileM)))
+        return rc;
+    }
+  }
 
   const int num_tiles = static_cast<int>((M + mlpk::kTileM - 1) / mlpk::kTileM);
   const int grid = num_tiles < di.sm_count ? num_tiles : di.sm_count;
