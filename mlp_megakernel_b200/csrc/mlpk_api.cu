@@ -318,7 +318,12 @@ int launch_stream_fwd(const void* x, const void* const* W, void* out, int64_t M,
                         mlpk::kStreamK);
   });
   if (wrc) return wrc;
-  for (int l = 0; l + 1 < L; ++l) maps.save[l] = hsave ? hsave[l] : nullptr;
+  if (hsave) {
+    for (int l = 0; l + 1 < L; ++l) {
+      if (!hsave[l]) return MLPK_ERR_NULL;
+      if ((rc = make_map_2d(&maps.save[l], hsave[l], Cfg::H, M, 64, mlpk::kTileM))) return rc;
+    }
+  }
   maps.M = static_cast<int>(M);
   const int64_t tiles = (M + mlpk::kTileM - 1) / mlpk::kTileM;
   const int grid = static_cast<int>(tiles < di.sm_count ? tiles : di.sm_count);
@@ -395,7 +400,7 @@ int launch_stream_bwd(const void* x, const void* const* W, const void* const* h,
     for (int s = 0; s + 1 < L; ++s) {
       const int l = L - 1 - s;
       maps.hact[s] = h[l - 1];
-      maps.save[s] = dz[l - 1];
+      if ((rc = make_map_2d(&maps.save[s], dz[l - 1], Cfg::H, M, 64, mlpk::kTileM))) return rc;
     }
     maps.M = static_cast<int>(M);
     const int64_t tiles = (M + mlpk::kTileM - 1) / mlpk::kTileM;

@@ -27,9 +27,9 @@
 //    fp16 result (tcgen05.mma ... [a_tmem]), chunk by chunk as published.
 //  * EPW epilogue warps (4 per column group): tcgen05.ld the accumulator,
 //    apply the stage's elementwise function in fp32, tcgen05.st the fp16
-//    result back into TMEM for the next stage (and to global memory when the
-//    stage's result is saved), and for the last stage stage the fp16 output
-//    in shared memory for a TMA store.
+//    result back into TMEM for the next stage; a saved stage result (h in the
+//    training forward, dz in the data-gradient chain) and the last stage's
+//    output go through one shared-memory staging tile and TMA stores.
 //  * All hand-offs are mbarriers and every wait is bounded (ptx.cuh).
 #pragma once
 #include "bwd_kernel.cuh"
@@ -58,7 +58,8 @@ struct alignas(64) StreamMaps {
   CUtensorMap in;    // stage-0 input [M, d_0 of the chain], box {64, 128}
   CUtensorMap out;   // last-stage output [M, d_L of the chain], box {64, 128}
   CUtensorMap w[L];  // stage s weight chunks (see the producer)
-  void* save[L > 1 ? L - 1 : 1];        // fp16 [M, d_{s+1}] result of stage s (or null)
+  // fp16 [M, d_{s+1}] result of hidden stage s, box {64, 128} (written when SAVE)
+  CUtensorMap save[L > 1 ? L - 1 : 1];
   const void* hact[L > 1 ? L - 1 : 1];  // dgrad: saved h_l read by stage s (l = L-1-s)
   int M;
 };
@@ -120,12 +121,12 @@ __device__ __forceinline__ void dgrad_load_h(uint4 (&hv)[4], const uint8_t* hrow
 // Data-gradient stage epilogue of one warp (mirrors hidden_job): dz = dh *
 // (1 - e^{-h}) for the thread's row over the group's stripes, fp16 result
 // packed into TMEM at h_tmem_col() for the next stage's A operand, optionally
-// saved to global memory, chunks published as in hidden_job.  hv holds the
+// staged for a TMA store (SAVE), chunks published as in hidden_job.  hv holds the
 // first two stripes' h (loaded before the accumulator wait); each later
 // stripe's h is loaded two stripes ahead, into the registers just consumed.
 template <int N, int NG, int SPC, bool SAVE>
 __device__ __forceinline__ void dgrad_job(uint32_t tbuf, int grp, uint32_t chunk_bar0, uint4 (&hv)[2][4],
-                                          const uint8_t* hrow, uint8_t* dzrow) {
+                                          const uint8_t* hrow, uint32_t stage_base, uint32_t row) {
   constexpr int SUBS = N / (32 * NG);
   static_assert(SUBS % SPC == 0, "stripes per chunk must divide the stripes per group");
   uint32_t a[32];
@@ -147,12 +148,14 @@ __device__ __forceinline__ void dgrad_job(uint32_t tbuf, int grp, uint32_t chunk
       w[p] = pack_half2(dz.x, dz.y);
     }
     tmem_st_x16(tbuf + h_tmem_col(col), w);
-    if constexpr (SAVE) {
-      if (dzrow != nullptr) {
-        uint4* dst = reinterpret_cast<uint4*>(dzrow + 2 * col);
+    if constexpr (SAVE) {  // into the swizzled staging tile (TMA-store layout)
+      constexpr int C = chunk_elems(N);
+      constexpr int P = pitch_bytes(N);
 #pragma unroll
-        for (int v = 0; v < 4; ++v)
-          dst[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+      for (int v = 0; v < 4; ++v) {
+        const int cc = col + 8 * v;
+        st_shared_v4(stage_base + (cc / C) * (kTileM * P) + swz_off<P>(row, (cc % C) / 8), w[4 * v],
+                     w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
       }
     }
     if ((j + 1) % SPC == 0) publish_chunk<false>(chunk_bar0 + 8 * (j / SPC));
@@ -393,26 +396,41 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
                         mbar_wait(bar_acc_full(g & 1), (g >> 1) & 1, abort_flag, kDevTimeoutEpi));
         if (!ok) break;
         tc_fence_after();
-        if (s == 0 && i > 0) {
-          // the output staging buffer may still be the source of the previous
-          // tile's TMA store: the leader waits for it to be read, then frees it
+        // the staging tile may still be the source of its previous TMA store:
+        // the leader waits for it to be read, then frees it.  Uses: one per
+        // tile (the output) or, when stage results are saved, one per stage.
+        const int use = SAVE ? g : i;
+        if ((SAVE || s == 0) && use > 0) {
           if (leader) {
             bulk_wait_group_read<0>();
             mbar_arrive(bar_store_free);
           }
           __syncwarp();
           ok = __all_sync(0xffffffffu,
-                          mbar_wait(bar_store_free, (i - 1) & 1, abort_flag, kDevTimeoutEpi));
+                          mbar_wait(bar_store_free, (use - 1) & 1, abort_flag, kDevTimeoutEpi));
           if (!ok) break;
         }
         const uint32_t t_buf = t_lane + (g & 1) * Cfg::SLOT_COLS;
-        uint8_t* srow = (SAVE && valid && maps.save[s] != nullptr)
-                            ? static_cast<uint8_t*>(maps.save[s]) + static_cast<size_t>(grow) * H * 2
-                            : nullptr;
         if constexpr (MODE == kStreamFwd)
-          hidden_job<H, NG, Cfg::SPC, false, SAVE>(t_buf, grp, bar_chunk(0), srow);
+          hidden_job<H, NG, Cfg::SPC, false, SAVE ? 2 : 0>(t_buf, grp, bar_chunk(0), nullptr, s_o, row);
         else
-          dgrad_job<H, NG, Cfg::SPC, SAVE>(t_buf, grp, bar_chunk(0), hv, hrow, srow);
+          dgrad_job<H, NG, Cfg::SPC, SAVE>(t_buf, grp, bar_chunk(0), hv, hrow, s_o, row);
+        if constexpr (SAVE) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_out_ready);
+          if (leader) {
+            ok = mbar_wait(bar_out_ready, use & 1, abort_flag, kDevTimeoutEpi);
+            if (ok) {
+#pragma unroll
+              for (int c = 0; c < H / 64; ++c)
+                tma_store_2d(&maps.save[s], s_o + c * kTileM * 128, c * 64, t * kTileM);
+              bulk_commit_group();
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          if (!ok) break;
+        }
       }
       if (!ok) break;
       {
@@ -422,13 +440,24 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
                         mbar_wait(bar_acc_full(g & 1), (g >> 1) & 1, abort_flag, kDevTimeoutEpi));
         if (!ok) break;
         tc_fence_after();
+        const int use = SAVE ? g : i;
+        if constexpr (SAVE) {  // the tile held the last saved stage: wait for its store's read
+          if (leader) {
+            bulk_wait_group_read<0>();
+            mbar_arrive(bar_store_free);
+          }
+          __syncwarp();
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(bar_store_free, (use - 1) & 1, abort_flag, kDevTimeoutEpi));
+          if (!ok) break;
+        }
         const uint32_t t_buf = t_lane + (g & 1) * Cfg::SLOT_COLS;
         out_job<Cfg::DL, NCOL_O>(t_buf, s_o, row, grp * NCOL_O);
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_out_ready);
-        if (leader) ok = mbar_wait(bar_out_ready, i & 1, abort_flag, kDevTimeoutEpi);
+        if (leader) ok = mbar_wait(bar_out_ready, use & 1, abort_flag, kDevTimeoutEpi);
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (leader && ok) {
 #pragma unroll
