@@ -311,6 +311,28 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
         const int uses = issued > r ? (issued - r + R - 1) / R : 0;
         if (uses > 0) mbar_wait(bar_slot_full(r), (uses - 1) & 1, &no_abort, kDevTimeoutFull);
       }
+    } else if (lane == 1) {
+      // dx stores, off the epilogue warps' path: the epilogue stages each
+      // tile's dx in x's ring slot; this lane TMA-stores it and, once the store
+      // has read it, returns the slot to the producer
+      bool ok = true;
+      for (int i = 0; ok; ++i) {
+        const int t = tile_of(i);
+        if (t >= num_tiles) break;
+        const int s = i % NS, j = i / NS;
+        ok = mbar_wait(bar_out_ready(s), j & 1, abort_flag, kDevTimeoutEpi);
+        if (!ok) break;
+        const int nx = i * NLD + L;
+        const uint32_t xb = slot_addr(nx % R);
+        constexpr int C = chunk_elems(Cfg::D0);
+        constexpr int P = pitch_bytes(Cfg::D0);
+#pragma unroll
+        for (int cc = 0; cc < Cfg::D0 / C; ++cc) tma_store_2d(&maps.dx, xb + cc * kTileM * P, cc * C, t * kTileM);
+        bulk_commit_group();
+        bulk_wait_group_read<0>();
+        mbar_arrive_cnt(bar_slot_empty(nx % R), EW);  // x's slot may take a new tile
+      }
+      bulk_wait_group<0>();
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -406,7 +428,6 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t acc = tmem_base + lane_off + Cfg::ACC_COL + s * Cfg::ACC_W;
     const uint32_t sg = s_g(s);
-    const bool store_leader = (ew == 0 && lane == 0);
     bool ok = true;
     for (int j = 0; ok; ++j) {
       const int i = j * NS + s;  // this slot's j-th tile
@@ -478,21 +499,7 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
             st_tile_row8<DI>(xb, row, c0 + 8 * u, o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar_out_ready(s));
-          if (store_leader) {
-            ok = mbar_wait(bar_out_ready(s), j & 1, abort_flag, kDevTimeoutEpi);
-            if (ok) {
-              constexpr int C = chunk_elems(DI);
-              constexpr int P = pitch_bytes(DI);
-#pragma unroll
-              for (int cc = 0; cc < DI / C; ++cc)
-                tma_store_2d(&maps.dx, xb + cc * kTileM * P, cc * C, t * kTileM);
-              bulk_commit_group();
-              bulk_wait_group_read<0>();
-              mbar_arrive_cnt(bar_slot_empty(nx % R), EW);  // x's slot may take a new tile
-            }
-          }
-          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          if (lane == 0) mbar_arrive(bar_out_ready(s));  // warp 0, lane 1 stores it
         }
       });
     }
@@ -532,7 +539,6 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
         off += NetT::dim(l) * DO;
       });
     }
-    if (store_leader) bulk_wait_group<0>();
     __syncwarp();
   }
 
