@@ -77,6 +77,10 @@ class NcclGradReducer:
         pass
 
 
+class PeerSetupError(RuntimeError):
+    """The ranks could not set up peer-memory buffers (every rank raises it)."""
+
+
 class _DevicePtr:
     """A raw device pointer seen by torch as a float32 tensor (no copy)."""
 
@@ -111,28 +115,42 @@ class PeerGradReducer:
         if self.world > _lib.PEER_MAX_RANKS:
             raise ValueError(f"peer-memory reduction serves at most {_lib.PEER_MAX_RANKS} ranks")
         self._lib = _lib.lib()
+        self._own = None
+        self._opened = []
+        # Every step below is agreed by all ranks, so a failure on one rank
+        # (no CUDA IPC, out of memory) makes every rank give up together
+        # instead of leaving the others in a collective.
         own = ctypes.c_void_p()
         handle = (ctypes.c_uint8 * _lib.PEER_HANDLE_BYTES)()
-        _lib.check("mlpk_peer_alloc", self._lib.mlpk_peer_alloc(n, ctypes.byref(own), handle))
-        self._own = own.value
-        handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=process_group)
-        self._opened = []
+        ok = self._lib.mlpk_peer_alloc(n, ctypes.byref(own), handle) == 0
+        if ok:
+            self._own = own.value
+        shared = [None] * self.world
+        dist.all_gather_object(shared, (ok, bytes(handle)), group=process_group)
+        if not all(flag for flag, _ in shared):
+            self.close(sync=False)
+            raise PeerSetupError("a rank could not allocate its peer buffer")
         ptrs = []
-        for q, h in enumerate(handles):
+        ok = True
+        for q, (_, h) in enumerate(shared):
             if q == self.rank:
                 ptrs.append(self._own)
                 continue
             p = ctypes.c_void_p()
             hb = (ctypes.c_uint8 * _lib.PEER_HANDLE_BYTES).from_buffer_copy(h)
-            _lib.check("mlpk_peer_open", self._lib.mlpk_peer_open(hb, ctypes.byref(p)))
+            if self._lib.mlpk_peer_open(hb, ctypes.byref(p)) != 0:
+                ok = False
+                break
             self._opened.append(p.value)
             ptrs.append(p.value)
+        flags = [None] * self.world
+        dist.all_gather_object(flags, ok, group=process_group)
+        if not all(flags):
+            self.close(sync=False)
+            raise PeerSetupError("a rank could not map the other ranks' peer buffers")
         self._ptrs = _lib.ptr_array(ptrs)
         self._local = torch.as_tensor(_DevicePtr(self._own, n),
                                       device=torch.device("cuda", torch.cuda.current_device()))
-        # every rank has opened every buffer before the first step
-        dist.barrier(group=process_group)
 
     def local_buffer(self, like: torch.Tensor = None) -> torch.Tensor:
         """This rank's dW slot (the backward writes dW here)."""
@@ -150,19 +168,19 @@ class PeerGradReducer:
                                                  torch.cuda.current_stream(out.device).cuda_stream))
         return out
 
-    def close(self):
+    def close(self, sync: bool = True):
         """Unmap the peers' buffers and free this rank's.  Safe once this rank's
         last reduction has completed: that kernel returns only after every rank
         finished reading and writing this rank's buffer."""
-        if self._own is None:
-            return
-        torch.cuda.synchronize()
+        if sync:
+            torch.cuda.synchronize()
         self._local = None
         for p in self._opened:
             self._lib.mlpk_peer_close(ctypes.c_void_p(p))
         self._opened = []
-        self._lib.mlpk_peer_free(ctypes.c_void_p(self._own))
-        self._own = None
+        if self._own is not None:
+            self._lib.mlpk_peer_free(ctypes.c_void_p(self._own))
+            self._own = None
 
 
 def single_node(process_group=None) -> bool:
@@ -181,8 +199,12 @@ def make_grad_reducer(n: int, process_group=None, kind: str = "auto"):
 
     if kind not in ("auto", "peer", "nccl"):
         raise ValueError(f"unknown reducer kind {kind!r}")
-    if kind == "peer" or (kind == "auto" and dist.get_backend(process_group) == "nccl"
-                          and single_node(process_group) and dist.get_world_size(process_group) <= 8
-                          and n % 4 == 0):
+    if kind == "peer":
         return PeerGradReducer(n, process_group)
+    if (kind == "auto" and dist.get_backend(process_group) == "nccl" and single_node(process_group)
+            and dist.get_world_size(process_group) <= 8 and n % 4 == 0):
+        try:
+            return PeerGradReducer(n, process_group)
+        except PeerSetupError:
+            pass  # every rank of the group lands here together
     return NcclGradReducer(n, process_group)

@@ -99,3 +99,44 @@ def test_dp_gradient_sum_equals_full_batch(config, M, tmp_path):
     err = np.linalg.norm(dw0 - full) / np.linalg.norm(full)
     assert err <= 1e-6, err
     assert np.array_equal(np.load(tmp_path / "p0.npy"), np.load(tmp_path / "p1.npy"))
+
+
+def _fallback_worker(rank, port, result_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        from mlp_megakernel_b200.dp import (NcclGradReducer, PeerGradReducer, PeerSetupError,
+                                            make_grad_reducer)
+
+        # no GPU here: the peer buffer cannot be allocated on any rank, and
+        # every rank must learn it together (no rank left in a collective)
+        raised = False
+        try:
+            PeerGradReducer(16)
+        except PeerSetupError:
+            raised = True
+        red = make_grad_reducer(16)  # "auto": not NCCL here -> the collective reducer
+        out = torch.full((16,), float(rank + 1))
+        red.reduce(red.local_buffer(out), out)
+        np.save(os.path.join(result_dir, f"f{rank}.npy"),
+                np.array([raised, isinstance(red, NcclGradReducer), float(out[0])]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_reducer_setup_failure_is_collective(tmp_path):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_fallback_worker, args=(r, port, str(tmp_path))) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    for r in range(WORLD):
+        raised, is_nccl, val = np.load(tmp_path / f"f{r}.npy")
+        assert raised and is_nccl and val == 3.0
