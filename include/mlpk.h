@@ -51,7 +51,14 @@ enum {
 /* Human-readable text for a status code. */
 const char* mlpk_status_string(int status);
 
-/* 1 if a kernel for this shape is compiled into the library, else 0. */
+/* 1 if a kernel serves this shape, else 0.  Compiled networks: 64-64-64-64,
+ * 128-128-128-128, 256-256-256-256 and 32-64-64-64-64-16.  A network of the
+ * same depth whose every width is a multiple of 8 and at most the compiled
+ * width is served by the smallest such kernel (its missing rows / columns are
+ * zero-filled on load and clipped on store; results are those of the
+ * caller's network).  Hidden widths need not be equal.  The reference's
+ * kernel takes the widths its tiles divide (kernel.py:25-53); all of them
+ * up to 256 wide are served. */
 int mlpk_shape_supported(const mlpk_shape* shape);
 
 /* Inference forward: out[M, dL] = MLP(x[M, d0]).
@@ -60,7 +67,8 @@ int mlpk_shape_supported(const mlpk_shape* shape);
 int mlpk_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W, void* out,
              mlpk_stream_t stream);
 
-/* 1 if training (mlpk_train_fwd + mlpk_bwd) is compiled for this shape. */
+/* 1 if training (mlpk_train_fwd + mlpk_bwd) serves this shape (the same
+ * rule as mlpk_shape_supported). */
 int mlpk_train_supported(const mlpk_shape* shape);
 
 /* Training forward: as mlpk_fwd, and also writes every hidden activation

@@ -46,6 +46,10 @@ struct alignas(64) BwdMaps {
   CUtensorMap h[L > 1 ? L - 1 : 1];  // h_1..h_{L-1}: [M, d_l] fp16 loads
   CUtensorMap w[L];            // [d_l, d_{l+1}] fp16 loads
   float* partials;             // [gridDim.x][sum_l d_l*d_{l+1}] fp32
+  // caller's d0 when the network is served by a larger one (the maps carry
+  // the caller's extents; loads zero-fill, the dx store skips chunks that
+  // start at or past this width)
+  int dx_cols;
 };
 
 template <class NetT>
@@ -327,7 +331,8 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
         constexpr int C = chunk_elems(Cfg::D0);
         constexpr int P = pitch_bytes(Cfg::D0);
 #pragma unroll
-        for (int cc = 0; cc < Cfg::D0 / C; ++cc) tma_store_2d(&maps.dx, xb + cc * kTileM * P, cc * C, t * kTileM);
+        for (int cc = 0; cc < Cfg::D0 / C; ++cc)
+          if (cc * C < maps.dx_cols) tma_store_2d(&maps.dx, xb + cc * kTileM * P, cc * C, t * kTileM);
         bulk_commit_group();
         bulk_wait_group_read<0>();
         mbar_arrive_cnt(bar_slot_empty(nx % R), EW);  // x's slot may take a new tile
@@ -559,12 +564,28 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
 constexpr int kReduceElems = 64;
 constexpr int kReduceSlices = 4;
 
+// Where the reduced weight gradients go.  layers == 0: the caller's flat dW has
+// the kernel network's layout (element e of group y lands at y * nfloats + e).
+// Otherwise the caller's network is smaller than the kernel's (served by zero
+// padding): element e of the kernel's flat layout (all groups concatenated) is
+// row r, column c of layer l's [k_l][n_l] block at kernel offset koff[l]; it
+// goes to the caller's [rk_l][rn_l] block at roff[l] when r < rk_l and c <
+// rn_l, and is dropped otherwise (it is an exact zero: padded activations and
+// data gradients are zero).
+struct DwLayout {
+  int layers;
+  long long koff[9];
+  int kn[8];
+  int rk[8];
+  int rn[8];
+  long long roff[8];
+};
+
 __global__ void __launch_bounds__(kReduceElems * kReduceSlices)
     mlp_reduce_kernel(const float* __restrict__ partials, int nparts, int nfloats,
-                      float* __restrict__ dw) {
+                      float* __restrict__ dw, const __grid_constant__ DwLayout lay) {
   __shared__ float red[kReduceSlices][kReduceElems];
   partials += static_cast<size_t>(blockIdx.y) * nparts * nfloats;
-  dw += static_cast<size_t>(blockIdx.y) * nfloats;
   const int le = threadIdx.x % kReduceElems, sl = threadIdx.x / kReduceElems;
   const int e = blockIdx.x * kReduceElems + le;
   float acc = 0.0f;
@@ -587,7 +608,17 @@ __global__ void __launch_bounds__(kReduceElems * kReduceSlices)
     float t = red[0][le];
 #pragma unroll
     for (int k = 1; k < kReduceSlices; ++k) t += red[k][le];
-    dw[e] = t;
+    const long long eg = static_cast<long long>(blockIdx.y) * nfloats + e;
+    if (lay.layers == 0) {
+      dw[eg] = t;
+    } else {
+      int l = 0;
+      while (l + 1 < lay.layers && eg >= lay.koff[l + 1]) ++l;
+      const long long q = eg - lay.koff[l];
+      const int r = static_cast<int>(q / lay.kn[l]);
+      const int c = static_cast<int>(q % lay.kn[l]);
+      if (r < lay.rk[l] && c < lay.rn[l]) dw[lay.roff[l] + static_cast<long long>(r) * lay.rn[l] + c] = t;
+    }
   }
 }
 

@@ -112,6 +112,13 @@ struct alignas(64) FwdMaps {
   // fp16 each, the exact values fed to the next GEMM), box {chunk(d_l), 128}
   CUtensorMap hsave[L > 1 ? L - 1 : 1];
   int M;
+  // The caller's widths when they are smaller than the kernel's network (a
+  // network served by a larger one): the maps above carry the caller's
+  // extents, so TMA loads fill the missing rows / columns with zeros, and the
+  // stores skip every chunk that starts at or past these widths (partially
+  // covered chunks are clipped by TMA).
+  int out_cols;                     // caller's d_L
+  int h_cols[L > 1 ? L - 1 : 1];   // caller's d_1 .. d_{L-1}
 };
 
 template <int I, int N, class F>
@@ -529,7 +536,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
               constexpr int P = pitch_bytes(H);
 #pragma unroll
               for (int c = 0; c < H / C; ++c)
-                tma_store_2d(&maps.hsave[l], obuf + c * kTileM * P, c * C, t * kTileM);
+                if (c * C < maps.h_cols[l]) tma_store_2d(&maps.hsave[l], obuf + c * kTileM * P, c * C, t * kTileM);
               bulk_commit_group();
             }
           }
@@ -571,7 +578,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
           constexpr int P = pitch_bytes(Cfg::DL);
 #pragma unroll
           for (int c = 0; c < Cfg::DL / C; ++c)
-            tma_store_2d(&maps.out, obuf + c * kTileM * P, c * C, t * kTileM);
+            if (c * C < maps.out_cols) tma_store_2d(&maps.out, obuf + c * kTileM * P, c * C, t * kTileM);
           bulk_commit_group();
         }
       }

@@ -152,9 +152,14 @@ bool set_smem_once(Kern kern, int bytes, int dev) {
 }
 
 // ------------------------------------------------------------------ forward
+// Every launcher takes the caller's widths rd[0..L] (each at most the kernel
+// network's width, a multiple of 8): tensor maps of the caller's tensors carry
+// the caller's extents with the kernel network's boxes, so a smaller network
+// is served by the larger kernel through TMA zero fill (rd equal to the kernel
+// network's widths is the plain case).
 template <class NetT, int NS, int EPW>
-int launch_fwd(const void* x, const void* const* W, void* out, int64_t M, void* const* hsave,
-               cudaStream_t st) {
+int launch_fwd(const int* rd, const void* x, const void* const* W, void* out, int64_t M,
+               void* const* hsave, cudaStream_t st) {
   using Cfg = FwdCfg<NetT, NS, EPW>;
   constexpr int L = NetT::L;
   DevInfo di;
@@ -166,23 +171,25 @@ int launch_fwd(const void* x, const void* const* W, void* out, int64_t M, void* 
 
   FwdMaps<L> maps;
   std::memset(&maps, 0, sizeof(maps));
-  rc = make_map_2d(&maps.x, x, Cfg::D0, M, mlpk::chunk_elems(Cfg::D0), mlpk::kTileM);
+  rc = make_map_2d(&maps.x, x, rd[0], M, mlpk::chunk_elems(Cfg::D0), mlpk::kTileM);
   if (rc) return rc;
-  rc = make_map_2d(&maps.out, out, Cfg::DL, M, mlpk::chunk_elems(Cfg::DL), mlpk::kTileM);
+  rc = make_map_2d(&maps.out, out, rd[L], M, mlpk::chunk_elems(Cfg::DL), mlpk::kTileM);
   if (rc) return rc;
   int wrc = MLPK_OK;
   mlpk::static_for<0, L>([&](auto lc) {
     constexpr int l = decltype(lc)::value;
     constexpr int K = NetT::template D<l>();
     constexpr int N = NetT::template D<l + 1>();
-    if (wrc == MLPK_OK) wrc = make_map_2d(&maps.w[l], W[l], N, K, mlpk::chunk_elems(N), K);
+    if (wrc == MLPK_OK) wrc = make_map_2d(&maps.w[l], W[l], rd[l + 1], rd[l], mlpk::chunk_elems(N), K);
   });
   if (wrc) return wrc;
   maps.M = static_cast<int>(M);
+  maps.out_cols = rd[L];
+  for (int l = 0; l + 1 < L; ++l) maps.h_cols[l] = rd[l + 1];
   if (hsave) {
     for (int l = 0; l + 1 < L; ++l) {
       if (!hsave[l]) return MLPK_ERR_NULL;
-      if ((rc = make_map_2d(&maps.hsave[l], hsave[l], Cfg::H, M, mlpk::chunk_elems(Cfg::H), mlpk::kTileM)))
+      if ((rc = make_map_2d(&maps.hsave[l], hsave[l], rd[l + 1], M, mlpk::chunk_elems(Cfg::H), mlpk::kTileM)))
         return rc;
     }
   }
@@ -201,9 +208,11 @@ int launch_fwd(const void* x, const void* const* W, void* out, int64_t M, void* 
 
 // CTA-pair forward: clusters of 2 CTAs, one M=256 UMMA per pair tile.
 template <class NetT, int NS, int EPW>
-int launch_fwd2(const void* x, const void* const* W, void* out, int64_t M, void* const* hsave,
-                cudaStream_t st) {
+int launch_fwd2(const int* rd, const void* x, const void* const* W, void* out, int64_t M,
+                void* const* hsave, cudaStream_t st) {
   if (hsave) return MLPK_ERR_UNSUPPORTED;  // the pair kernel is inference-only
+  for (int i = 0; i <= NetT::L; ++i)       // and serves its own widths only
+    if (rd[i] != NetT::dim(i)) return MLPK_ERR_UNSUPPORTED;
   using Cfg = mlpk::Fwd2Cfg<NetT, NS, EPW>;
   constexpr int L = NetT::L;
   DevInfo di;
@@ -228,6 +237,8 @@ int launch_fwd2(const void* x, const void* const* W, void* out, int64_t M, void*
     if (wrc == MLPK_OK) wrc = make_map_2d(&maps.w[l], W[l], 2 * NH, K, mlpk::chunk_elems(NH), K);
   });
   if (wrc) return wrc;
+  maps.M = static_cast<int>(M);
+  maps.out_cols = Cfg::DL;
 
   auto kern = mlpk::mlp_fwd2_kernel<NetT, NS, EPW>;
   if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
@@ -250,9 +261,34 @@ size_t bwd_workspace(int64_t M, int sm_count) {
          sizeof(float);
 }
 
+// Output layout of the weight-gradient reduction for the caller's widths rd
+// (identity when they are the kernel network's widths).
 template <class NetT>
-int launch_bwd(const void* x, const void* const* W, const void* const* h, const void* g, void* dx,
-               float* ws, size_t ws_bytes, float* dw, int64_t M, cudaStream_t st) {
+mlpk::DwLayout dw_layout(const int* rd) {
+  constexpr int L = NetT::L;
+  mlpk::DwLayout lay;
+  std::memset(&lay, 0, sizeof(lay));
+  bool same = true;
+  for (int i = 0; i <= L; ++i) same = same && rd[i] == NetT::dim(i);
+  if (same) return lay;
+  lay.layers = L;
+  long long ko = 0, ro = 0;
+  for (int l = 0; l < L; ++l) {
+    lay.koff[l] = ko;
+    lay.kn[l] = NetT::dim(l + 1);
+    lay.rk[l] = rd[l];
+    lay.rn[l] = rd[l + 1];
+    lay.roff[l] = ro;
+    ko += static_cast<long long>(NetT::dim(l)) * NetT::dim(l + 1);
+    ro += static_cast<long long>(rd[l]) * rd[l + 1];
+  }
+  lay.koff[L] = ko;
+  return lay;
+}
+
+template <class NetT>
+int launch_bwd(const int* rd, const void* x, const void* const* W, const void* const* h, const void* g,
+               void* dx, float* ws, size_t ws_bytes, float* dw, int64_t M, cudaStream_t st) {
   using Cfg = mlpk::BwdCfg<NetT>;
   constexpr int L = NetT::L;
   DevInfo di;
@@ -266,20 +302,22 @@ int launch_bwd(const void* x, const void* const* W, const void* const* h, const 
     if (ws_bytes < bwd_workspace<NetT>(M, di.sm_count)) return MLPK_ERR_SHAPE;
     mlpk::BwdMaps<L> maps;
     std::memset(&maps, 0, sizeof(maps));
-    if ((rc = make_map_2d(&maps.x, x, Cfg::D0, M, mlpk::chunk_elems(Cfg::D0), mlpk::kTileM))) return rc;
-    if ((rc = make_map_2d(&maps.g, g, Cfg::DL, M, mlpk::chunk_elems(Cfg::DL), mlpk::kTileM))) return rc;
-    if ((rc = make_map_2d(&maps.dx, dx, Cfg::D0, M, mlpk::chunk_elems(Cfg::D0), mlpk::kTileM))) return rc;
+    if ((rc = make_map_2d(&maps.x, x, rd[0], M, mlpk::chunk_elems(Cfg::D0), mlpk::kTileM))) return rc;
+    if ((rc = make_map_2d(&maps.g, g, rd[L], M, mlpk::chunk_elems(Cfg::DL), mlpk::kTileM))) return rc;
+    if ((rc = make_map_2d(&maps.dx, dx, rd[0], M, mlpk::chunk_elems(Cfg::D0), mlpk::kTileM))) return rc;
     int wrc = MLPK_OK;
     mlpk::static_for<0, L>([&](auto lc) {
       constexpr int l = decltype(lc)::value;
       constexpr int K = NetT::template D<l>();
       constexpr int N = NetT::template D<l + 1>();
-      if (wrc == MLPK_OK) wrc = make_map_2d(&maps.w[l], W[l], N, K, mlpk::chunk_elems(N), K);
+      if (wrc == MLPK_OK) wrc = make_map_2d(&maps.w[l], W[l], rd[l + 1], rd[l], mlpk::chunk_elems(N), K);
       if constexpr (l >= 1)
-        if (wrc == MLPK_OK) wrc = make_map_2d(&maps.h[l - 1], h[l - 1], K, M, mlpk::chunk_elems(K), mlpk::kTileM);
+        if (wrc == MLPK_OK)
+          wrc = make_map_2d(&maps.h[l - 1], h[l - 1], rd[l], M, mlpk::chunk_elems(K), mlpk::kTileM);
     });
     if (wrc) return wrc;
     maps.partials = ws;
+    maps.dx_cols = rd[0];
     auto kern = mlpk::mlp_bwd_kernel<NetT>;
     if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
     const int num_tiles = static_cast<int>((M + mlpk::kTileM - 1) / mlpk::kTileM);
@@ -287,7 +325,7 @@ int launch_bwd(const void* x, const void* const* W, const void* const* h, const 
   }
   return launch_kernel(mlpk::mlp_reduce_kernel, (nfloats + mlpk::kReduceElems - 1) / mlpk::kReduceElems,
                        mlpk::kReduceElems * mlpk::kReduceSlices, 0, st,
-                       static_cast<const float*>(ws), grid, nfloats, dw);
+                       static_cast<const float*>(ws), grid, nfloats, dw, dw_layout<NetT>(rd));
 }
 
 // ------------------------------------------------------------------ streamed weights
@@ -295,8 +333,8 @@ int launch_bwd(const void* x, const void* const* W, const void* const* h, const 
 constexpr int kStreamEpw = 8;
 
 template <class NetT>
-int launch_stream_fwd(const void* x, const void* const* W, void* out, int64_t M, void* const* hsave,
-                      cudaStream_t st) {
+int launch_stream_fwd(const int* rd, const void* x, const void* const* W, void* out, int64_t M,
+                      void* const* hsave, cudaStream_t st) {
   using Cfg = mlpk::StreamCfg<NetT, kStreamEpw>;
   constexpr int L = NetT::L;
   DevInfo di;
@@ -307,24 +345,24 @@ int launch_stream_fwd(const void* x, const void* const* W, void* out, int64_t M,
   if (M > (int64_t(1) << 31) - 256) return MLPK_ERR_SHAPE;
   mlpk::StreamMaps<L> maps;
   std::memset(&maps, 0, sizeof(maps));
-  if ((rc = make_map_2d(&maps.in, x, Cfg::D0, M, 64, mlpk::kTileM))) return rc;
-  if ((rc = make_map_2d(&maps.out, out, Cfg::DL, M, 64, mlpk::kTileM))) return rc;
+  if ((rc = make_map_2d(&maps.in, x, rd[0], M, 64, mlpk::kTileM))) return rc;
+  if ((rc = make_map_2d(&maps.out, out, rd[L], M, 64, mlpk::kTileM))) return rc;
   int wrc = MLPK_OK;
   mlpk::static_for<0, L>([&](auto lc) {
     constexpr int l = decltype(lc)::value;
     // W_l [d_l][d_{l+1}]: K-chunks of 64 rows read as {64 columns, 64 rows} boxes
-    if (wrc == MLPK_OK)
-      wrc = make_map_2d(&maps.w[l], W[l], NetT::template D<l + 1>(), NetT::template D<l>(), 64,
-                        mlpk::kStreamK);
+    if (wrc == MLPK_OK) wrc = make_map_2d(&maps.w[l], W[l], rd[l + 1], rd[l], 64, mlpk::kStreamK);
   });
   if (wrc) return wrc;
   if (hsave) {
     for (int l = 0; l + 1 < L; ++l) {
       if (!hsave[l]) return MLPK_ERR_NULL;
-      if ((rc = make_map_2d(&maps.save[l], hsave[l], Cfg::H, M, 64, mlpk::kTileM))) return rc;
+      if ((rc = make_map_2d(&maps.save[l], hsave[l], rd[l + 1], M, 64, mlpk::kTileM))) return rc;
     }
   }
   maps.M = static_cast<int>(M);
+  maps.out_cols = rd[L];
+  for (int l = 0; l + 1 < L; ++l) maps.save_cols[l] = maps.hact_cols[l] = rd[l + 1];
   const int64_t tiles = (M + mlpk::kTileM - 1) / mlpk::kTileM;
   const int grid = static_cast<int>(tiles < di.sm_count ? tiles : di.sm_count);
   if (hsave) {
@@ -363,8 +401,9 @@ size_t stream_bwd_workspace(int64_t M, int sm_count) {
 }
 
 template <class NetT>
-int launch_stream_bwd(const void* x, const void* const* W, const void* const* h, const void* g,
-                      void* dx, float* ws, size_t ws_bytes, float* dw, int64_t M, cudaStream_t st) {
+int launch_stream_bwd(const int* rd, const void* x, const void* const* W, const void* const* h,
+                      const void* g, void* dx, float* ws, size_t ws_bytes, float* dw, int64_t M,
+                      cudaStream_t st) {
   using Lay = StreamBwdLayout<NetT>;
   using Chain = mlpk::NetReverse<NetT>;
   using Cfg = mlpk::StreamCfg<Chain, kStreamEpw>;
@@ -385,24 +424,27 @@ int launch_stream_bwd(const void* x, const void* const* W, const void* const* h,
     // 1. data-gradient chain: stage s handles layer l = L-1-s
     mlpk::StreamMaps<L> maps;
     std::memset(&maps, 0, sizeof(maps));
-    if ((rc = make_map_2d(&maps.in, g, Cfg::D0, M, 64, mlpk::kTileM))) return rc;
-    if ((rc = make_map_2d(&maps.out, dx, Cfg::DL, M, 64, mlpk::kTileM))) return rc;
+    if ((rc = make_map_2d(&maps.in, g, rd[L], M, 64, mlpk::kTileM))) return rc;
+    if ((rc = make_map_2d(&maps.out, dx, rd[0], M, 64, mlpk::kTileM))) return rc;
     int wrc = MLPK_OK;
     mlpk::static_for<0, L>([&](auto sc) {
       constexpr int s = decltype(sc)::value;
       constexpr int l = L - 1 - s;
       // W_l [d_l][d_{l+1}] read as W_l^T K-chunks: boxes {64 columns, all d_l rows}
       if (wrc == MLPK_OK)
-        wrc = make_map_2d(&maps.w[s], W[l], NetT::template D<l + 1>(), NetT::template D<l>(), 64,
-                          NetT::template D<l>());
+        wrc = make_map_2d(&maps.w[s], W[l], rd[l + 1], rd[l], 64, NetT::template D<l>());
     });
     if (wrc) return wrc;
     for (int s = 0; s + 1 < L; ++s) {
       const int l = L - 1 - s;
       maps.hact[s] = h[l - 1];
+      maps.hact_cols[s] = rd[l];
+      // dz_l is this library's scratch: the kernel network's width
+      maps.save_cols[s] = Cfg::H;
       if ((rc = make_map_2d(&maps.save[s], dz[l - 1], Cfg::H, M, 64, mlpk::kTileM))) return rc;
     }
     maps.M = static_cast<int>(M);
+    maps.out_cols = rd[0];
     const int64_t tiles = (M + mlpk::kTileM - 1) / mlpk::kTileM;
     const int grid = static_cast<int>(tiles < di.sm_count ? tiles : di.sm_count);
     auto kern = mlpk::mlp_stream_kernel<Chain, kStreamEpw, mlpk::kStreamDgrad, true>;
@@ -418,9 +460,14 @@ int launch_stream_bwd(const void* x, const void* const* W, const void* const* h,
     for (int l = 0; l < L; ++l) {
       const void* a = l == 0 ? x : h[l - 1];
       const void* b = l == L - 1 ? g : dz[l];
-      if (M == 0) a = b = ws;  // never read
-      if ((rc = make_map_2d(&wm.a[l], a, Lay::DA, rows, 64, mlpk::kWgStageRows))) return rc;
-      if ((rc = make_map_2d(&wm.b[l], b, Lay::DB, rows, 64, mlpk::kWgStageRows))) return rc;
+      int acols = rd[l], bcols = l == L - 1 ? rd[L] : Lay::DB;  // dz_l: scratch, full width
+      if (M == 0) {  // never read
+        a = b = ws;
+        acols = Lay::DA;
+        bcols = Lay::DB;
+      }
+      if ((rc = make_map_2d(&wm.a[l], a, acols, rows, 64, mlpk::kWgStageRows))) return rc;
+      if ((rc = make_map_2d(&wm.b[l], b, bcols, rows, 64, mlpk::kWgStageRows))) return rc;
     }
     wm.partials = partials;
     auto kern = mlpk::mlp_wgrad_kernel<L, Lay::DA, Lay::DB>;
@@ -433,23 +480,14 @@ int launch_stream_bwd(const void* x, const void* const* W, const void* const* h,
   return launch_kernel(mlpk::mlp_reduce_kernel,
                        dim3((nfloats + mlpk::kReduceElems - 1) / mlpk::kReduceElems, L, 1),
                        mlpk::kReduceElems * mlpk::kReduceSlices, 0, st,
-                       static_cast<const float*>(partials), P, nfloats, dw);
+                       static_cast<const float*>(partials), P, nfloats, dw, dw_layout<NetT>(rd));
 }
 
 // ------------------------------------------------------------------ dispatch
-template <int... Ds>
-bool shape_is(const mlpk_shape* s) {
-  constexpr int d[] = {Ds...};
-  constexpr int n = sizeof...(Ds);
-  if (s->num_layers != n - 1) return false;
-  for (int i = 0; i < n; ++i)
-    if (s->dims[i] != d[i]) return false;
-  return true;
-}
-
-using Fwd = int (*)(const void*, const void* const*, void*, int64_t, void* const*, cudaStream_t);
-using Bwd = int (*)(const void*, const void* const*, const void* const*, const void*, void*, float*,
-                    size_t, float*, int64_t, cudaStream_t);
+using Fwd = int (*)(const int*, const void*, const void* const*, void*, int64_t, void* const*,
+                   cudaStream_t);
+using Bwd = int (*)(const int*, const void*, const void* const*, const void* const*, const void*, void*,
+                    float*, size_t, float*, int64_t, cudaStream_t);
 using BwdWs = size_t (*)(int64_t, int);
 
 struct ShapeOps {
@@ -466,28 +504,52 @@ bool prefer_pair() {
   return e && e[0] == '1';
 }
 
+// The compiled networks, smallest first.  A caller's network is served by the
+// first one of its depth that covers it: every width at most the compiled
+// width and a multiple of 8 (16-byte rows, the TMA stride rule).  The missing
+// rows and columns are zero-filled by TMA on the way in and clipped on the
+// way out; zero inputs and weights contribute exact zeros, and the padded
+// hidden units feed only zero weight rows, so the caller's outputs and
+// gradients are those of its own network.  The reference's widths are all
+// multiples of 16 (its tl.dot tiles, kernel.py:25-53).
+template <class NetT>
+bool covers(const mlpk_shape* s) {
+  if (s->num_layers != NetT::L) return false;
+  for (int i = 0; i <= NetT::L; ++i)
+    if (s->dims[i] > NetT::dim(i) || s->dims[i] % 8 != 0) return false;
+  return true;
+}
+
+template <class NetT>
+bool exact(const mlpk_shape* s) {
+  if (s->num_layers != NetT::L) return false;
+  for (int i = 0; i <= NetT::L; ++i)
+    if (s->dims[i] != NetT::dim(i)) return false;
+  return true;
+}
+
 ShapeOps pick_ops(const mlpk_shape* s, bool training) {
+  using N64 = Net<64, 64, 64, 64>;
+  using N3 = Net<128, 128, 128, 128>;
+  using N256 = Net<256, 256, 256, 256>;
+  using N5 = Net<32, 64, 64, 64, 64, 16>;
   ShapeOps o;
-  if (shape_is<128, 128, 128, 128>(s)) {
-    using N3 = Net<128, 128, 128, 128>;
-    o.fwd = (prefer_pair() && !training) ? &launch_fwd2<N3, 2, 4> : &launch_fwd<N3, 2, 4>;
-    o.bwd = &launch_bwd<N3>;
-    o.bwd_ws = &bwd_workspace<N3>;
-  } else if (shape_is<32, 64, 64, 64, 64, 16>(s)) {
-    using N5 = Net<32, 64, 64, 64, 64, 16>;
-    o.fwd = &launch_fwd<N5, 2, 4>;
-    o.bwd = &launch_bwd<N5>;
-    o.bwd_ws = &bwd_workspace<N5>;
-  } else if (shape_is<64, 64, 64, 64>(s)) {
-    using N64 = Net<64, 64, 64, 64>;
+  if (covers<N64>(s)) {
     o.fwd = &launch_fwd<N64, 2, 4>;
     o.bwd = &launch_bwd<N64>;
     o.bwd_ws = &bwd_workspace<N64>;
-  } else if (shape_is<256, 256, 256, 256>(s)) {
-    using N256 = Net<256, 256, 256, 256>;
+  } else if (covers<N3>(s)) {
+    o.fwd = (prefer_pair() && !training && exact<N3>(s)) ? &launch_fwd2<N3, 2, 4> : &launch_fwd<N3, 2, 4>;
+    o.bwd = &launch_bwd<N3>;
+    o.bwd_ws = &bwd_workspace<N3>;
+  } else if (covers<N256>(s)) {
     o.fwd = &launch_stream_fwd<N256>;
     o.bwd = &launch_stream_bwd<N256>;
     o.bwd_ws = &stream_bwd_workspace<N256>;
+  } else if (covers<N5>(s)) {
+    o.fwd = &launch_fwd<N5, 2, 4>;
+    o.bwd = &launch_bwd<N5>;
+    o.bwd_ws = &bwd_workspace<N5>;
   }
   return o;
 }
@@ -554,7 +616,7 @@ int mlpk_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* cons
   if (rc) return rc;
   Fwd f = pick_ops(shape, false).fwd;
   if (!f) return MLPK_ERR_UNSUPPORTED;
-  return f(x, W, out, M, nullptr, static_cast<cudaStream_t>(stream));
+  return f(shape->dims, x, W, out, M, nullptr, static_cast<cudaStream_t>(stream));
 }
 
 int mlpk_train_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
@@ -568,7 +630,7 @@ int mlpk_train_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void
   }
   const ShapeOps o = pick_ops(shape, true);
   if (!o.fwd || !o.bwd) return MLPK_ERR_UNSUPPORTED;
-  return o.fwd(x, W, out, M, h_saved, static_cast<cudaStream_t>(stream));
+  return o.fwd(shape->dims, x, W, out, M, h_saved, static_cast<cudaStream_t>(stream));
 }
 
 int64_t mlpk_bwd_workspace_size(const mlpk_shape* shape, int64_t M) {
@@ -594,7 +656,7 @@ int mlpk_bwd(const mlpk_shape* shape, int64_t M, const void* x, const void* cons
   if (workspace_bytes < 0) return MLPK_ERR_SHAPE;
   const ShapeOps o = pick_ops(shape, true);
   if (!o.bwd) return MLPK_ERR_UNSUPPORTED;
-  return o.bwd(x, W, h_saved, grad_out, dx, static_cast<float*>(workspace),
+  return o.bwd(shape->dims, x, W, h_saved, grad_out, dx, static_cast<float*>(workspace),
                static_cast<size_t>(workspace_bytes), dW, M, static_cast<cudaStream_t>(stream));
 }
 

@@ -62,6 +62,15 @@ struct alignas(64) StreamMaps {
   CUtensorMap save[L > 1 ? L - 1 : 1];
   const void* hact[L > 1 ? L - 1 : 1];  // dgrad: saved h_l read by stage s (l = L-1-s)
   int M;
+  // The caller's widths when they are smaller than the kernel's network (a
+  // network served by a larger one): the maps carry the caller's extents, so
+  // TMA loads fill the missing rows / columns with zeros; stores skip every
+  // 64-column chunk that starts at or past these widths (partially covered
+  // chunks are clipped by TMA); hact rows have hact_cols columns and the
+  // columns past them read as zero.
+  int out_cols;
+  int save_cols[L > 1 ? L - 1 : 1];
+  int hact_cols[L > 1 ? L - 1 : 1];
 };
 
 template <class ChainT, int EPW>
@@ -109,13 +118,16 @@ struct StreamCfg {
 
 // Loads this thread's saved activations of stripe j of one data-gradient
 // stage: stripe j of column group grp covers columns 32*(j*NG + grp) .. +31
-// (64 bytes).  Rows past M (hrow == nullptr) get zeros.
+// (64 bytes).  Rows past M (hrow == nullptr) and columns at or past the row's
+// width hcols (a multiple of 8) get zeros.
 template <int NG>
-__device__ __forceinline__ void dgrad_load_h(uint4 (&hv)[4], const uint8_t* hrow, int grp, int j) {
+__device__ __forceinline__ void dgrad_load_h(uint4 (&hv)[4], const uint8_t* hrow, int grp, int j,
+                                             int hcols) {
   const int col = 32 * (j * NG + grp);
 #pragma unroll
   for (int v = 0; v < 4; ++v)
-    hv[v] = hrow ? __ldg(reinterpret_cast<const uint4*>(hrow + 2 * col) + v) : make_uint4(0, 0, 0, 0);
+    hv[v] = (hrow && col + 8 * v < hcols) ? __ldg(reinterpret_cast<const uint4*>(hrow + 2 * col) + v)
+                                          : make_uint4(0, 0, 0, 0);
 }
 
 // Data-gradient stage epilogue of one warp (mirrors hidden_job): dz = dh *
@@ -126,7 +138,7 @@ __device__ __forceinline__ void dgrad_load_h(uint4 (&hv)[4], const uint8_t* hrow
 // stripe's h is loaded two stripes ahead, into the registers just consumed.
 template <int N, int NG, int SPC, bool SAVE>
 __device__ __forceinline__ void dgrad_job(uint32_t tbuf, int grp, uint32_t chunk_bar0, uint4 (&hv)[2][4],
-                                          const uint8_t* hrow, uint32_t stage_base, uint32_t row) {
+                                          const uint8_t* hrow, int hcols, uint32_t stage_base, uint32_t row) {
   constexpr int SUBS = N / (32 * NG);
   static_assert(SUBS % SPC == 0, "stripes per chunk must divide the stripes per group");
   uint32_t a[32];
@@ -139,7 +151,7 @@ __device__ __forceinline__ void dgrad_job(uint32_t tbuf, int grp, uint32_t chunk
     uint4(&hc)[4] = hv[j & 1];
     const uint32_t hw[16] = {hc[0].x, hc[0].y, hc[0].z, hc[0].w, hc[1].x, hc[1].y, hc[1].z, hc[1].w,
                              hc[2].x, hc[2].y, hc[2].z, hc[2].w, hc[3].x, hc[3].y, hc[3].z, hc[3].w};
-    if (j + 2 < SUBS) dgrad_load_h<NG>(hc, hrow, grp, j + 2);
+    if (j + 2 < SUBS) dgrad_load_h<NG>(hc, hrow, grp, j + 2, hcols);
     uint32_t w[16];
 #pragma unroll
     for (int p = 0; p < 16; ++p) {
@@ -253,8 +265,8 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
 #pragma unroll 1
             for (int s = 0; s + 1 < L; ++s)
               prefetch_l2_bulk(static_cast<const uint8_t*>(maps.hact[s]) +
-                                   static_cast<size_t>(tt) * kTileM * Cfg::H * 2,
-                               static_cast<uint32_t>(rows) * Cfg::H * 2);
+                                   static_cast<size_t>(tt) * kTileM * maps.hact_cols[s] * 2,
+                               static_cast<uint32_t>(rows) * maps.hact_cols[s] * 2);
           }
         }
         static_for<0, L>([&](auto sc) {
@@ -386,11 +398,13 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
         const int g = i * L + s;
         uint4 hv[2][4];
         const uint8_t* hrow = nullptr;
+        int hcols = H;
         if constexpr (MODE == kStreamDgrad) {
-          hrow = valid ? static_cast<const uint8_t*>(maps.hact[s]) + static_cast<size_t>(grow) * H * 2
+          hcols = maps.hact_cols[s];
+          hrow = valid ? static_cast<const uint8_t*>(maps.hact[s]) + static_cast<size_t>(grow) * hcols * 2
                        : nullptr;
-          dgrad_load_h<NG>(hv[0], hrow, grp, 0);
-          if (H / (32 * NG) > 1) dgrad_load_h<NG>(hv[1], hrow, grp, 1);
+          dgrad_load_h<NG>(hv[0], hrow, grp, 0, hcols);
+          if (H / (32 * NG) > 1) dgrad_load_h<NG>(hv[1], hrow, grp, 1, hcols);
         }
         ok = __all_sync(0xffffffffu,
                         mbar_wait(bar_acc_full(g & 1), (g >> 1) & 1, abort_flag, kDevTimeoutEpi));
@@ -414,7 +428,7 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
         if constexpr (MODE == kStreamFwd)
           hidden_job<H, NG, Cfg::SPC, false, SAVE ? 2 : 0>(t_buf, grp, bar_chunk(0), nullptr, s_o, row);
         else
-          dgrad_job<H, NG, Cfg::SPC, SAVE>(t_buf, grp, bar_chunk(0), hv, hrow, s_o, row);
+          dgrad_job<H, NG, Cfg::SPC, SAVE>(t_buf, grp, bar_chunk(0), hv, hrow, hcols, s_o, row);
         if constexpr (SAVE) {
           fence_proxy_async_smem();
           __syncwarp();
@@ -424,7 +438,7 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
             if (ok) {
 #pragma unroll
               for (int c = 0; c < H / 64; ++c)
-                tma_store_2d(&maps.save[s], s_o + c * kTileM * 128, c * 64, t * kTileM);
+                if (c * 64 < maps.save_cols[s]) tma_store_2d(&maps.save[s], s_o + c * kTileM * 128, c * 64, t * kTileM);
               bulk_commit_group();
             }
           }
@@ -462,7 +476,7 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
         if (leader && ok) {
 #pragma unroll
           for (int c = 0; c < Cfg::DL / 64; ++c)
-            tma_store_2d(&maps.out, s_o + c * kTileM * 128, c * 64, t * kTileM);
+            if (c * 64 < maps.out_cols) tma_store_2d(&maps.out, s_o + c * kTileM * 128, c * 64, t * kTileM);
           bulk_commit_group();
         }
       }

@@ -29,6 +29,13 @@ CASES = {
     "w256_M384": ((256, 256, 256, 256), 384, "normal", 4, 1.0, 0),
     # narrow 3-layer network D=H=OUT=64
     "d64_M200": ((64, 64, 64, 64), 200, "normal", 16, 1.0, 0),
+    # mixed widths the reference's tiles accept (kernel.py:25-53: BK1 =
+    # min(64, K1), BK2 = min(128, N1), BK3 = min(128, N2), BN3 = min(128, N3)
+    # dividing their dims); served here by a larger compiled network
+    "mixed_32_128_64_16_M300": ((32, 128, 64, 16), 300, "normal", 17, 1.0, 0),
+    "mixed_128_64_32_128_M200": ((128, 64, 32, 128), 200, "normal", 18, 1.0, 0),
+    "mixed_16_32_64_32_M129": ((16, 32, 64, 32), 129, "normal", 19, 1.0, 0),
+    "mixed_192_256_128_256_M130": ((192, 256, 128, 256), 130, "normal", 20, 1.0, 0),
 }
 
 

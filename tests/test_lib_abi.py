@@ -43,10 +43,23 @@ def test_status_strings(built_lib):
     ((128, 128, 128, 128), True),
     ((32, 64, 64, 64, 64, 16), True),
     ((64, 64, 64, 64), True),
-    ((128, 96, 128, 128), False),
+    ((256, 256, 256, 256), True),
+    # served by a larger compiled network: widths multiples of 8, at most the
+    # compiled widths of the same depth, hidden widths free
+    ((128, 96, 128, 128), True),
+    ((8, 8, 8, 8), True),
+    ((200, 136, 256, 72), True),
+    ((16, 32, 48, 64, 40, 8), True),
+    # not served
+    ((128, 100, 128, 128), False),   # 100 is not a multiple of 8
+    ((264, 256, 256, 256), False),   # wider than every 3-layer kernel
+    ((64, 64, 64, 64, 64, 64), False),  # 5 layers wider than 32-64-64-64-64-16
+    ((64, 64, 64, 64, 64), False),   # 4 layers: no kernel of that depth
+    ((128, 128), False),
 ])
 def test_shape_supported(built_lib, dims, ok):
     assert _lib.shape_supported(dims) == ok
+    assert _lib.train_supported(dims) == ok
 
 
 def test_fwd_rejects_bad_arguments_without_touching_the_device(built_lib):
@@ -65,7 +78,7 @@ def test_fwd_rejects_bad_arguments_without_touching_the_device(built_lib):
     # unsupported shape
     bad = _lib.MlpkShape()
     bad.num_layers = 3
-    for i, d in enumerate((128, 96, 128, 128)):
+    for i, d in enumerate((128, 100, 128, 128)):
         bad.dims[i] = d
     assert lib.mlpk_fwd(ctypes.byref(bad), 16, 256, w, 512, None) == 2
     # zero layers
