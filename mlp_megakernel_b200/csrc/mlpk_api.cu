@@ -533,6 +533,9 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
   using N3 = Net<128, 128, 128, 128>;
   using N256 = Net<256, 256, 256, 256>;
   using N5 = Net<32, 64, 64, 64, 64, 16>;
+  using N5w64 = Net<64, 64, 64, 64, 64, 64>;
+  using N5w128 = Net<128, 128, 128, 128, 128, 128>;
+  using N5w256 = Net<256, 256, 256, 256, 256, 256>;
   ShapeOps o;
   if (covers<N64>(s)) {
     o.fwd = &launch_fwd<N64, 2, 4>;
@@ -550,6 +553,18 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.fwd = &launch_fwd<N5, 2, 4>;
     o.bwd = &launch_bwd<N5>;
     o.bwd_ws = &bwd_workspace<N5>;
+  } else if (covers<N5w64>(s)) {
+    o.fwd = &launch_fwd<N5w64, 2, 4>;
+    o.bwd = &launch_bwd<N5w64>;
+    o.bwd_ws = &bwd_workspace<N5w64>;
+  } else if (covers<N5w128>(s)) {
+    o.fwd = &launch_stream_fwd<N5w128>;
+    o.bwd = &launch_stream_bwd<N5w128>;
+    o.bwd_ws = &stream_bwd_workspace<N5w128>;
+  } else if (covers<N5w256>(s)) {
+    o.fwd = &launch_stream_fwd<N5w256>;
+    o.bwd = &launch_stream_bwd<N5w256>;
+    o.bwd_ws = &stream_bwd_workspace<N5w256>;
   }
   return o;
 }

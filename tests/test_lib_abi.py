@@ -50,10 +50,13 @@ def test_status_strings(built_lib):
     ((8, 8, 8, 8), True),
     ((200, 136, 256, 72), True),
     ((16, 32, 48, 64, 40, 8), True),
+    ((64, 64, 64, 64, 64, 64), True),
+    ((96, 128, 64, 128, 112, 16), True),
+    ((256, 256, 256, 256, 256, 256), True),
     # not served
     ((128, 100, 128, 128), False),   # 100 is not a multiple of 8
     ((264, 256, 256, 256), False),   # wider than every 3-layer kernel
-    ((64, 64, 64, 64, 64, 64), False),  # 5 layers wider than 32-64-64-64-64-16
+    ((64, 64, 64, 64, 64, 264), False),  # wider than every 5-layer kernel
     ((64, 64, 64, 64, 64), False),   # 4 layers: no kernel of that depth
     ((128, 128), False),
 ])

@@ -1,7 +1,8 @@
 """GPU parity for networks served by a larger compiled network (zero padding
 through TMA): the caller's widths need only be multiples of 8 and at most the
 compiled widths of the same depth (64^3, 128^3, 256^3 for 3 layers;
-32-64-64-64-64-16 for 5), hidden widths may differ from each other.
+32-64-64-64-64-16, 64^5, 128^5 and 256^5 for 5), hidden widths may differ from
+each other.
 
 The reference's kernel accepts any widths its tl.dot tiles divide
 (kernel.py:25-53, kernel.py:130-156) and its modules take D, H, out_features
@@ -34,6 +35,12 @@ SHAPES = [
     ((256, 160, 200, 256), "256^3"),
     ((16, 32, 48, 64, 40, 8), "5-layer"),
     ((32, 64, 64, 64, 64, 16), "5-layer (exact)"),
+    ((64, 64, 64, 64, 64, 64), "5-layer 64-wide (exact)"),
+    ((48, 64, 32, 64, 56, 24), "5-layer 64-wide"),
+    ((128, 128, 128, 128, 128, 128), "5-layer 128-wide streamed (exact)"),
+    ((96, 128, 64, 128, 112, 16), "5-layer 128-wide streamed"),
+    ((256, 256, 256, 256, 256, 256), "5-layer 256-wide streamed (exact)"),
+    ((200, 136, 256, 72, 128, 64), "5-layer 256-wide streamed"),
 ]
 
 
@@ -124,8 +131,9 @@ def test_padded_network_equals_compiled_network_exactly():
 @pytest.mark.parametrize("cls", [FusedMLPSoftplus, FusedMLPSoftplusWN])
 @pytest.mark.parametrize("kw", [dict(D=48, H=96, out_features=24),
                                 dict(D=64, H=200, out_features=40),
-                                dict(D=16, H=48, out_features=8, num_layers=5)],
-                         ids=["3L-96", "3L-200", "5L-48"])
+                                dict(D=16, H=48, out_features=8, num_layers=5),
+                                dict(D=64, H=160, out_features=32, num_layers=5)],
+                         ids=["3L-96", "3L-200", "5L-48", "5L-160"])
 def test_modules_with_other_widths(cls, kw):
     """The reference's modules take any D, H, out_features (README.md:58-70):
     gradients through autograd against torch's own autograd in fp32 on the same
@@ -144,7 +152,6 @@ def test_modules_with_other_widths(cls, kw):
     else:
         ws = []
         for l in range(len(model.dims) - 1):
-            v = model.v(l)
             off_v = sum(a * b for a, b in zip(model.dims[:l], model.dims[1:l + 1]))
             off_g = sum(model.dims[1:l + 1])
             a, b = model.dims[l], model.dims[l + 1]
