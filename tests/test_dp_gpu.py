@@ -2,7 +2,8 @@
 config 4 shape) trained on row shards with its process group gives the
 full-batch gradients of one GPU, identical on both ranks -- with the dW sum
 done by this library's NVLink peer-memory kernel and by NCCL; and the
-peer-memory reducer itself over several steps (both slots) against the exact
+peer-memory reducer itself over several consecutive steps (the slot is
+rewritten each step; the device-side step number advances) against the exact
 sum, bitwise equal on every rank.
 
 Needs two sm_100 GPUs; skipped otherwise.  Two processes are spawned, one per
@@ -117,7 +118,7 @@ def _reducer_worker(rank, port, out_dir):
         n = 49152  # the 3L128 weight-gradient length
         red = PeerGradReducer(n)
         out = torch.empty(n, device="cuda")
-        for step in range(5):  # both slots, twice
+        for step in range(5):  # the slot rewritten, the step number advanced
             gen = torch.Generator().manual_seed(1000 * step + rank)
             red.local_buffer(out).copy_(torch.randn(n, generator=gen).cuda())
             red.reduce(red.local_buffer(out), out)
