@@ -13,7 +13,10 @@ collective, so the scaling is weak and ``value`` = N*M*K / max-over-ranks time.
 Timing: W untimed warm-up steps, then K steps between CUDA events on the
 launching stream, bracketed by a barrier and a device synchronize; inputs
 (1 GiB x, 1 GiB out) are larger than L2, so no flush is needed.  SM clocks and
-throttle reasons are sampled through NVML during the timed region.
+throttle reasons are sampled through NVML during the timed region.  ``e2e``
+is the same forward from pinned host rows to pinned host results through
+``fused_mlp_fwd_host`` (chunked; the copies in and out overlap each other and
+the forward), all bytes crossing the host link every step.
 
 The same JSON line carries the training steps (forward + backward through
 the C ABI on preallocated buffers, replayed as one CUDA graph per step, dW
@@ -232,7 +235,7 @@ def run_reference(args):
 def run_mlpk(args):
     import torch
 
-    from mlp_megakernel_b200 import _lib, fused_mlp_fwd
+    from mlp_megakernel_b200 import _lib, fused_mlp_fwd, fused_mlp_fwd_host
     from mlp_megakernel_b200.synthetic import make_weights, make_x
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -283,15 +286,14 @@ def run_mlpk(args):
     if status != 0:
         raise RuntimeError(f"device status {status} after the timed region")
 
-    # e2e through the public API: pinned host x -> device -> fused_mlp_fwd -> pinned host out
+    # e2e through the public API for host-resident rows: pinned host x ->
+    # fused_mlp_fwd_host (chunks copied in, run and copied out, the copies of
+    # neighbouring chunks overlapping) -> pinned host out
     xh = x.cpu().pin_memory()
     oh = torch.empty((M, DIMS[-1]), dtype=torch.float16, pin_memory=True)
-    xd = torch.empty_like(x)
 
     def e2e_step():
-        xd.copy_(xh, non_blocking=True)
-        out = fused_mlp_fwd(xd, *ws)
-        oh.copy_(out, non_blocking=True)
+        fused_mlp_fwd_host(xh, *ws, out=oh)
 
     e2e_step()
     torch.cuda.synchronize()
@@ -372,7 +374,10 @@ def run_mlpk(args):
             "h2d_bytes_per_step": M * DIMS[0] * 2,
             "d2h_bytes_per_step": M * DIMS[-1] * 2,
             "steps": args.e2e_steps,
-            "api": "mlp_megakernel_b200.fused_mlp_fwd with pinned host buffers",
+            "api": "mlp_megakernel_b200.fused_mlp_fwd_host: pinned host rows streamed through the "
+                   "GPU in 131,072-row chunks (copy in, forward, copy out of neighbouring chunks "
+                   "overlap); every byte of x crosses to the device and every byte of out back, "
+                   "each step",
         },
         "gpu_launches": args.steps,
         "clocks": clocks,

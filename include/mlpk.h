@@ -128,6 +128,27 @@ int mlpk_bwd_noalloc(const mlpk_shape* shape, int64_t M, const void* x, const vo
                      const void* const* h_saved, const void* grad_out, void* dx, float* dW,
                      mlpk_stream_t stream);
 
+/* ---- Inference on host-resident rows.  No counterpart in the reference (its
+ * forward takes device tensors, kernel.py:130-156): for serving batches that
+ * live in host memory.  out_host[M, dL] = MLP(x_host[M, d0]); x_host and
+ * out_host are host buffers (page-locked for the copies to overlap), W the
+ * device weights as for mlpk_fwd.  The rows stream through the GPU in chunks
+ * of chunk_rows (0 = MLPK_FWD_HOST_CHUNK_ROWS): chunk k+1 is copied in and
+ * chunk k-1 copied out (one cudaMemcpyAsync each, on two copy streams of the
+ * library) while chunk k runs the fused forward on `stream`, through
+ * MLPK_FWD_HOST_BUFFERS device buffers of each kind in `workspace`
+ * (mlpk_fwd_host_workspace_size bytes).  Asynchronous: the results are in
+ * out_host once `stream` has reached the point of the call (the copy streams
+ * wait for `stream` at entry and `stream` waits for the last copy out).  The
+ * copy streams and events are per host thread and device; concurrent calls
+ * from one host thread on different streams are serialised by them. */
+#define MLPK_FWD_HOST_CHUNK_ROWS 131072
+#define MLPK_FWD_HOST_BUFFERS 3
+int64_t mlpk_fwd_host_workspace_size(const mlpk_shape* shape, int64_t chunk_rows);
+int mlpk_fwd_host(const mlpk_shape* shape, int64_t M, const void* x_host, const void* const* W,
+                  void* out_host, int64_t chunk_rows, void* workspace, int64_t workspace_bytes,
+                  mlpk_stream_t stream);
+
 /* Reads (and optionally clears) the device-side status word of the current
  * device: bit flags set by bounded waits that expired.  Synchronises. */
 int mlpk_device_status(int clear, int* status_out);

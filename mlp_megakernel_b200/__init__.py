@@ -5,7 +5,8 @@ forward ``_fused_mlp_fwd`` / ``ModelNew`` (kernel.py:130-180) and the module API
 ``FusedMLPSoftplus`` / ``FusedMLPSoftplusWN`` (README.md:58-70).  All compute
 runs in hand-written CUDA kernels (libmlpk.so, C ABI in include/mlpk.h).
 """
-from .functional import ModelNew, _fused_mlp_fwd, fused_mlp_fwd  # noqa: F401
+from .functional import ModelNew, _fused_mlp_fwd, fused_mlp_fwd, fused_mlp_fwd_host  # noqa: F401
 from .modules import FusedMLPSoftplus, FusedMLPSoftplusWN  # noqa: F401
 
-__all__ = ["fused_mlp_fwd", "_fused_mlp_fwd", "ModelNew", "FusedMLPSoftplus", "FusedMLPSoftplusWN"]
+__all__ = ["fused_mlp_fwd", "fused_mlp_fwd_host", "_fused_mlp_fwd", "ModelNew", "FusedMLPSoftplus",
+           "FusedMLPSoftplusWN"]

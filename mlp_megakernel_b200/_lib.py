@@ -61,7 +61,11 @@ SIGNATURES = {
     "mlpk_peer_close": (ctypes.c_int, [ctypes.c_void_p]),
     "mlpk_peer_free": (ctypes.c_int, [ctypes.c_void_p]),
     "mlpk_peer_allreduce": (ctypes.c_int, [_VPP, ctypes.c_int, ctypes.c_int, ctypes.c_int64, _vp, _vp]),
+    "mlpk_fwd_host_workspace_size": (ctypes.c_int64, [_SHAPE_P, ctypes.c_int64]),
+    "mlpk_fwd_host": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _vp, ctypes.c_int64, _vp,
+                                     ctypes.c_int64, _vp]),
 }
+FWD_HOST_CHUNK_ROWS = 131072
 PEER_HANDLE_BYTES = 64
 PEER_MAX_RANKS = 8
 

@@ -785,6 +785,133 @@ int mlpk_bwd_noalloc(const mlpk_shape* shape, int64_t M, const void* x, const vo
                   static_cast<int64_t>(MLPK_BWD_NOALLOC_SCRATCH_BYTES), dW, stream);
 }
 
+// ------------------------------------------------------------------ host-resident rows
+namespace {
+constexpr int kPipeBufs = MLPK_FWD_HOST_BUFFERS;
+
+// Copy streams and events of one host thread on one device (created on first
+// use, kept for the thread's lifetime).
+struct HostPipe {
+  bool ready = false;
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t start = nullptr;
+  cudaEvent_t in_ready[kPipeBufs] = {};   // chunk copied into x buffer b
+  cudaEvent_t comp_done[kPipeBufs] = {};  // forward of buffer b done (x_b free, out_b written)
+  cudaEvent_t out_done[kPipeBufs] = {};   // out buffer b copied out (free again)
+};
+
+int host_pipe(int dev, HostPipe** out) {
+  thread_local HostPipe pipes[kMaxDevices];
+  HostPipe& p = pipes[dev];
+  if (!p.ready) {
+    int rc;
+    if ((rc = cuda_status(cudaStreamCreateWithFlags(&p.h2d, cudaStreamNonBlocking))) ||
+        (rc = cuda_status(cudaStreamCreateWithFlags(&p.d2h, cudaStreamNonBlocking))) ||
+        (rc = cuda_status(cudaEventCreateWithFlags(&p.start, cudaEventDisableTiming))))
+      return rc;
+    for (int b = 0; b < kPipeBufs; ++b)
+      if ((rc = cuda_status(cudaEventCreateWithFlags(&p.in_ready[b], cudaEventDisableTiming))) ||
+          (rc = cuda_status(cudaEventCreateWithFlags(&p.comp_done[b], cudaEventDisableTiming))) ||
+          (rc = cuda_status(cudaEventCreateWithFlags(&p.out_done[b], cudaEventDisableTiming))))
+        return rc;
+    p.ready = true;
+  }
+  *out = &p;
+  return MLPK_OK;
+}
+
+size_t host_chunk_bytes(int64_t rows, int width) {
+  return (static_cast<size_t>(rows) * width * 2 + 255) / 256 * 256;
+}
+}  // namespace
+
+int64_t mlpk_fwd_host_workspace_size(const mlpk_shape* shape, int64_t chunk_rows) {
+  if (check_shape(shape) != MLPK_OK || chunk_rows < 0) return -1;
+  if (chunk_rows == 0) chunk_rows = MLPK_FWD_HOST_CHUNK_ROWS;
+  const int L = shape->num_layers;
+  return static_cast<int64_t>(kPipeBufs * (host_chunk_bytes(chunk_rows, shape->dims[0]) +
+                                           host_chunk_bytes(chunk_rows, shape->dims[L])));
+}
+
+int mlpk_fwd_host(const mlpk_shape* shape, int64_t M, const void* x_host, const void* const* W,
+                  void* out_host, int64_t chunk_rows, void* workspace, int64_t workspace_bytes,
+                  mlpk_stream_t stream) {
+  int rc = check_shape(shape);
+  if (rc) return rc;
+  if (M < 0 || chunk_rows < 0) return MLPK_ERR_SHAPE;
+  if (chunk_rows == 0) chunk_rows = MLPK_FWD_HOST_CHUNK_ROWS;
+  if (!W) return MLPK_ERR_NULL;
+  for (int l = 0; l < shape->num_layers; ++l) {
+    if (!W[l]) return MLPK_ERR_NULL;
+    if (!aligned16(W[l])) return MLPK_ERR_ALIGN;
+  }
+  const Fwd f = pick_ops(shape, false).fwd;
+  if (!f) return MLPK_ERR_UNSUPPORTED;
+  if (M == 0) return MLPK_OK;
+  if (!x_host || !out_host || !workspace) return MLPK_ERR_NULL;
+  if (!aligned16(workspace)) return MLPK_ERR_ALIGN;
+  if (workspace_bytes < mlpk_fwd_host_workspace_size(shape, chunk_rows)) return MLPK_ERR_SHAPE;
+  DevInfo di;
+  int dev = 0;
+  if ((rc = current_device_info(&di, &dev)) != MLPK_OK) return rc;
+  HostPipe* p = nullptr;
+  if ((rc = host_pipe(dev, &p)) != MLPK_OK) return rc;
+
+  const int L = shape->num_layers;
+  const int d0 = shape->dims[0], dL = shape->dims[L];
+  const size_t xb = host_chunk_bytes(chunk_rows, d0), ob = host_chunk_bytes(chunk_rows, dL);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  auto xbuf = [&](int b) { return ws + b * xb; };
+  auto obuf = [&](int b) { return ws + kPipeBufs * xb + b * ob; };
+  const auto* xh = static_cast<const uint8_t*>(x_host);
+  auto* oh = static_cast<uint8_t*>(out_host);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  // The copy streams start after the work already queued on `stream` (which
+  // may still use the workspace or produce the weights).
+  if ((rc = cuda_status(cudaEventRecord(p->start, st))) ||
+      (rc = cuda_status(cudaStreamWaitEvent(p->h2d, p->start, 0))) ||
+      (rc = cuda_status(cudaStreamWaitEvent(p->d2h, p->start, 0))))
+    return rc;
+  const int64_t nchunks = (M + chunk_rows - 1) / chunk_rows;
+  auto rows_of = [&](int64_t k) { return k + 1 < nchunks ? chunk_rows : M - k * chunk_rows; };
+  // copy in chunk k (its buffer is free once the forward of chunk k - B read it)
+  auto copy_in = [&](int64_t k) {
+    const int b = static_cast<int>(k % kPipeBufs);
+    int r = MLPK_OK;
+    if (k >= kPipeBufs) r = cuda_status(cudaStreamWaitEvent(p->h2d, p->comp_done[b], 0));
+    if (!r)
+      r = cuda_status(cudaMemcpyAsync(xbuf(b), xh + static_cast<size_t>(k * chunk_rows) * d0 * 2,
+                                      static_cast<size_t>(rows_of(k)) * d0 * 2, cudaMemcpyHostToDevice,
+                                      p->h2d));
+    if (!r) r = cuda_status(cudaEventRecord(p->in_ready[b], p->h2d));
+    return r;
+  };
+  for (int64_t k = 0; k < nchunks && k < kPipeBufs - 1; ++k)
+    if ((rc = copy_in(k))) return rc;
+  for (int64_t k = 0; k < nchunks; ++k) {
+    const int b = static_cast<int>(k % kPipeBufs);
+    // keep B - 1 chunks of input in flight ahead of the forward
+    if (k + kPipeBufs - 1 < nchunks && (rc = copy_in(k + kPipeBufs - 1))) return rc;
+    // forward of chunk k: its input has arrived and its output buffer is free
+    if ((rc = cuda_status(cudaStreamWaitEvent(st, p->in_ready[b], 0)))) return rc;
+    if (k >= kPipeBufs && (rc = cuda_status(cudaStreamWaitEvent(st, p->out_done[b], 0)))) return rc;
+    if ((rc = f(shape->dims, xbuf(b), W, obuf(b), rows_of(k), nullptr, st))) return rc;
+    if ((rc = cuda_status(cudaEventRecord(p->comp_done[b], st)))) return rc;
+    // copy out chunk k
+    if ((rc = cuda_status(cudaStreamWaitEvent(p->d2h, p->comp_done[b], 0))) ||
+        (rc = cuda_status(cudaMemcpyAsync(oh + static_cast<size_t>(k * chunk_rows) * dL * 2, obuf(b),
+                                          static_cast<size_t>(rows_of(k)) * dL * 2, cudaMemcpyDeviceToHost,
+                                          p->d2h))) ||
+        (rc = cuda_status(cudaEventRecord(p->out_done[b], p->d2h))))
+      return rc;
+  }
+  // `stream` reaches this point only after the last copy out (and, through
+  // it, every earlier one: the copy-out stream is in order)
+  const int last = static_cast<int>((nchunks - 1) % kPipeBufs);
+  return cuda_status(cudaStreamWaitEvent(st, p->out_done[last], 0));
+}
+
 int mlpk_device_status(int clear, int* status_out) {
   int v = 0;
   int rc = cuda_status(cudaMemcpyFromSymbol(&v, mlpk::g_device_status, sizeof(int)));

@@ -109,6 +109,60 @@ def _cast(lib, t: torch.Tensor, dtype, stream) -> torch.Tensor:
     return dst
 
 
+@torch.compiler.disable
+def fused_mlp_fwd_host(x: torch.Tensor, *weights: torch.Tensor, out: torch.Tensor = None,
+                       chunk_rows: int = _lib.FWD_HOST_CHUNK_ROWS) -> torch.Tensor:
+    """The fused forward on rows that live in HOST memory (serving from host
+    buffers; no counterpart in the reference, whose forward takes device
+    tensors).
+
+    ``x`` is a CPU fp16 tensor ``[M, in_features]`` (page-locked -- e.g.
+    ``.pin_memory()`` -- for the copies to overlap), the weights are fp16 CUDA
+    tensors; returns a CPU fp16 tensor ``[M, out_features]`` (``out``, if
+    given: contiguous, CPU, fp16), complete when the call returns.  The rows
+    stream through the GPU in chunks of ``chunk_rows``: the copy in of the next
+    chunk and the copy out of the previous one overlap the forward of the
+    current one (the host link runs both directions at once), on the current
+    CUDA stream of the weights' device (mlpk_fwd_host).
+    """
+    if not isinstance(x, torch.Tensor) or x.dim() != 2 or x.is_cuda:
+        raise ValueError("x must be a 2-D CPU tensor [M, in_features] (host rows)")
+    if x.dtype != torch.float16:
+        raise TypeError(f"fused_mlp_fwd_host takes fp16 rows; got {x.dtype}")
+    if not weights or not all(w.is_cuda for w in weights):
+        raise ValueError("the weights must be CUDA tensors")
+    dev = weights[0].device
+    dims = [x.shape[1]]
+    for i, w in enumerate(weights):
+        if w.dim() != 2 or w.dtype != torch.float16 or w.device != dev or w.shape[0] != dims[-1]:
+            raise ValueError(f"weight {i} must be a 2-D fp16 [{dims[-1]}, out] tensor on {dev}")
+        dims.append(w.shape[1])
+    x = x.contiguous()
+    ws = [_aligned(w) for w in weights]
+    M = x.shape[0]
+    if out is None:
+        out = torch.empty((M, dims[-1]), dtype=torch.float16, pin_memory=x.is_pinned())
+    elif (out.shape != (M, dims[-1]) or out.dtype != torch.float16 or out.is_cuda
+          or not out.is_contiguous()):
+        raise ValueError(f"out must be a contiguous CPU [{M}, {dims[-1]}] fp16 tensor")
+    if M == 0:
+        return out
+    lib = _lib.lib()
+    shape = _lib.shape_struct(dims)
+    with torch.cuda.device(dev):
+        wsb = lib.mlpk_fwd_host_workspace_size(ctypes.byref(shape), chunk_rows)
+        if wsb < 0:
+            raise ValueError(f"invalid chunk_rows {chunk_rows}")
+        work = torch.empty(int(wsb), dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        rc = lib.mlpk_fwd_host(ctypes.byref(shape), M, x.data_ptr(), _lib.ptr_array([w.data_ptr() for w in ws]),
+                               out.data_ptr(), chunk_rows, work.data_ptr(), int(work.numel()),
+                               stream.cuda_stream)
+        _lib.check("mlpk_fwd_host", rc)
+        stream.synchronize()  # the rows are in `out` once the stream got there
+    return out
+
+
 def _fused_mlp_fwd(x, w1, w2, w3):
     """3-layer inference forward -- drop-in for kernel.py:130-156."""
     return fused_mlp_fwd(x, w1, w2, w3)

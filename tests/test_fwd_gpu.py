@@ -10,7 +10,7 @@ import pytest
 import torch
 
 import oracle
-from mlp_megakernel_b200 import ModelNew, _fused_mlp_fwd, fused_mlp_fwd
+from mlp_megakernel_b200 import ModelNew, _fused_mlp_fwd, fused_mlp_fwd, fused_mlp_fwd_host
 from mlp_megakernel_b200 import _lib
 from mlp_megakernel_b200.synthetic import make_inputs, make_weights, make_x
 from tests.golden_io import case_names, load_case
@@ -222,3 +222,38 @@ def test_fwd_rejects_other_dtypes():
     x, ws = make_inputs("3L128", 64)
     with pytest.raises(TypeError):
         fused_mlp_fwd(x.cuda().bfloat16(), *[w.cuda().bfloat16() for w in ws])
+
+
+@pytest.mark.parametrize("dims,M,chunk,pinned", [
+    ((128, 128, 128, 128), 1, 0, True),
+    ((128, 128, 128, 128), 300, 128, True),
+    ((128, 128, 128, 128), 2 * 131072 + 5, 0, True),
+    ((128, 128, 128, 128), 1 << 20, 65536, True),
+    ((128, 128, 128, 128), 5000, 1000, False),
+    ((32, 64, 64, 64, 64, 16), 70001, 8192, True),
+    ((48, 128, 80, 24), 9999, 1024, True),
+])
+def test_fwd_host_rows_equal_device_forward(dims, M, chunk, pinned):
+    """Host-resident rows streamed through the GPU in chunks give bitwise the
+    device forward's result (every chunk runs the same kernel on its rows)."""
+    x = make_x(M, dims[0], "normal", 21)
+    ws = [w.cuda() for w in make_weights(dims, seed=22)]
+    ref = fused_mlp_fwd(x.cuda(), *ws).cpu()
+    xh = x.pin_memory() if pinned else x
+    out = fused_mlp_fwd_host(xh, *ws, chunk_rows=chunk)
+    assert not out.is_cuda and out.shape == (M, dims[-1])
+    assert torch.equal(out, ref)
+    buf = torch.full((M, dims[-1]), float("nan"), dtype=torch.float16)
+    assert fused_mlp_fwd_host(xh, *ws, out=buf, chunk_rows=chunk) is buf and torch.equal(buf, ref)
+
+
+def test_fwd_host_rows_errors():
+    x, ws = make_inputs("3L128", 64)
+    wg = _gpu(ws)
+    with pytest.raises(ValueError):
+        fused_mlp_fwd_host(x.cuda(), *wg)   # device rows: use fused_mlp_fwd
+    with pytest.raises(TypeError):
+        fused_mlp_fwd_host(x.float(), *wg)
+    with pytest.raises(ValueError):
+        fused_mlp_fwd_host(x, *ws)          # CPU weights
+    assert fused_mlp_fwd_host(x[:0], *wg).shape == (0, 128)

@@ -88,3 +88,24 @@ def test_fwd_rejects_bad_arguments_without_touching_the_device(built_lib):
     z = _lib.MlpkShape()
     z.num_layers = 0
     assert lib.mlpk_fwd(ctypes.byref(z), 16, 256, w, 512, None) == 1
+
+
+def test_fwd_host_rejects_bad_arguments_without_touching_the_device(built_lib):
+    lib = built_lib
+    shape = _lib.shape_struct((128, 128, 128, 128))
+    w = _lib.ptr_array([256, 512, 768])
+    assert lib.mlpk_fwd_host_workspace_size(ctypes.byref(shape), -1) == -1
+    ws0 = lib.mlpk_fwd_host_workspace_size(ctypes.byref(shape), 0)
+    assert ws0 == lib.mlpk_fwd_host_workspace_size(ctypes.byref(shape), _lib.FWD_HOST_CHUNK_ROWS)
+    assert ws0 == 3 * 2 * _lib.FWD_HOST_CHUNK_ROWS * 128 * 2  # x and out buffers, 3 of each
+    # NULL shape, negative M / chunk, NULL weight, unsupported shape, M = 0
+    assert lib.mlpk_fwd_host(None, 16, 256, w, 512, 0, 1024, ws0, None) == 6
+    assert lib.mlpk_fwd_host(ctypes.byref(shape), -1, 256, w, 512, 0, 1024, ws0, None) == 1
+    assert lib.mlpk_fwd_host(ctypes.byref(shape), 16, 256, w, 512, -5, 1024, ws0, None) == 1
+    assert lib.mlpk_fwd_host(ctypes.byref(shape), 16, 256, _lib.ptr_array([256, 0, 768]), 512, 0,
+                             1024, ws0, None) == 6
+    bad = _lib.shape_struct((128, 100, 128, 128))
+    assert lib.mlpk_fwd_host(ctypes.byref(bad), 16, 256, w, 512, 0, 1024, ws0, None) == 2
+    assert lib.mlpk_fwd_host(ctypes.byref(shape), 0, None, w, None, 0, None, 0, None) == 0
+    # too small a workspace
+    assert lib.mlpk_fwd_host(ctypes.byref(shape), 16, 256, w, 512, 0, 1024, ws0 - 1, None) == 1
