@@ -15,6 +15,9 @@ accepts (kernel.py:37-43, 134-138): fp32 operands are rounded to fp16 by the
 library's cast kernel, the fused fp16 kernel runs, and its fp16-rounded result
 is widened into the fp32 output -- the reference's own rounding points for the
 hidden activations (kernel.py:110, 117) and the output (kernel.py:121-124).
+(The reference rounds fp32 x and W to tf32 for its first GEMM: the same 10
+mantissa bits, but fp32's exponent range; fp16 here turns magnitudes above
+65,504 into infinities.)
 There is no CPU or PyTorch fallback: CPU tensors, other dtypes or unsupported
 shapes raise.
 """
