@@ -51,16 +51,17 @@ enum {
 /* Human-readable text for a status code. */
 const char* mlpk_status_string(int status);
 
-/* 1 if a kernel serves this shape, else 0.  Compiled networks: 3 layers at
- * 64, 128 and 256 wide; 5 layers at 32-64-64-64-64-16 and 64, 128 and 256
- * wide (the 256-wide 3-layer and the 128- and 256-wide 5-layer networks run
- * the streamed-weight kernels).  A network of the
+/* 1 if a kernel serves this shape, else 0.  Compiled networks: 2, 3 and 4
+ * layers at 64, 128 and 256 wide; 5 layers at 32-64-64-64-64-16 and 64, 128
+ * and 256 wide (the networks whose weights do not fit in shared memory --
+ * 256 wide, and 128 wide at 4 and 5 layers -- run the streamed-weight
+ * kernels).  A network of the
  * same depth whose every width is a multiple of 8 and at most the compiled
  * width is served by the smallest such kernel (its missing rows / columns are
  * zero-filled on load and clipped on store; results are those of the
  * caller's network).  Hidden widths need not be equal.  The reference's
  * kernel takes the widths its tiles divide (kernel.py:25-53); all of them
- * up to 256 wide are served, at 3 and 5 layers. */
+ * up to 256 wide are served, at 3 and 5 layers (and 2 and 4). */
 int mlpk_shape_supported(const mlpk_shape* shape);
 
 /* Inference forward: out[M, dL] = MLP(x[M, d0]).

@@ -99,11 +99,25 @@ struct BwdCfg {
   }
   static constexpr int NG = dgmax() >= 128 ? 4 : dgmax() >= 64 ? 2 : 1;
   static constexpr int EPI_WARPS = 4 * NG;  // per slot
-  // Tiles in flight ("slots"): two when TMEM holds a second dgrad accumulator
-  // next to the dW accumulators; the MMA warp then alternates the slots' layer
-  // steps so one slot's epilogue overlaps the other slot's MMAs.
   static constexpr int ACC_W = align_up(DMAX, 32);
-  static constexpr int NS = dw_col(L) + 2 * ACC_W <= 512 ? 2 : 1;
+  static constexpr int TILE_BYTES = align_up(tile_bytes(kTileM, DMAX), 1024);
+  static constexpr int W_TOTAL = NetT::w_total();
+  static constexpr int ZERO_BYTES = any_pad() ? 16384 : 0;  // 128 rows x 128 B
+  // ring slots that fit in shared memory next to the weights, `ns` dz tiles
+  // (G), the zero chunk and the barriers: w_full, slot_full[8],
+  // slot_empty[8], then per tile slot acc_full, acc_free, wg_done, dz_full,
+  // out_ready; mma_done
+  __host__ __device__ static constexpr int ring_fit(int ns) {
+    return (232448 - 1024 - 16 - 8 * (2 + 2 * 8 + 5 * ns) - (W_TOTAL + ns * TILE_BYTES) - ZERO_BYTES) /
+           TILE_BYTES;
+  }
+  // Tiles in flight ("slots"): two when TMEM holds a second dgrad accumulator
+  // next to the dW accumulators and the ring can hold one tile's loads plus
+  // the first two of the next (see the producer); the MMA warp then
+  // alternates the slots' layer steps so one slot's epilogue overlaps the
+  // other slot's MMAs.
+  static constexpr int NS =
+      (dw_col(L) + 2 * ACC_W <= 512 && (ring_fit(2) > 8 ? 8 : ring_fit(2)) >= L + 3) ? 2 : 1;
   static constexpr int THREADS = (2 + NS * EPI_WARPS) * 32;
   __host__ __device__ static constexpr bool groups_ok() {
     for (int l = 0; l < L; ++l) {
@@ -112,15 +126,9 @@ struct BwdCfg {
     }
     return true;
   }
-  static constexpr int TILE_BYTES = align_up(tile_bytes(kTileM, DMAX), 1024);
-  static constexpr int W_TOTAL = NetT::w_total();
   static constexpr int OFF_G = W_TOTAL;                  // G of slot s at OFF_G + s * TILE_BYTES
   static constexpr int OFF_RING = OFF_G + NS * TILE_BYTES;
-  static constexpr int ZERO_BYTES = any_pad() ? 16384 : 0;  // 128 rows x 128 B
-  // barriers: w_full, slot_full[RING], slot_empty[RING], then per tile slot
-  //           acc_full, acc_free, wg_done, dz_full, out_ready; mma_done
-  static constexpr int RING_FIT =
-      (232448 - 1024 - 16 - 8 * (2 + 2 * 8 + 5 * NS) - OFF_RING - ZERO_BYTES) / TILE_BYTES;
+  static constexpr int RING_FIT = ring_fit(NS);
   static constexpr int RING = RING_FIT > 8 ? 8 : RING_FIT;
   static constexpr int OFF_ZERO = OFF_RING + RING * TILE_BYTES;
   static constexpr int OFF_BAR = OFF_ZERO + ZERO_BYTES;

@@ -540,6 +540,12 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
   using N5w64 = Net<64, 64, 64, 64, 64, 64>;
   using N5w128 = Net<128, 128, 128, 128, 128, 128>;
   using N5w256 = Net<256, 256, 256, 256, 256, 256>;
+  using N2w64 = Net<64, 64, 64>;
+  using N2w128 = Net<128, 128, 128>;
+  using N2w256 = Net<256, 256, 256>;
+  using N4w64 = Net<64, 64, 64, 64, 64>;
+  using N4w128 = Net<128, 128, 128, 128, 128>;
+  using N4w256 = Net<256, 256, 256, 256, 256>;
   ShapeOps o;
   if (covers<N64>(s)) {
     o.fwd = &launch_fwd<N64, 3, 4>;
@@ -569,6 +575,30 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.fwd = &launch_stream_fwd<N5w256>;
     o.bwd = &launch_stream_bwd<N5w256>;
     o.bwd_ws = &stream_bwd_workspace<N5w256>;
+  } else if (covers<N2w64>(s)) {  // one hidden layer
+    o.fwd = &launch_fwd<N2w64, 3, 4>;
+    o.bwd = &launch_bwd<N2w64>;
+    o.bwd_ws = &bwd_workspace<N2w64>;
+  } else if (covers<N2w128>(s)) {
+    o.fwd = &launch_fwd<N2w128, 2, 4>;
+    o.bwd = &launch_bwd<N2w128>;
+    o.bwd_ws = &bwd_workspace<N2w128>;
+  } else if (covers<N2w256>(s)) {
+    o.fwd = &launch_stream_fwd<N2w256>;
+    o.bwd = &launch_stream_bwd<N2w256>;
+    o.bwd_ws = &stream_bwd_workspace<N2w256>;
+  } else if (covers<N4w64>(s)) {  // three hidden layers
+    o.fwd = &launch_fwd<N4w64, 3, 4>;
+    o.bwd = &launch_bwd<N4w64>;
+    o.bwd_ws = &bwd_workspace<N4w64>;
+  } else if (covers<N4w128>(s)) {
+    o.fwd = &launch_stream_fwd<N4w128>;
+    o.bwd = &launch_stream_bwd<N4w128>;
+    o.bwd_ws = &stream_bwd_workspace<N4w128>;
+  } else if (covers<N4w256>(s)) {
+    o.fwd = &launch_stream_fwd<N4w256>;
+    o.bwd = &launch_stream_bwd<N4w256>;
+    o.bwd_ws = &stream_bwd_workspace<N4w256>;
   }
   return o;
 }

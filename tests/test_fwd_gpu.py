@@ -194,8 +194,9 @@ def test_fwd_errors_are_loud():
         fused_mlp_fwd(x.float().cuda(), *[w.cuda() for w in ws])
     with pytest.raises(ValueError):
         fused_mlp_fwd(x.cuda(), ws[0].cuda(), ws[1][:64].cuda(), ws[2].cuda())
-    bad = [torch.zeros(128, 96, dtype=torch.float16, device="cuda"),
-           torch.zeros(96, 128, dtype=torch.float16, device="cuda")]
+    # a width that is not a multiple of 8: no kernel serves it
+    bad = [torch.zeros(128, 100, dtype=torch.float16, device="cuda"),
+           torch.zeros(100, 128, dtype=torch.float16, device="cuda")]
     with pytest.raises(_lib.MlpkError):
         fused_mlp_fwd(x.cuda(), *bad)
 

@@ -57,7 +57,13 @@ def test_status_strings(built_lib):
     ((128, 100, 128, 128), False),   # 100 is not a multiple of 8
     ((264, 256, 256, 256), False),   # wider than every 3-layer kernel
     ((64, 64, 64, 64, 64, 264), False),  # wider than every 5-layer kernel
-    ((64, 64, 64, 64, 64), False),   # 4 layers: no kernel of that depth
+    # 2 and 4 layers (one and three hidden layers)
+    ((64, 64, 64), True),
+    ((128, 96, 16), True),
+    ((256, 256, 256), True),
+    ((64, 64, 64, 64, 64), True),
+    ((200, 128, 64, 256, 8), True),
+    ((64, 64, 64, 64, 64, 64, 64), False),  # 6 layers: no kernel of that depth
     ((128, 128), False),
 ])
 def test_shape_supported(built_lib, dims, ok):

@@ -1,7 +1,7 @@
 """GPU parity for networks served by a larger compiled network (zero padding
 through TMA): the caller's widths need only be multiples of 8 and at most the
-compiled widths of the same depth (64^3, 128^3, 256^3 for 3 layers;
-32-64-64-64-64-16, 64^5, 128^5 and 256^5 for 5), hidden widths may differ from
+compiled widths of the same depth (64, 128 and 256 wide for 2, 3 and 4 layers;
+32-64-64-64-64-16, 64, 128 and 256 wide for 5), hidden widths may differ from
 each other.
 
 The reference's kernel accepts any widths its tl.dot tiles divide
@@ -41,6 +41,15 @@ SHAPES = [
     ((96, 128, 64, 128, 112, 16), "5-layer 128-wide streamed"),
     ((256, 256, 256, 256, 256, 256), "5-layer 256-wide streamed (exact)"),
     ((200, 136, 256, 72, 128, 64), "5-layer 256-wide streamed"),
+    ((64, 64, 64), "2-layer 64-wide (exact)"),
+    ((32, 48, 16), "2-layer 64-wide"),
+    ((128, 128, 128), "2-layer 128-wide (exact)"),
+    ((128, 96, 16), "2-layer 128-wide"),
+    ((256, 200, 64), "2-layer 256-wide streamed"),
+    ((64, 64, 64, 64, 64), "4-layer 64-wide (exact)"),
+    ((32, 64, 48, 64, 8), "4-layer 64-wide"),
+    ((128, 96, 128, 112, 16), "4-layer 128-wide streamed"),
+    ((200, 128, 64, 256, 8), "4-layer 256-wide streamed"),
 ]
 
 
@@ -132,8 +141,10 @@ def test_padded_network_equals_compiled_network_exactly():
 @pytest.mark.parametrize("kw", [dict(D=48, H=96, out_features=24),
                                 dict(D=64, H=200, out_features=40),
                                 dict(D=16, H=48, out_features=8, num_layers=5),
-                                dict(D=64, H=160, out_features=32, num_layers=5)],
-                         ids=["3L-96", "3L-200", "5L-48", "5L-160"])
+                                dict(D=64, H=160, out_features=32, num_layers=5),
+                                dict(D=32, H=96, out_features=8, num_layers=2),
+                                dict(D=48, H=64, out_features=16, num_layers=4)],
+                         ids=["3L-96", "3L-200", "5L-48", "5L-160", "2L-96", "4L-64"])
 def test_modules_with_other_widths(cls, kw):
     """The reference's modules take any D, H, out_features (README.md:58-70):
     gradients through autograd against torch's own autograd in fp32 on the same
