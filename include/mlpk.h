@@ -10,7 +10,8 @@
  * Conventions (mirroring the reference, kernel.py:130-156):
  *   - weights are [in, out] row-major (out = x @ W), fp16;
  *   - activations x / out / grad_out / dx are [M, d] row-major fp16;
- *   - saved training activations and weight gradients are fp32;
+ *   - saved training activations are fp16 (the next GEMM's operand), weight
+ *     gradients and weight-norm parameters fp32;
  *   - every pointer must be 16-byte aligned and tensors contiguous;
  *   - all work is enqueued on `stream`; no entry point synchronises the host
  *     (except mlpk_device_status, which reads a device word);
@@ -111,10 +112,10 @@ int mlpk_wn_bwd(const mlpk_shape* shape, const float* dW_all, const float* v_all
                 mlpk_stream_t stream);
 
 /* Allocation-free backward.  No counterpart in the reference: it exists for
- * callers that cannot allocate device memory at the time they call it (code
- * running under CUDA stream capture, plain C / FFI callers that own only their
- * input and output buffers, serving processes whose memory is fixed at
- * start-up).  Same arguments and results as mlpk_bwd minus the workspace: the
+ * callers that cannot allocate device memory at the time they call it (plain
+ * C / FFI callers that hold only their input and output buffers and have no
+ * device allocator of their own, serving processes that reserve all their
+ * device memory at start-up and must not allocate afterwards).  Same arguments and results as mlpk_bwd minus the workspace: the
  * per-CTA weight-gradient partials live in a static device array of
  * MLPK_BWD_NOALLOC_SCRATCH_BYTES (32 MiB) that every GPU which loads the
  * library holds until the process exits.  Returns MLPK_ERR_SCRATCH when the

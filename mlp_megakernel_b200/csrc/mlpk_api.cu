@@ -763,9 +763,9 @@ int mlpk_wn_bwd(const mlpk_shape* shape, const float* dW_all, const float* v_all
 
 // ------------------------------------------------------------------ allocation-free backward
 // Backward for callers that cannot allocate device memory when they call it
-// (code running under CUDA stream capture, plain C / FFI callers that own only
-// their input and output buffers, serving processes whose device memory is
-// fixed at start-up).  Instead of a caller-provided workspace, the per-CTA
+// (plain C / FFI callers that hold only their input and output buffers and no
+// device allocator, serving processes whose device memory is fixed at
+// start-up).  Instead of a caller-provided workspace, the per-CTA
 // weight-gradient partials live in this file-scope array, which every GPU that
 // loads the library holds until the process exits.
 }  // extern "C"

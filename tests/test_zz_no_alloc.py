@@ -1,8 +1,9 @@
 """The allocation-free backward (mlpk_bwd_noalloc) against the allocating one.
 
 mlpk_bwd_noalloc serves callers that cannot allocate device memory when they
-call the backward -- code under CUDA stream capture, C / FFI callers that own
-only their inputs and outputs, serving processes with a fixed memory budget.
+call the backward -- C / FFI callers that hold only their inputs and outputs
+and no device allocator, serving processes whose device memory is fixed at
+start-up.
 It keeps its scratch (the per-CTA weight-gradient partials) in a static 32 MiB
 device array inside the library instead of a caller workspace.  This test calls
 it through the C ABI twice in a row -- a large batch, then a small one that
