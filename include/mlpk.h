@@ -4,8 +4,7 @@
  * The drop-in boundary for the reference's fused-MLP path
  * (Marcelo5444/mlp-megakernel).  Every entry point takes plain device
  * pointers, sizes and a CUDA stream; no torch types cross this boundary.  The
- * Python package binds these symbols with ctypes (see INTEGRATION.md for the
- * binding a maintainer of the reference would add).
+ * Python package binds these symbols with ctypes.
  *
  * Conventions (mirroring the reference, kernel.py:130-156):
  *   - weights are [in, out] row-major (out = x @ W), fp16;
@@ -115,12 +114,19 @@ int mlpk_wn_bwd(const mlpk_shape* shape, const float* dW_all, const float* v_all
  * callers that cannot allocate device memory at the time they call it (plain
  * C / FFI callers that hold only their input and output buffers and have no
  * device allocator of their own, serving processes that reserve all their
- * device memory at start-up and must not allocate afterwards).  Same arguments and results as mlpk_bwd minus the workspace: the
- * per-CTA weight-gradient partials live in a static device array of
+ * device memory at start-up and must not allocate afterwards).  Same
+ * arguments and results as mlpk_bwd minus the workspace: the scratch mlpk_bwd
+ * keeps in its workspace lives in a static device array of
  * MLPK_BWD_NOALLOC_SCRATCH_BYTES (32 MiB) that every GPU which loads the
- * library holds until the process exits.  Returns MLPK_ERR_SCRATCH when the
- * problem needs more than that (mlpk_bwd_workspace_size > 32 MiB; 3L128 on a
- * 148-SM B200 needs at most 29 MB).  Calls no allocator.  The first call on a
+ * library holds until the process exits.  Returns MLPK_ERR_SCRATCH, before
+ * any launch, when the problem needs more than that (mlpk_bwd_workspace_size
+ * > 32 MiB).  On a 148-SM B200 that serves: every network of the fused
+ * backward (the 64- and 128-wide 2- and 3-layer networks, the 64-wide 4- and
+ * 5-layer ones and the 5-layer 32-64-64-64-64-16) at any M (3L128 needs at
+ * most 29 MB); the streamed 128-wide 4-layer network up to about 31,000 rows
+ * and the 5-layer one up to about 23,000 rows (their data gradients are kept
+ * in the scratch); no 256-wide network (their weight-gradient partials alone
+ * take about 38 MB).  Calls no allocator.  The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress) with that
  * device current; make that first call before any stream capture.  All calls
  * share the array, so calls that overlap on the GPU (other streams, other

@@ -18,7 +18,7 @@ LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libmlpk.so")
 
 SOURCES = ["mlpk_api.cu"]
-DEPS = ["ptx.cuh", "layout.cuh", "softplus.cuh", "fwd_kernel.cuh", "fwd2_kernel.cuh",
+DEPS = ["ptx.cuh", "layout.cuh", "softplus.cuh", "fwd_kernel.cuh",
         "bwd_kernel.cuh", "wn_kernel.cuh", "stream_kernel.cuh", "wgrad_kernel.cuh", "peer_kernel.cuh", "cast_kernel.cuh"]
 
 NVCC_FLAGS = [

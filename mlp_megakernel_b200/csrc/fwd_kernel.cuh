@@ -71,20 +71,6 @@ struct Net {
     for (int i = 0; i < L; ++i) o += tile_bytes(a[i], a[i + 1]);
     return o;
   }
-  // Offsets/bytes when each CTA of a pair holds half of every weight's columns.
-  template <int l>
-  __host__ __device__ static constexpr int w_half_off() {
-    constexpr int a[] = {Ds...};
-    int o = 0;
-    for (int i = 0; i < l; ++i) o += align_up(tile_bytes(a[i], a[i + 1] / 2), 1024);
-    return o;
-  }
-  __host__ __device__ static constexpr int w_half_bytes_exact() {
-    constexpr int a[] = {Ds...};
-    int o = 0;
-    for (int i = 0; i < L; ++i) o += tile_bytes(a[i], a[i + 1] / 2);
-    return o;
-  }
   __host__ __device__ static constexpr int dim(int i) {
     constexpr int a[] = {Ds...};
     return a[i];
@@ -190,17 +176,12 @@ __device__ __forceinline__ void pack_cols(const uint32_t* r, uint32_t* w) {
 }
 
 // Publishes one finished chunk of h to the MMA issuer: the TMEM stores are
-// complete and ordered (with this chunk's TMEM loads) before the arrive.  With
-// CLUSTER the barrier is a cluster address (the pair leader's barrier).
-template <bool CLUSTER = false>
+// complete and ordered (with this chunk's TMEM loads) before the arrive.
 __device__ __forceinline__ void publish_chunk(uint32_t bar) {
   tmem_wait_st();
   tc_fence_before();
   __syncwarp();
-  if (lane_id() == 0) {
-    if constexpr (CLUSTER) mbar_arrive_cluster(bar);
-    else mbar_arrive(bar);
-  }
+  if (lane_id() == 0) mbar_arrive(bar);
 }
 
 // Hidden-layer job of one warp of column group `grp` (of NG): stripes
@@ -214,7 +195,7 @@ __device__ __forceinline__ void publish_chunk(uint32_t bar) {
 // column is always loaded before the packed activation overwrites it: a
 // stripe's packed columns lie in its own range, and the async load of the
 // next stripe is issued before this stripe's store.
-template <int N, int NG, int SPC, bool CLUSTER = false, int SAVE = 0>
+template <int N, int NG, int SPC, int SAVE = 0>
 __device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chunk_bar0,
                                            uint8_t* hrow = nullptr, uint32_t stage_base = 0,
                                            uint32_t row = 0) {
@@ -248,7 +229,7 @@ __device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chun
                      w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
       }
     }
-    if ((j + 1) % SPC == 0) publish_chunk<CLUSTER>(chunk_bar0 + 8 * (j / SPC));
+    if ((j + 1) % SPC == 0) publish_chunk(chunk_bar0 + 8 * (j / SPC));
     if (j + 1 < SUBS) {
       tmem_wait_ld_bind_x32(b);
 #pragma unroll
@@ -525,7 +506,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
         const uint32_t t_buf = t_lane + ((i * L + l) & 1) * Cfg::SLOT_COLS;
         if constexpr (TRAIN) {
           // h_l -> TMEM (next layer's A) and the staging tile -> TMA store
-          hidden_job<H, Cfg::NG, Cfg::SPC, false, 2>(t_buf, grp, bar_chunk(s, 0), nullptr, obuf, row);
+          hidden_job<H, Cfg::NG, Cfg::SPC, 2>(t_buf, grp, bar_chunk(s, 0), nullptr, obuf, row);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar_out_ready(s));

@@ -9,7 +9,6 @@
 
 #include <cstdint>
 #include <cstdio>
-#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <set>
@@ -18,7 +17,6 @@
 #include "../../include/mlpk.h"
 #include "bwd_kernel.cuh"
 #include "cast_kernel.cuh"
-#include "fwd2_kernel.cuh"
 #include "stream_kernel.cuh"
 #include "peer_kernel.cuh"
 #include "wgrad_kernel.cuh"
@@ -204,48 +202,6 @@ int launch_fwd(const int* rd, const void* x, const void* const* W, void* out, in
   auto kern = mlpk::mlp_fwd_kernel<NetT, NS, EPW, false>;
   if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
   return launch_kernel(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, st, maps, num_tiles);
-}
-
-// CTA-pair forward: clusters of 2 CTAs, one M=256 UMMA per pair tile.
-template <class NetT, int NS, int EPW>
-int launch_fwd2(const int* rd, const void* x, const void* const* W, void* out, int64_t M,
-                void* const* hsave, cudaStream_t st) {
-  if (hsave) return MLPK_ERR_UNSUPPORTED;  // the pair kernel is inference-only
-  for (int i = 0; i <= NetT::L; ++i)       // and serves its own widths only
-    if (rd[i] != NetT::dim(i)) return MLPK_ERR_UNSUPPORTED;
-  using Cfg = mlpk::Fwd2Cfg<NetT, NS, EPW>;
-  constexpr int L = NetT::L;
-  DevInfo di;
-  int dev = 0;
-  int rc = current_device_info(&di, &dev);
-  if (rc != MLPK_OK) return rc;
-  if (M == 0) return MLPK_OK;
-  if (M > (int64_t(1) << 31) - 512) return MLPK_ERR_SHAPE;
-
-  FwdMaps<L> maps;
-  std::memset(&maps, 0, sizeof(maps));
-  rc = make_map_2d(&maps.x, x, Cfg::D0, M, mlpk::chunk_elems(Cfg::D0), mlpk::kTileM);
-  if (rc) return rc;
-  rc = make_map_2d(&maps.out, out, Cfg::DL, M, mlpk::chunk_elems(Cfg::DL), mlpk::kTileM);
-  if (rc) return rc;
-  int wrc = MLPK_OK;
-  mlpk::static_for<0, L>([&](auto lc) {
-    constexpr int l = decltype(lc)::value;
-    constexpr int K = NetT::template D<l>();
-    constexpr int NH = NetT::template D<l + 1>() / 2;
-    // box covers one CTA's half of the output columns
-    if (wrc == MLPK_OK) wrc = make_map_2d(&maps.w[l], W[l], 2 * NH, K, mlpk::chunk_elems(NH), K);
-  });
-  if (wrc) return wrc;
-  maps.M = static_cast<int>(M);
-  maps.out_cols = Cfg::DL;
-
-  auto kern = mlpk::mlp_fwd2_kernel<NetT, NS, EPW>;
-  if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
-  const int num_pairs = static_cast<int>((M + 2 * mlpk::kTileM - 1) / (2 * mlpk::kTileM));
-  const int max_clusters = di.sm_count / 2;
-  const int clusters = num_pairs < max_clusters ? num_pairs : max_clusters;
-  return launch_kernel(kern, 2 * clusters, Cfg::THREADS, Cfg::SMEM_BYTES, st, maps, num_pairs);
 }
 
 // ------------------------------------------------------------------ backward
@@ -496,14 +452,6 @@ struct ShapeOps {
   BwdWs bwd_ws = nullptr;
 };
 
-// MLPK_FWD_PAIR=1 selects the CTA-pair (cta_group::2) forward for shapes that
-// have one; the single-SM kernel is the default (measured faster on B200 for
-// the 128-wide network).  Read on every call so a process can switch.
-bool prefer_pair() {
-  const char* e = std::getenv("MLPK_FWD_PAIR");
-  return e && e[0] == '1';
-}
-
 // The compiled networks, smallest first.  A caller's network is served by the
 // first one of its depth that covers it: every width at most the compiled
 // width and a multiple of 8 (16-byte rows, the TMA stride rule).  The missing
@@ -517,14 +465,6 @@ bool covers(const mlpk_shape* s) {
   if (s->num_layers != NetT::L) return false;
   for (int i = 0; i <= NetT::L; ++i)
     if (s->dims[i] > NetT::dim(i) || s->dims[i] % 8 != 0) return false;
-  return true;
-}
-
-template <class NetT>
-bool exact(const mlpk_shape* s) {
-  if (s->num_layers != NetT::L) return false;
-  for (int i = 0; i <= NetT::L; ++i)
-    if (s->dims[i] != NetT::dim(i)) return false;
   return true;
 }
 
@@ -552,7 +492,7 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.bwd = &launch_bwd<N64>;
     o.bwd_ws = &bwd_workspace<N64>;
   } else if (covers<N3>(s)) {
-    o.fwd = (prefer_pair() && !training && exact<N3>(s)) ? &launch_fwd2<N3, 2, 4> : &launch_fwd<N3, 2, 4>;
+    o.fwd = &launch_fwd<N3, 2, 4>;
     o.bwd = &launch_bwd<N3>;
     o.bwd_ws = &bwd_workspace<N3>;
   } else if (covers<N256>(s)) {
@@ -802,12 +742,17 @@ extern "C" {
 int mlpk_bwd_noalloc(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
                      const void* const* h_saved, const void* grad_out, void* dx, float* dW,
                      mlpk_stream_t stream) {
-  const int64_t need = mlpk_bwd_workspace_size(shape, M);
-  if (need < 0) return check_shape(shape) != MLPK_OK || M < 0 ? MLPK_ERR_SHAPE : MLPK_ERR_UNSUPPORTED;
-  if (need > static_cast<int64_t>(MLPK_BWD_NOALLOC_SCRATCH_BYTES)) return MLPK_ERR_SCRATCH;
+  int rc = check_shape(shape);
+  if (rc) return rc;
+  if (M < 0) return MLPK_ERR_SHAPE;
+  const ShapeOps o = pick_ops(shape, true);
+  if (!o.bwd_ws) return MLPK_ERR_UNSUPPORTED;
+  DevInfo di;
+  if ((rc = current_device_info(&di, nullptr)) != MLPK_OK) return rc;  // CUDA failure or not sm_100
+  const size_t need = o.bwd_ws(M, di.sm_count);
+  if (need > static_cast<size_t>(MLPK_BWD_NOALLOC_SCRATCH_BYTES)) return MLPK_ERR_SCRATCH;
   void* scratch = nullptr;
-  const int rc = noalloc_scratch(&scratch);
-  if (rc != MLPK_OK) return rc;
+  if ((rc = noalloc_scratch(&scratch)) != MLPK_OK) return rc;
   // Every call reuses the same array: the backward kernel overwrites the
   // partials of every CTA it launches before the reduction reads them, so no
   // stale contents from an earlier call are ever read.

@@ -170,7 +170,7 @@ __device__ __forceinline__ void dgrad_job(uint32_t tbuf, int grp, uint32_t chunk
                      w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
       }
     }
-    if ((j + 1) % SPC == 0) publish_chunk<false>(chunk_bar0 + 8 * (j / SPC));
+    if ((j + 1) % SPC == 0) publish_chunk(chunk_bar0 + 8 * (j / SPC));
     if (j + 1 < SUBS) {
       tmem_wait_ld_bind_x32(b);
 #pragma unroll
@@ -426,7 +426,7 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
         }
         const uint32_t t_buf = t_lane + (g & 1) * Cfg::SLOT_COLS;
         if constexpr (MODE == kStreamFwd)
-          hidden_job<H, NG, Cfg::SPC, false, SAVE ? 2 : 0>(t_buf, grp, bar_chunk(0), nullptr, s_o, row);
+          hidden_job<H, NG, Cfg::SPC, SAVE ? 2 : 0>(t_buf, grp, bar_chunk(0), nullptr, s_o, row);
         else
           dgrad_job<H, NG, Cfg::SPC, SAVE>(t_buf, grp, bar_chunk(0), hv, hrow, hcols, s_o, row);
         if constexpr (SAVE) {

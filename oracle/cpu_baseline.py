@@ -40,6 +40,19 @@ def train_step(x: torch.Tensor, weights, grad_out: torch.Tensor):
     return out, [w.grad for w in ws]
 
 
+def train_step_wn(x: torch.Tensor, vs, gs, grad_out: torch.Tensor):
+    """One weight-normed training step: W_l = g_l v_l / ||v_l|| per output
+    column (mlp_fused.md:466-480), the forward above, and torch.autograd back
+    to dx and (dv_l, dg_l) for every layer."""
+    x = x.detach().requires_grad_(True)
+    vs = [v.detach().requires_grad_(True) for v in vs]
+    gs = [g.detach().requires_grad_(True) for g in gs]
+    ws = [g * v / v.norm(dim=0, keepdim=True) for v, g in zip(vs, gs)]
+    out = model_forward(x, ws)
+    out.backward(grad_out)
+    return out, x.grad, [v.grad for v in vs], [g.grad for g in gs]
+
+
 def time_rows_per_s(fn, rows_per_call: int, min_seconds: float = 10.0, max_calls: int = 1000):
     """Call fn() repeatedly for at least min_seconds; return rows/s and calls made."""
     fn()  # warm-up

@@ -49,3 +49,36 @@ def make_case_inputs(dims, M, dist, seed, scale):
     else:
         ws = [(w.float() * scale).half() for w in make_weights(dims)]
     return x, ws
+
+
+# Training cases (fixtures ``train_<name>.npz``): BASELINE config 3 -- 3L128
+# with weight norm W_l = g_l v_l / ||v_l|| (per output column), v_l ~
+# U(+-1/sqrt(in)) seed 1 (the fp16 weights of make_weights, widened), g_l =
+# ||v_l||, x ~ N(0,1) seed 0, grad_out ~ N(0,1) seed 2, fp16 inputs.
+# name -> (dims, M, rows recorded for out / dx (0 = all))
+TRAIN_CASES = {
+    "cfg3_M16384": ((128, 128, 128, 128), 16384, 512),
+    "cfg3_M262144": ((128, 128, 128, 128), 262144, 512),
+}
+
+
+def make_train_inputs(dims, M):
+    """(x fp16, grad_out fp16, v fp32 list, g fp32 list) of a training case."""
+    from mlp_megakernel_b200.synthetic import make_grad
+
+    x = make_x(M, dims[0], "normal", 0)
+    grad = make_grad(M, dims[-1], seed=2)
+    vs = [w.float() for w in make_weights(dims)]
+    gs = [v.norm(dim=0) for v in vs]
+    return x, grad, vs, gs
+
+
+def train_rows(M, n):
+    """The recorded row subsample of a training case: the first and last 64
+    rows and an even stride over the batch."""
+    import numpy as np
+
+    if n == 0 or n >= M:
+        return np.arange(M)
+    return np.unique(np.concatenate([np.arange(0, 64), np.arange(M - 64, M),
+                                     np.arange(0, M, max(1, M // n))])).astype(np.int64)

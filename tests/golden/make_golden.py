@@ -8,11 +8,19 @@ at import (kernel.py:18); with no GPU in this container that query is answered
 with 148 (a B200's SM count) -- it only sizes the persistent grid, not the
 arithmetic.
 
-Needs the reference checkout (default /root/reference, or $MLPK_REFERENCE)
-and only ever runs in the development container; the GPU box and the tests
-use the committed fixtures.  Usage:
+It also records TRAINING fixtures from the reference's own PyTorch model:
+``Model`` (kernel.py:163-171) imported from the reference, fed the effective
+weights of an explicit weight norm W_l = g_l v_l / ||v_l|| (per output column,
+the weight norm of mlp_fused.md:466-480), run in fp32 on the CPU and
+differentiated by torch.autograd: out and dx on a row subsample, the full
+gradients of the effective weights dW_l and of the weight-norm parameters
+dv_l, dg_l (BASELINE config 3 at M = 16,384 and 262,144).
 
-    python tests/golden/make_golden.py
+Needs the reference checkout at $MLPK_REFERENCE (a directory holding its
+kernel.py) and only ever runs in the development container; the GPU box and
+the tests use the committed fixtures.  Usage:
+
+    MLPK_REFERENCE=<reference checkout> python tests/golden/make_golden.py [--train-only]
 """
 from __future__ import annotations
 
@@ -31,9 +39,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 
-from tests.golden.cases import CASES, make_case_inputs  # noqa: E402
+from tests.golden.cases import CASES, TRAIN_CASES, make_case_inputs, make_train_inputs, train_rows  # noqa: E402
 
-REF = os.environ.get("MLPK_REFERENCE", "/root/reference")
+REF = os.environ.get("MLPK_REFERENCE")
 
 
 class _Props:
@@ -42,6 +50,8 @@ class _Props:
 
 
 def load_reference():
+    if not REF or not os.path.exists(os.path.join(REF, "kernel.py")):
+        raise SystemExit("set MLPK_REFERENCE to the reference checkout (the directory holding kernel.py)")
     torch.cuda.get_device_properties = lambda *_a, **_k: _Props()
     spec = importlib.util.spec_from_file_location("ref_kernel", os.path.join(REF, "kernel.py"))
     mod = importlib.util.module_from_spec(spec)
@@ -56,8 +66,48 @@ def make_case(mod, dims, M, dist, seed, scale):
     return x, ws, out, ref32
 
 
+def _digest(*ts) -> str:
+    return hashlib.sha256(b"".join(t.contiguous().numpy().tobytes() for t in ts)).hexdigest()
+
+
+def make_train_case(mod, name, dims, M, nrows):
+    """Reference Model (kernel.py:163-171) on weight-normed weights, fp32,
+    torch.autograd; records the gradients the training kernels must match."""
+    x16, g16, vs, gs = make_train_inputs(dims, M)
+    x = x16.float().requires_grad_(True)
+    vs = [v.clone().requires_grad_(True) for v in vs]
+    gs = [g.clone().requires_grad_(True) for g in gs]
+    ws = [g * v / v.norm(dim=0, keepdim=True) for v, g in zip(vs, gs)]
+    for w in ws:
+        w.retain_grad()
+    out = mod.Model()(x, *ws)
+    out.backward(g16.float())
+    rows = train_rows(M, nrows)
+    rec = {
+        "dims": np.array(dims, dtype=np.int32),
+        "M": np.int64(M),
+        "x_sha256": _digest(x16),
+        "grad_sha256": _digest(g16),
+        "v_sha256": _digest(*[v.detach() for v in vs]),
+        "rows": rows,
+        "out_ref": out.detach().numpy()[rows],
+        "dx_ref": x.grad.numpy()[rows],
+        "dw_ref": np.concatenate([w.grad.reshape(-1).numpy() for w in ws]),
+        "dv_ref": np.concatenate([v.grad.reshape(-1).numpy() for v in vs]),
+        "dg_ref": np.concatenate([g.grad.numpy() for g in gs]),
+    }
+    path = os.path.join(HERE, f"train_{name}.npz")
+    np.savez_compressed(path, **rec)
+    print(f"train {name}: M={M} dims={dims} |dv| {np.linalg.norm(rec['dv_ref']):.4e} "
+          f"-> {os.path.getsize(path)} bytes")
+
+
 def main():
     mod = load_reference()
+    for name, (dims, M, nrows) in TRAIN_CASES.items():
+        make_train_case(mod, name, dims, M, nrows)
+    if "--train-only" in sys.argv[1:]:
+        return
     for f in os.listdir(HERE):
         if f.startswith("fwd_") and f.endswith(".npz"):
             os.remove(os.path.join(HERE, f))
