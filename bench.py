@@ -64,7 +64,6 @@ def parse_args():
     ap.add_argument("--impl", default="mlpk", choices=["mlpk", "reference"])
     ap.add_argument("--rows", type=int, default=ROWS, help="rows per GPU")
     ap.add_argument("--e2e-steps", type=int, default=3)
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--train-rows", type=int, default=TRAIN_ROWS, help="training rows per GPU")
     ap.add_argument("--train5-rows", type=int, default=TRAIN5_ROWS,
@@ -74,6 +73,7 @@ def parse_args():
     ap.add_argument("--train-steps", type=int, default=50)
     ap.add_argument("--no-train", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="time training steps as eager launches")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the config-2 batch sweep")
     return ap.parse_args()
 
 
@@ -111,14 +111,20 @@ REASON_BITS = {
 
 
 class ClockSampler:
-    """Samples SM clock and clock-event reasons through NVML in a thread."""
+    """Samples SM clock and clock-event reasons through NVML in a thread.
 
-    def __init__(self, device_index: int, period_s: float = 0.005):
+    Samples are timestamped; ``mark_start`` / ``mark_stop`` bracket the timed
+    region and ``summary`` reports the samples inside it (plus the ones taken
+    under load in the warm-up just before it when the timed region is shorter
+    than a few sample periods)."""
+
+    def __init__(self, device_index: int, period_s: float = 0.001):
         self.samples = []
         self.period = period_s
         self._stop = threading.Event()
         self.ok = False
         self.max_mhz = None
+        self.t_start = self.t_stop = None
         try:
             import pynvml as nv
 
@@ -148,19 +154,28 @@ class ClockSampler:
         nv = self.nv
         while not self._stop.is_set():
             try:
-                self.samples.append((nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM), self._reasons()))
+                t = time.perf_counter()
+                self.samples.append((t, nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM), self._reasons()))
             except Exception:
                 pass
             time.sleep(self.period)
+
+    def mark_start(self):
+        self.t_start = time.perf_counter()
+
+    def mark_stop(self):
+        self.t_stop = time.perf_counter()
 
     def __enter__(self):
         if self.ok:
             self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
+            time.sleep(3 * self.period)  # first samples before the caller's work starts
         return self
 
     def __exit__(self, *a):
         if self.ok:
+            time.sleep(2 * self.period)
             self._stop.set()
             self.t.join()
 
@@ -168,32 +183,28 @@ class ClockSampler:
         if not self.ok or not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
                     "note": "NVML unavailable" if not self.ok else "no samples"}
-        mhz = [s[0] for s in self.samples]
+        t0 = self.t_start if self.t_start is not None else -1e30
+        t1 = self.t_stop if self.t_stop is not None else 1e30
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        used, window = inside, "timed region"
+        if len(inside) < 5:
+            # a short timed region: add the samples of the warm-up steps just
+            # before it (the same kernels under load) and the first after it
+            near = [s for s in self.samples if t0 - 0.05 <= s[0] <= t1 + 0.002]
+            used, window = near, "timed region and the 50 ms of warm-up before it"
+        if not used:
+            used, window = self.samples, "whole sampler run"
+        mhz = [s[1] for s in used]
         bits = 0
-        for _, r in self.samples:
-            bits |= int(r)
+        for s in used:
+            bits |= int(s[2])
         reasons = [n for b, n in REASON_BITS.items() if bits & b and n != "gpu_idle"]
-        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
-                "samples": len(mhz)}
+        return {"sm_mhz": statistics.median(mhz), "sm_min_mhz": min(mhz), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(mhz), "samples_in_timed_region": len(inside),
+                "window": window, "period_ms": 1e3 * self.period}
 
 
 # ---------------------------------------------------------------------- CPU legs
-def cpu_forward_rows_per_s(rows: int, seconds: float):
-    """The reference's PyTorch forward (kernel.py:163-171) in fp32 on all host
-    threads, on a bounded sample of the workload (`rows` rows)."""
-    import torch
-
-    from oracle.cpu_baseline import model_forward, set_all_threads, time_rows_per_s
-    from mlp_megakernel_b200.synthetic import make_weights, make_x
-
-    cores = set_all_threads()
-    x = make_x(rows, DIMS[0], "normal", 0).float()
-    ws = [w.float() for w in make_weights(DIMS)]
-    with torch.no_grad():
-        rps, calls, dt = time_rows_per_s(lambda: model_forward(x, ws), rows, seconds)
-    return rps, cores, calls, dt
-
-
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -231,6 +242,187 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def cpu_model_name() -> str:
+    """The host CPU model (the `model name` line of /proc/cpuinfo)."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
+def cpu_forward_full(rows: int, reps: int = 3):
+    """The reference's PyTorch forward (kernel.py:163-171) in fp32 on all host
+    threads at the bench's full row count: median of `reps` timed passes
+    (after one warm-up pass)."""
+    import torch
+
+    from oracle.cpu_baseline import model_forward, set_all_threads
+    from mlp_megakernel_b200.synthetic import make_weights, make_x
+
+    cores = set_all_threads()
+    x = make_x(rows, DIMS[0], "normal", 0).float()
+    ws = [w.float() for w in make_weights(DIMS)]
+    times = []
+    with torch.no_grad():
+        model_forward(x, ws)
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            model_forward(x, ws)
+            times.append(time.perf_counter() - t0)
+    return rows / statistics.median(times), cores, times
+
+
+def cpu_train_full(rows: int, reps: int = 3):
+    """The reference's PyTorch training step for BASELINE config 3 in fp32 on
+    all host threads: weight norm W = g v / ||v|| per output column, the
+    forward of kernel.py:163-171 and torch.autograd back to (dv, dg) and dx.
+    Median of `reps` timed steps after one warm-up step."""
+    from oracle.cpu_baseline import set_all_threads, train_step_wn
+    from mlp_megakernel_b200.synthetic import make_grad, make_weights, make_x
+
+    cores = set_all_threads()
+    x = make_x(rows, DIMS[0], "normal", 0).float()
+    g = make_grad(rows, DIMS[-1]).float()
+    ws = [w.float() for w in make_weights(DIMS)]
+    vs = [w.clone() for w in ws]
+    gs = [w.norm(dim=0) for w in ws]
+    train_step_wn(x, vs, gs, g)
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        train_step_wn(x, vs, gs, g)
+        times.append(time.perf_counter() - t0)
+    return rows / statistics.median(times), cores, times
+
+
+# ---------------------------------------------------------------------- batch sweep
+SWEEP_MIN_LOG2, SWEEP_MAX_LOG2 = 6, 22  # BASELINE config 2: M = 64 .. 4,194,304
+
+
+def _load_reference_kernel():
+    """The reference's own Triton forward (kernel.py, unmodified) from
+    baseline/_ref, or None when it is not present (the reference tree has no
+    package metadata, so it is placed there as files)."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.exists(os.path.join(ref_dir, "kernel.py")):
+        return None, "baseline/_ref/kernel.py not present"
+    try:
+        import importlib.util
+
+        spec = importlib.util.spec_from_file_location("mlpk_bench_ref_kernel", os.path.join(ref_dir, "kernel.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return mod, None
+    except Exception as e:  # e.g. triton missing on the box
+        return None, f"import failed: {type(e).__name__}: {e}"[:200]
+
+
+def _graph_us_per_call(fn, calls: int, reps: int = 5) -> float:
+    """Device time per call: `calls` calls captured in one CUDA graph,
+    replayed `reps` times between CUDA events (the graph-replay method of
+    profile.py:230-260)."""
+    import torch
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(calls):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = 1e3 * e0.elapsed_time(e1) / (reps * calls)
+    del g
+    return us
+
+
+def _eager_us_per_call(fn, calls: int) -> float:
+    """Host wall time per call of back-to-back eager calls (synchronised
+    before and after): the per-call latency a Python caller sees, the
+    reference's "non-graph" figure (README.md:240-249)."""
+    import torch
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(calls):
+        fn()
+    torch.cuda.synchronize()
+    return 1e6 * (time.perf_counter() - t0) / calls
+
+
+def run_sweep(x_full, ws, peaks):
+    """the 3L128 forward at M = 64 .. 4,194,304 (powers of
+    2), per call: device time replayed from a CUDA graph, host per-call time
+    of eager calls through ``fused_mlp_fwd`` (the drop-in API), rows/s and the
+    fraction of the HBM roofline; the reference's Triton kernel beside it when
+    baseline/_ref holds it."""
+    import torch
+
+    from mlp_megakernel_b200 import fused_mlp_fwd
+
+    ref, why = _load_reference_kernel()
+    out_full = torch.empty((x_full.shape[0], DIMS[-1]), dtype=torch.float16, device=x_full.device)
+    rows_out = []
+    for lg in range(SWEEP_MIN_LOG2, SWEEP_MAX_LOG2 + 1):
+        M = 1 << lg
+        if M > x_full.shape[0]:
+            break
+        x, out = x_full[:M], out_full[:M]
+        ours = lambda: fused_mlp_fwd(x, *ws, out=out)  # noqa: E731
+        calls = max(1, min(64, (1 << 20) // M))
+        n_eager = max(20, min(500, (1 << 24) // M))
+        g_us = _graph_us_per_call(ours, calls)
+        e_us = _eager_us_per_call(ours, n_eager)
+        gbs = BYTES_PER_ROW * M / (g_us * 1e-6) / 1e9
+        row = {"M": M, "graph_us": g_us, "eager_us": e_us, "rows_per_s": M / (g_us * 1e-6),
+               "eager_rows_per_s": M / (e_us * 1e-6), "hbm_frac": gbs / peaks["hbm_gbs"],
+               "l2_resident": BYTES_PER_ROW * M < 100e6}
+        if ref is not None:
+            try:
+                rfn = lambda: ref._fused_mlp_fwd(x, *ws)  # noqa: E731
+                rg = _graph_us_per_call(rfn, calls)
+                re_ = _eager_us_per_call(rfn, n_eager)
+                row.update({"triton_ref_graph_us": rg, "triton_ref_eager_us": re_,
+                            "speedup_graph": rg / g_us, "speedup_eager": re_ / e_us})
+            except Exception as e:
+                why = f"reference Triton kernel failed at M={M}: {type(e).__name__}: {e}"[:200]
+                ref = None
+        rows_out.append(row)
+    res = {
+        "workload": "BASELINE config 2: 3L128 forward, M = 64 .. 4,194,304 (powers of 2), x ~ N(0,1) "
+                    "seed 0, W ~ U(+-1/sqrt(in)) seed 1, one GPU; rows with l2_resident = true have "
+                    "inputs and outputs that fit in L2 (no flush: the small-batch serving regime)",
+        "graph_us": "device time per call, calls replayed from a CUDA graph (profile.py:230-260 method)",
+        "eager_us": "host time per call of back-to-back fused_mlp_fwd calls (Python + ctypes + launch)",
+        "rows": rows_out,
+    }
+    if ref is not None:
+        res["triton_reference"] = ("the reference's unmodified kernel.py _fused_mlp_fwd (kernel.py:130-156), "
+                                   "Triton JIT for this GPU, same inputs, timed the same two ways")
+    else:
+        res["triton_reference_unavailable"] = why
+    return res
+
+
 # ---------------------------------------------------------------------- GPU arm
 def run_mlpk(args):
     import torch
@@ -262,20 +454,22 @@ def run_mlpk(args):
 
     out = torch.empty((M, DIMS[-1]), dtype=torch.float16, device="cuda")
     step = lambda: fused_mlp_fwd(x, *ws, out=out)  # noqa: E731
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        clk.mark_start()
         ev0.record(stream)
         for _ in range(args.steps):
             step()
         ev1.record(stream)
         torch.cuda.synchronize()
+        clk.mark_stop()
     barrier()
     ms = ev0.elapsed_time(ev1)
     if dist is not None:
@@ -311,6 +505,10 @@ def run_mlpk(args):
         t = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
+
+    sweep = None
+    if world == 1 and not args.no_sweep:
+        sweep = run_sweep(x, ws, load_peaks())
 
     train = train5 = train256 = train5w = None
     if not args.no_train:
@@ -390,14 +588,26 @@ def run_mlpk(args):
         line["fwd_bwd_w256"] = train256
     if train5w is not None:
         line["fwd_bwd_5l_weak"] = train5w
+    if sweep is not None:
+        line["sweep"] = sweep
     if world == 1 and not args.no_cpu_baseline:
-        rows = 65536
-        rps, cores, calls, dt = cpu_forward_rows_per_s(rows, args.cpu_seconds)
+        cpu = cpu_model_name()
+        rps, cores, times = cpu_forward_full(M)
         line["cpu_baseline"] = {
-            "value": rps, "unit": "rows/s", "cores": cores, "kind": "port",
-            "sample": f"{rows} rows of the 3L128 forward x {calls} calls ({dt:.1f} s), "
-                      f"reference PyTorch formula (kernel.py:163-171) in fp32 on {cores} threads",
+            "value": rps, "unit": "rows/s", "cores": cores, "kind": "port", "cpu_model": cpu,
+            "sample": f"the full M={M} rows of the 3L128 forward, median of {len(times)} passes "
+                      f"({', '.join(f'{t:.2f}' for t in times)} s), reference PyTorch formula "
+                      f"(kernel.py:163-171) in fp32 on {cores} threads",
         }
+        if train is not None:
+            trows = args.train_rows
+            trps, tcores, ttimes = cpu_train_full(trows)
+            train["cpu_baseline"] = {
+                "value": trps, "unit": "rows/s", "cores": tcores, "kind": "port", "cpu_model": cpu,
+                "sample": f"BASELINE config 3 training step at M={trows} (weight norm, forward, "
+                          f"torch.autograd backward to dx, dv, dg), median of {len(ttimes)} steps "
+                          f"({', '.join(f'{t:.2f}' for t in ttimes)} s), fp32 on {tcores} threads",
+            }
     print(json.dumps(line), flush=True)
 
 
@@ -425,6 +635,31 @@ TRAIN_SPECS = {
              "workload": "BASELINE config 5: 3L D=H=OUT=256 training step (streamed weights), "
                          "global M={G} rows, {M} per GPU"},
 }
+
+
+# Per-kernel DRAM bytes of one launch, from the ncu captures summarised in
+# profiles/ (name, rows of the captured launch); a step's traffic is their
+# sum scaled to the step's rows (the traffic of these kernels grows with the
+# rows: activations in and out; weights come from L2).
+TRAIN_TRAFFIC = {
+    "3L128": [("trainfwd_3L128_M262K", 262144), ("bwd_3L128_M262K", 262144)],
+    "5L": [("trainfwd_5L_M262K", 262144), ("bwd_5L_M262K", 262144)],
+    "5L_weak": [("trainfwd_5L_M262K", 262144), ("bwd_5L_M262K", 262144)],
+    "W256": [("trainfwd_W256_M131K", 131072), ("dgrad_W256_M131K", 131072), ("wgrad_W256_M131K", 131072)],
+}
+
+
+def step_traffic(name: str, rows: int):
+    parts = TRAIN_TRAFFIC.get(name)
+    if not parts:
+        return None, None
+    total = 0.0
+    for prof, cap_rows in parts:
+        b = load_traffic(prof)
+        if b is None:
+            return None, None
+        total += b * rows / cap_rows
+    return int(total), "sum of " + ", ".join(f"profiles/{p}.md" for p, _ in parts) + " scaled to the step's rows"
 
 
 def run_training(args, world, rank, dist, barrier, name, rows):
@@ -568,6 +803,7 @@ def run_training(args, world, rank, dist, barrier, name, rows):
     if red is not None:
         red.close()
     peaks = load_peaks()
+    traffic, traffic_src = step_traffic(name, M)
     per_step = ms / 1e3 / args.train_steps
     tflops = flop_per_row * M / per_step / 1e12
     gbs = bytes_per_row * M / per_step / 1e9
@@ -593,7 +829,8 @@ def run_training(args, world, rank, dist, barrier, name, rows):
                      "achieved": tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": tflops / peaks["bf16_tflops"],
                      "rows_frac_of_roofline": (M / per_step) / roof_rows,
-                     "achieved_algorithmic_gbs": gbs, "traffic": None,
+                     "achieved_algorithmic_gbs": gbs, "traffic": traffic, "traffic_source": traffic_src,
+                     "traffic_unit": "DRAM bytes per step (all of the step's kernels)",
                      "flop_per_row": flop_per_row, "algorithmic_bytes_per_row": bytes_per_row},
         "e2e": {"value": world * M * n_e2e / (e2e_ms / 1e3), "unit": "rows/s",
                 "h2d_bytes_per_step": M * (dims[0] + dims[-1]) * 2,
