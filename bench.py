@@ -21,7 +21,9 @@ the forward), all bytes crossing the host link every step.
 The same JSON line carries the training steps (forward + backward through
 the C ABI on preallocated buffers, replayed as one CUDA graph per step, dW
 summed over the ranks by the library's NVLink peer-memory kernel when N > 1):
-``fwd_bwd`` (3L128 with weight norm, 262,144 rows per GPU),
+``fwd_bwd`` (3L128 with weight norm and fp32 activation
+storage, 262,144 rows per GPU), ``fwd_bwd_h16`` (the same saving fp16
+activations, with its gradients' difference from the fp32-storage step),
 ``fwd_bwd_5l`` (config 4: 5-layer with weight norm, 1,048,576 rows in total,
 strong scaling), ``fwd_bwd_5l_weak`` (N > 1 only: the same with 1,048,576 rows
 per GPU) and ``fwd_bwd_w256`` (config 5: D = H = OUT = 256, 1,048,576 rows in
@@ -510,17 +512,27 @@ def run_mlpk(args):
     if world == 1 and not args.no_sweep:
         sweep = run_sweep(x, ws, load_peaks())
 
-    train = train5 = train256 = train5w = None
+    train = train16 = train5 = train256 = train5w = None
     if not args.no_train:
         from mlp_megakernel_b200.dp import shard_rows
 
         train = run_training(args, world, rank, dist, barrier, "3L128", args.train_rows)
+        train16 = run_training(args, world, rank, dist, barrier, "3L128_h16", args.train_rows)
+        # the fp16-storage step against the fp32-storage step (same inputs):
+        # relative L2 difference of the gradients the step returns
+        g32, g16 = train.pop("_grads"), train16.pop("_grads")
+        train16["grad_diff_vs_fp32_storage"] = {
+            name: float((a16.double() - a32.double()).norm() / a32.double().norm().clamp_min(1e-30))
+            for name, a32, a16 in zip(("dx", "dv", "dg"), g32, g16)}
         a, b = shard_rows(args.train5_rows, rank, world)
         train5 = run_training(args, world, rank, dist, barrier, "5L", b - a)
         a, b = shard_rows(args.train256_rows, rank, world)
         train256 = run_training(args, world, rank, dist, barrier, "W256", b - a)
         train5w = (run_training(args, world, rank, dist, barrier, "5L_weak", args.train5_rows)
                    if world > 1 else None)  # at N = 1 it is the fwd_bwd_5l run
+        for t in (train5, train256, train5w):
+            if t is not None:
+                t.pop("_grads")
 
     clocks = clk.summary()
     if dist is not None:
@@ -582,6 +594,8 @@ def run_mlpk(args):
     }
     if train is not None:
         line["fwd_bwd"] = train
+    if train16 is not None:
+        line["fwd_bwd_h16"] = train16
     if train5 is not None:
         line["fwd_bwd_5l"] = train5
     if train256 is not None:
@@ -613,27 +627,32 @@ def run_mlpk(args):
 
 TRAIN_SPECS = {
     # 3L128 with weight norm, split-K regime, rows per GPU fixed
-    "3L128": {"dims": (128, 128, 128, 128), "x_dist": "normal", "x_seed": 0, "strong": False,
+    "3L128": {"dims": (128, 128, 128, 128), "x_dist": "normal", "x_seed": 0, "strong": False, "h32": True,
               "metric": "fused MLP fwd+bwd rows/s (3L128 with weight norm)",
               "workload": "BASELINE config 3: 3L D=H=OUT=128 training step with weight norm, "
-                          "M={M} rows per GPU"},
+                          "fp32 activation storage, M={M} rows per GPU"},
+    # the same step saving the fp16 operand copy of h (half the saved-activation traffic)
+    "3L128_h16": {"dims": (128, 128, 128, 128), "x_dist": "normal", "x_seed": 0, "strong": False,
+                  "metric": "fused MLP fwd+bwd rows/s (3L128 with weight norm)",
+                  "workload": "BASELINE config 3 shape with fp16 activation storage (not the config as "
+                              "written): 3L D=H=OUT=128 training step with weight norm, M={M} rows per GPU"},
     # 5L 32-64-64-64-64-16 with weight norm, global M = 1,048,576
     # split over the ranks (strong scaling, NCCL all-reduce of dW)
     "5L": {"dims": (32, 64, 64, 64, 64, 16), "x_dist": "uniform", "x_seed": 3, "strong": True,
            "metric": "fused MLP fwd+bwd rows/s (5L 32-64-64-64-64-16 with weight norm)",
            "workload": "BASELINE config 4: 5L D=32 H=64 OUT=16 training step with weight norm, "
-                       "global M={G} rows, {M} per GPU"},
+                       "fp16 activation storage, global M={G} rows, {M} per GPU"},
     # the same 5-layer step with the rows per GPU fixed (1,048,576 each): weak scaling
     "5L_weak": {"dims": (32, 64, 64, 64, 64, 16), "x_dist": "uniform", "x_seed": 3, "strong": False,
                 "metric": "fused MLP fwd+bwd rows/s (5L 32-64-64-64-64-16 with weight norm)",
                 "workload": "BASELINE config 4 shape, rows per GPU fixed: 5L D=32 H=64 OUT=16 training "
-                            "step with weight norm, M={M} rows per GPU"},
+                            "step with weight norm, fp16 activation storage, M={M} rows per GPU"},
     # wide 3L D=H=OUT=256 (weights streamed), plain weights,
     # global M = 1,048,576 split over the ranks
     "W256": {"dims": (256, 256, 256, 256), "x_dist": "normal", "x_seed": 4, "strong": True, "wn": False,
              "metric": "fused MLP fwd+bwd rows/s (wide 3L D=H=OUT=256)",
              "workload": "BASELINE config 5: 3L D=H=OUT=256 training step (streamed weights), "
-                         "global M={G} rows, {M} per GPU"},
+                         "fp16 activation storage, global M={G} rows, {M} per GPU"},
 }
 
 
@@ -642,7 +661,8 @@ TRAIN_SPECS = {
 # sum scaled to the step's rows (the traffic of these kernels grows with the
 # rows: activations in and out; weights come from L2).
 TRAIN_TRAFFIC = {
-    "3L128": [("trainfwd_3L128_M262K", 262144), ("bwd_3L128_M262K", 262144)],
+    "3L128": [("trainfwd_f32h_3L128_M262K", 262144), ("bwd_f32h_3L128_M262K", 262144)],
+    "3L128_h16": [("trainfwd_3L128_M262K", 262144), ("bwd_3L128_M262K", 262144)],
     "5L": [("trainfwd_5L_M262K", 262144), ("bwd_5L_M262K", 262144)],
     "5L_weak": [("trainfwd_5L_M262K", 262144), ("bwd_5L_M262K", 262144)],
     "W256": [("trainfwd_W256_M131K", 131072), ("dgrad_W256_M131K", 131072), ("wgrad_W256_M131K", 131072)],
@@ -691,7 +711,9 @@ def run_training(args, world, rank, dist, barrier, name, rows):
     W = [torch.empty_like(w) for w in ws0]
     inv = torch.empty_like(g_all)
     out = torch.empty((M, dims[-1]), dtype=torch.float16, device=dev)
-    hs = [torch.empty((M, d), dtype=torch.float16, device=dev) for d in dims[1:-1]]
+    h32 = spec.get("h32", False)
+    h_code = _lib.H_F32 if h32 else _lib.H_F16
+    hs = [torch.empty((M, d), dtype=torch.float32 if h32 else torch.float16, device=dev) for d in dims[1:-1]]
     dx = torch.empty_like(x)
     dw = torch.empty_like(v_all)
     dv = torch.empty_like(v_all)
@@ -715,10 +737,10 @@ def run_training(args, world, rank, dist, barrier, name, rows):
         if wn:
             _lib.check("wn_fwd", lib.mlpk_wn_fwd(shape, v_all.data_ptr(), g_all.data_ptr(), Wp,
                                                  inv.data_ptr(), st))
-        _lib.check("train_fwd", lib.mlpk_train_fwd(shape, M, x.data_ptr(), Wp, out.data_ptr(), Hp, st))
+        _lib.check("train_fwd", lib.mlpk_train_fwd_ex(shape, M, x.data_ptr(), Wp, out.data_ptr(), Hp, h_code, st))
         local = red.local_buffer(dw) if red is not None else dw
-        _lib.check("bwd", lib.mlpk_bwd(shape, M, x.data_ptr(), Wp, Hp, g.data_ptr(), dx.data_ptr(),
-                                       work.data_ptr(), work.numel(), local.data_ptr(), st))
+        _lib.check("bwd", lib.mlpk_bwd_ex(shape, M, x.data_ptr(), Wp, Hp, h_code, g.data_ptr(), dx.data_ptr(),
+                                          work.data_ptr(), work.numel(), local.data_ptr(), st))
         if red is not None:
             red.reduce(local, dw)
         if wn:
@@ -811,6 +833,7 @@ def run_training(args, world, rank, dist, barrier, name, rows):
     hbm_rows = peaks["hbm_gbs"] * 1e9 / bytes_per_row
     roof_rows = min(tensor_rows, hbm_rows)
     return {
+        "_grads": (dx.detach().clone(), dv.detach().clone(), dg.detach().clone()),
         "metric": spec["metric"],
         "value": world * M * args.train_steps / (ms / 1e3),
         "unit": "rows/s",
@@ -819,6 +842,7 @@ def run_training(args, world, rank, dist, barrier, name, rows):
         "scaling": "strong" if spec["strong"] else "weak",
         "config": {"workload": spec["workload"].format(M=M, G=world * M),
                    "dims": list(dims), "rows_per_gpu": M, "global_rows": world * M,
+                   "activation_storage": "fp32" if h32 else "fp16",
                    "parallelism": f"dp{world}" + ((" (fp32 dW summed by the NVLink peer-memory kernel)" if peer
                                                    else " (NCCL all-reduce of fp32 dW)") if world > 1 else ""),
                    "launch": "eager" if args.no_graph else "CUDA graph of the whole step",
@@ -835,7 +859,7 @@ def run_training(args, world, rank, dist, barrier, name, rows):
         "e2e": {"value": world * M * n_e2e / (e2e_ms / 1e3), "unit": "rows/s",
                 "h2d_bytes_per_step": M * (dims[0] + dims[-1]) * 2,
                 "d2h_bytes_per_step": ((dv.numel() + dg.numel()) if wn else dw.numel()) * 4,
-                "api": "C ABI (" + ("mlpk_wn_fwd, " if wn else "") + "mlpk_train_fwd, mlpk_bwd"
+                "api": "C ABI (" + ("mlpk_wn_fwd, " if wn else "") + "mlpk_train_fwd_ex, mlpk_bwd_ex"
                        + (", mlpk_wn_bwd" if wn else "") + ") with pinned host buffers"},
         "gpu_launches": launches_per_step * args.train_steps,
     }

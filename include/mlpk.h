@@ -9,8 +9,9 @@
  * Conventions (mirroring the reference, kernel.py:130-156):
  *   - weights are [in, out] row-major (out = x @ W), fp16;
  *   - activations x / out / grad_out / dx are [M, d] row-major fp16;
- *   - saved training activations are fp16 (the next GEMM's operand), weight
- *     gradients and weight-norm parameters fp32;
+ *   - saved training activations are fp16 (the next GEMM's operand) or, with
+ *     the _ex entry points, fp32; weight gradients and weight-norm parameters
+ *     fp32;
  *   - every pointer must be 16-byte aligned and tensors contiguous;
  *   - all work is enqueued on `stream`; no entry point synchronises the host
  *     (except mlpk_device_status, which reads a device word);
@@ -82,8 +83,26 @@ int mlpk_train_supported(const mlpk_shape* shape);
 int mlpk_train_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
                    void* out, void* const* h_saved, mlpk_stream_t stream);
 
-/* Bytes of device workspace mlpk_bwd needs for M rows on the current device
- * (one fp32 weight-gradient partial per persistent CTA); -1 if unsupported. */
+/* ---- Saved-activation precision.  The reference's training forward stores
+ * the hidden activations in fp32 "to avoid numerical loss in the backward
+ * sigmoid derivative" (README.md:30; mlp_fused.md:52-61); the _ex entry points
+ * below take that choice: MLPK_H_F32 saves h_l in fp32 (the backward computes
+ * softplus' = 1 - e^{-h} from it and rounds h to fp16 only as its
+ * weight-gradient operand, the value the forward's next GEMM consumed),
+ * MLPK_H_F16 saves the fp16 operand copy (half the traffic; what
+ * mlpk_train_fwd / mlpk_bwd do).  fp32 is served by every network of the fused
+ * backward (mlpk_train_supported_ex); the streamed-weight networks (256 wide,
+ * 128 wide at 4 and 5 layers) save fp16 only. */
+#define MLPK_H_F16 0
+#define MLPK_H_F32 1
+int mlpk_train_supported_ex(const mlpk_shape* shape, int h_dtype);
+/* mlpk_train_fwd with h_saved[l] of h_dtype ([M, dims[l+1]] fp16 or fp32). */
+int mlpk_train_fwd_ex(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
+                      void* out, void* const* h_saved, int h_dtype, mlpk_stream_t stream);
+
+/* Bytes of device workspace mlpk_bwd (and mlpk_bwd_ex, either precision)
+ * needs for M rows on the current device (one fp32 weight-gradient partial
+ * per persistent CTA); -1 if unsupported. */
 int64_t mlpk_bwd_workspace_size(const mlpk_shape* shape, int64_t M);
 
 /* Backward: from x, W, the saved h and grad_out ([M, dims[L]] fp16) writes
@@ -95,6 +114,10 @@ int64_t mlpk_bwd_workspace_size(const mlpk_shape* shape, int64_t M);
 int mlpk_bwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
              const void* const* h_saved, const void* grad_out, void* dx, void* workspace,
              int64_t workspace_bytes, float* dW, mlpk_stream_t stream);
+/* mlpk_bwd reading h_saved of h_dtype (as written by mlpk_train_fwd_ex). */
+int mlpk_bwd_ex(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
+                const void* const* h_saved, int h_dtype, const void* grad_out, void* dx, void* workspace,
+                int64_t workspace_bytes, float* dW, mlpk_stream_t stream);
 
 /* Weight norm forward, all layers in one launch: W_l = g_l * v_l / ||v_l||
  * per output column.  v_all: fp32 concat of v_l [dims[l], dims[l+1]]; g_all and

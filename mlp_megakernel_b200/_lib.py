@@ -45,9 +45,13 @@ SIGNATURES = {
     "mlpk_fwd": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _vp, _vp]),
     "mlpk_train_supported": (ctypes.c_int, [_SHAPE_P]),
     "mlpk_train_fwd": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _vp, _VPP, _vp]),
+    "mlpk_train_supported_ex": (ctypes.c_int, [_SHAPE_P, ctypes.c_int]),
+    "mlpk_train_fwd_ex": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _vp, _VPP, ctypes.c_int, _vp]),
     "mlpk_bwd_workspace_size": (ctypes.c_int64, [_SHAPE_P, ctypes.c_int64]),
     "mlpk_bwd": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _VPP, _vp, _vp, _vp,
                                 ctypes.c_int64, _vp, _vp]),
+    "mlpk_bwd_ex": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _VPP, ctypes.c_int, _vp, _vp, _vp,
+                                   ctypes.c_int64, _vp, _vp]),
     "mlpk_bwd_noalloc": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _VPP, _vp, _vp, _vp,
                                         _vp]),
     "mlpk_wn_fwd": (ctypes.c_int, [_SHAPE_P, _vp, _vp, _VPP, _vp, _vp]),
@@ -66,6 +70,8 @@ SIGNATURES = {
                                      ctypes.c_int64, _vp]),
 }
 FWD_HOST_CHUNK_ROWS = 131072
+H_F16 = 0  # MLPK_H_F16: saved activations in fp16
+H_F32 = 1  # MLPK_H_F32: saved activations in fp32 (the reference's storage)
 PEER_HANDLE_BYTES = 64
 PEER_MAX_RANKS = 8
 
@@ -136,8 +142,8 @@ def shape_supported(dims) -> bool:
     return bool(lib().mlpk_shape_supported(ctypes.byref(shape_struct(dims))))
 
 
-def train_supported(dims) -> bool:
-    return bool(lib().mlpk_train_supported(ctypes.byref(shape_struct(dims))))
+def train_supported(dims, h_dtype: int = H_F16) -> bool:
+    return bool(lib().mlpk_train_supported_ex(ctypes.byref(shape_struct(dims)), h_dtype))
 
 
 def ptr_array(ptrs) -> ctypes.Array:

@@ -52,7 +52,14 @@ struct alignas(64) BwdMaps {
   int dx_cols;
 };
 
-template <class NetT>
+// H32: the saved activations are fp32 (the reference's storage, README.md:30).
+// Each h_l arrives as two ring slots (columns [0, d_l/2) and [d_l/2, d_l), in
+// 32-column fp32 chunks); the epilogue computes the sigmoid from the fp32
+// values and then overwrites the two slots in place with the fp16 h_l (the
+// weight-gradient operand, rounded as the forward rounded it for the next
+// GEMM) and dz_l, so no separate dz tile is needed; each layer's
+// weight-gradient GEMM is issued after that epilogue.  One tile in flight.
+template <class NetT, bool H32 = false>
 struct BwdCfg {
   static constexpr int L = NetT::L;
   static constexpr int D0 = NetT::template D<0>();
@@ -103,13 +110,22 @@ struct BwdCfg {
   static constexpr int TILE_BYTES = align_up(tile_bytes(kTileM, DMAX), 1024);
   static constexpr int W_TOTAL = NetT::w_total();
   static constexpr int ZERO_BYTES = any_pad() ? 16384 : 0;  // 128 rows x 128 B
+  static constexpr int G_TILES = H32 ? 0 : 1;  // dz tiles (G) per tile slot
   // ring slots that fit in shared memory next to the weights, `ns` dz tiles
   // (G), the zero chunk and the barriers: w_full, slot_full[8],
   // slot_empty[8], then per tile slot acc_full, acc_free, wg_done, dz_full,
-  // out_ready; mma_done
+  // out_ready; mma_done; rd_done
   __host__ __device__ static constexpr int ring_fit(int ns) {
-    return (232448 - 1024 - 16 - 8 * (2 + 2 * 8 + 5 * ns) - (W_TOTAL + ns * TILE_BYTES) - ZERO_BYTES) /
+    return (232448 - 1024 - 16 - 8 * (3 + 2 * 8 + 5 * ns) - (W_TOTAL + ns * G_TILES * TILE_BYTES) -
+            ZERO_BYTES) /
            TILE_BYTES;
+  }
+  // every hidden width splits into two fp32 halves of whole 32-column chunks,
+  // each fitting a ring slot
+  __host__ __device__ static constexpr bool h32_ok() {
+    for (int l = 1; l < L; ++l)
+      if ((NetT::dim(l) / 2) % 32 != 0 || kTileM * (NetT::dim(l) / 2) * 4 > TILE_BYTES) return false;
+    return true;
   }
   // Tiles in flight ("slots"): two when TMEM holds a second dgrad accumulator
   // next to the dW accumulators and the ring can hold one tile's loads plus
@@ -117,7 +133,13 @@ struct BwdCfg {
   // alternates the slots' layer steps so one slot's epilogue overlaps the
   // other slot's MMAs.
   static constexpr int NS =
-      (dw_col(L) + 2 * ACC_W <= 512 && (ring_fit(2) > 8 ? 8 : ring_fit(2)) >= L + 3) ? 2 : 1;
+      (!H32 && dw_col(L) + 2 * ACC_W <= 512 && (ring_fit(2) > 8 ? 8 : ring_fit(2)) >= L + 3) ? 2 : 1;
+  // loads per tile: g, then h_{L-1} .. h_1 (one slot each, or two fp32 halves
+  // each), then x
+  static constexpr int NLD = H32 ? 2 * L : L + 1;
+  // load index (within a tile) of h_l: fp16 -> its slot; fp32 -> its low
+  // half (the high half is the next load)
+  __host__ __device__ static constexpr int h_load(int l) { return H32 ? 1 + 2 * (L - 1 - l) : L - l; }
   static constexpr int THREADS = (2 + NS * EPI_WARPS) * 32;
   __host__ __device__ static constexpr bool groups_ok() {
     for (int l = 0; l < L; ++l) {
@@ -127,12 +149,12 @@ struct BwdCfg {
     return true;
   }
   static constexpr int OFF_G = W_TOTAL;                  // G of slot s at OFF_G + s * TILE_BYTES
-  static constexpr int OFF_RING = OFF_G + NS * TILE_BYTES;
+  static constexpr int OFF_RING = OFF_G + NS * G_TILES * TILE_BYTES;
   static constexpr int RING_FIT = ring_fit(NS);
   static constexpr int RING = RING_FIT > 8 ? 8 : RING_FIT;
   static constexpr int OFF_ZERO = OFF_RING + RING * TILE_BYTES;
   static constexpr int OFF_BAR = OFF_ZERO + ZERO_BYTES;
-  static constexpr int NUM_BARS = 2 + 2 * RING + 5 * NS;
+  static constexpr int NUM_BARS = 2 + 2 * RING + 5 * NS + 1;
   static constexpr int OFF_MISC = OFF_BAR + 8 * NUM_BARS;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static constexpr int ACC_COL = dw_col(L);
@@ -152,6 +174,9 @@ struct BwdCfg {
   static_assert(NS == 1 || RING >= L + 3, "ring too shallow for two tiles in flight");
   static_assert(TMEM_COLS_RAW <= 512, "dW + dgrad accumulators exceed TMEM");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
+  // fp32 saved activations: a ring of 3 keeps every load's slot free of the
+  // step that waits for it (see the producer)
+  static_assert(!H32 || (RING >= 3 && h32_ok()), "fp32 saved activations: ring too shallow or widths");
 };
 
 // this thread's row of an fp16 operand tile of extent N: 8 values at column c
@@ -171,6 +196,16 @@ __device__ __forceinline__ void st_tile_row8(uint32_t tile_base, uint32_t row, i
   constexpr int C = chunk_elems(N);
   constexpr int P = pitch_bytes(N);
   st_shared_v4(tile_base + (c / C) * (kTileM * P) + swz_off<P>(row, (c % C) / 8), a, b, d, e);
+}
+
+// this thread's row of an fp32 tile stored as 32-column chunks (128-byte
+// rows, 128B swizzle): 4 values at column c (c % 4 == 0)
+__device__ __forceinline__ uint4 ld_tile_row4_f32(uint32_t tile_base, uint32_t row, int c) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(tile_base + (c / 32) * (kTileM * 128) + swz_off<128>(row, (c % 32) / 4)));
+  return v;
 }
 
 __device__ __forceinline__ float2 half2_to_float2(uint32_t v) {
@@ -194,13 +229,21 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[CW]) 
   else tmem_ld_wait_x64(taddr, r);
 }
 
-template <class NetT>
-__global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
+// The layer index l = L - 1 - i of static_for iteration i, as a type.
+template <int L, class IC>
+__device__ __forceinline__ constexpr auto lc_rev(IC) {
+  return std::integral_constant<int, L - 1 - IC::value>{};
+}
+
+template <class NetT, bool H32 = false>
+__global__ void __launch_bounds__(BwdCfg<NetT, H32>::THREADS, 1)
     mlp_bwd_kernel(const __grid_constant__ BwdMaps<NetT::L> maps, int num_tiles) {
-  using Cfg = BwdCfg<NetT>;
+  using Cfg = BwdCfg<NetT, H32>;
   constexpr int L = Cfg::L;
   constexpr int R = Cfg::RING;
-  constexpr int NLD = L + 1;  // loads per tile: k = 0 g, k = 1..L-1 h_{L-k}, k = L x
+  // loads per tile: k = 0 g; fp16 h: k = 1..L-1 h_{L-k}; fp32 h: k = 1..2L-2
+  // the halves (lo, hi) of h_{L-1}, .., h_1; k = NLD-1 x
+  constexpr int NLD = Cfg::NLD;
   constexpr int NG = Cfg::NG;
   constexpr int EW = Cfg::EPI_WARPS;  // epilogue warps per slot
   constexpr int NS = Cfg::NS;
@@ -220,10 +263,13 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
   // per tile slot s
   auto bar_acc_full = [&](int s) { return s_bar + 8u + 16u * R + 40u * s; };  // dgrad accumulator written
   auto bar_acc_free = [&](int s) { return bar_acc_full(s) + 8; };   // ... and read (once per tile)
-  auto bar_wg_done = [&](int s) { return bar_acc_full(s) + 16; };   // this layer's wgrad read its operands
-  auto bar_dz_full = [&](int s) { return bar_acc_full(s) + 24; };   // G holds the next layer's dz
+  auto bar_wg_done = [&](int s) { return bar_acc_full(s) + 16; };   // a wgrad read its operands
+  auto bar_dz_full = [&](int s) { return bar_acc_full(s) + 24; };   // the next layer's dz is staged
   auto bar_out_ready = [&](int s) { return bar_acc_full(s) + 32; }; // dx staged
   const uint32_t bar_mma_done = bar_acc_full(NS);
+  // (H32) every epilogue warp has read its fp32 h of the current layer: the
+  // two half-slots may be overwritten in place
+  const uint32_t bar_rd_done = bar_mma_done + 8u;
   const uint32_t s_tmem_slot = sbase + Cfg::OFF_MISC;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + Cfg::OFF_MISC + 4);
 
@@ -244,6 +290,7 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
       mbar_init(bar_out_ready(s), EW);
     }
     mbar_init(bar_mma_done, 1);
+    mbar_init(bar_rd_done, EW);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -283,9 +330,19 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
         mbar_arrive_expect_tx(bar, kTileM * d * 2);
         for (int c = 0; c < d / C; ++c) tma_load_2d(dst + c * kTileM * P, map, bar, c * C, t * kTileM);
       };
+      // fp32 half `half` of an h tile of width d: d/64 chunks of 32 columns
+      auto load_half_f32 = [&](const CUtensorMap* map, uint32_t dst, uint32_t bar, int d, int half, int t) {
+        const int hw = d / 2;
+        mbar_arrive_expect_tx(bar, kTileM * hw * 4);
+        for (int c = 0; c < hw / 32; ++c)
+          tma_load_2d(dst + c * kTileM * 128, map, bar, half * hw + c * 32, t * kTileM);
+      };
       auto prefetch_tile = [&](const CUtensorMap* map, int d, int t) {
         const int C = d < 64 ? d : 64;
         for (int c = 0; c < d / C; ++c) tma_prefetch_l2_2d(map, c * C, t * kTileM);
+      };
+      auto prefetch_tile_f32 = [&](const CUtensorMap* map, int d, int t) {
+        for (int c = 0; c < d / 32; ++c) tma_prefetch_l2_2d(map, c * 32, t * kTileM);
       };
       bool ok = true;
       int issued = 0;
@@ -299,7 +356,8 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
           prefetch_tile(&maps.g, Cfg::DL, tn);
           static_for<1, L>([&](auto hc) {
             constexpr int l = decltype(hc)::value;
-            prefetch_tile(&maps.h[l - 1], NetT::template D<l>(), tn);
+            if constexpr (H32) prefetch_tile_f32(&maps.h[l - 1], NetT::template D<l>(), tn);
+            else prefetch_tile(&maps.h[l - 1], NetT::template D<l>(), tn);
           });
           prefetch_tile(&maps.x, Cfg::D0, tn);
         }
@@ -310,9 +368,16 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
           const int r = n % R;
           ok = mbar_wait(bar_slot_empty(r), ((n / R) & 1) ^ 1, abort_flag, kDevTimeoutEmpty);
           if (!ok) return;
-          if constexpr (k == 0) load_tile(&maps.g, slot_addr(r), bar_slot_full(r), Cfg::DL, t);
-          else if constexpr (k == L) load_tile(&maps.x, slot_addr(r), bar_slot_full(r), Cfg::D0, t);
-          else load_tile(&maps.h[L - k - 1], slot_addr(r), bar_slot_full(r), NetT::template D<L - k>(), t);
+          if constexpr (k == 0) {
+            load_tile(&maps.g, slot_addr(r), bar_slot_full(r), Cfg::DL, t);
+          } else if constexpr (k == NLD - 1) {
+            load_tile(&maps.x, slot_addr(r), bar_slot_full(r), Cfg::D0, t);
+          } else if constexpr (H32) {
+            constexpr int l = L - 1 - (k - 1) / 2;
+            load_half_f32(&maps.h[l - 1], slot_addr(r), bar_slot_full(r), NetT::template D<l>(), (k - 1) % 2, t);
+          } else {
+            load_tile(&maps.h[L - k - 1], slot_addr(r), bar_slot_full(r), NetT::template D<L - k>(), t);
+          }
           ++issued;
         });
       }
@@ -334,7 +399,7 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
         const int s = i % NS, j = i / NS;
         ok = mbar_wait(bar_out_ready(s), j & 1, abort_flag, kDevTimeoutEpi);
         if (!ok) break;
-        const int nx = i * NLD + L;
+        const int nx = i * NLD + NLD - 1;
         const uint32_t xb = slot_addr(nx % R);
         constexpr int C = chunk_elems(Cfg::D0);
         constexpr int P = pitch_bytes(Cfg::D0);
@@ -350,79 +415,152 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // Tiles i = p*NS + s of round p; per layer, every slot's step in turn.
     const bool issuer = (lane == 0);
+    // dgrad: dh_l[128 x d_l] = dz_{l+1} W_l^T: A = dz (K-major, K = d_{l+1}),
+    // B = W_l as stored ([d_l rows][d_{l+1}] = K-major W_l^T)
+    auto issue_dgrad = [&](auto lc, uint32_t acc, uint32_t zsrc) {
+      constexpr int l = decltype(lc)::value;
+      constexpr int DI = NetT::template D<l>();
+      constexpr int DO = NetT::template D<l + 1>();
+      constexpr uint32_t idesc_d = make_idesc_f16(kTileM, DI, 0, 0);
+      const uint64_t ad0 = kmajor_base_desc<DO>(zsrc);
+      const uint64_t bd0 = kmajor_base_desc<DO>(s_w + NetT::template w_off<l>());
+#pragma unroll
+      for (int k = 0; k < DO / 16; ++k)
+        umma_f16(acc, ad0 + (kmajor_koff<kTileM, DO>(k) >> 4), bd0 + (kmajor_koff<DI, DO>(k) >> 4), idesc_d,
+                 k > 0 ? 1u : 0u);
+    };
+    // wgrad over the 128 tile rows (K): dW_l += h_l^T dz (A = h_l, B = dz) or,
+    // transposed, dW_l^T += dz^T h_l (A = dz, B = h_l); both operands
+    // MN-major from shared memory; a 64-wide A is padded to M = 128 by
+    // pointing its second 64-column chunk (LBO) at the zero chunk.
+    auto issue_wgrad = [&](auto lc, int i, uint32_t a_h, uint32_t zsrc) {
+      constexpr int l = decltype(lc)::value;
+      constexpr bool TR = Cfg::wg_trans(l);
+      constexpr int MW = Cfg::wg_m(l);
+      constexpr int NW = Cfg::wg_n(l);
+      constexpr uint32_t idesc_w = make_idesc_f16(kTileM, NW, 1, 1);
+      const uint32_t a_base = TR ? zsrc : a_h;
+      const uint32_t b_base = TR ? a_h : zsrc;
+      constexpr int PA = pitch_bytes(MW);
+      const uint32_t lbo = (MW < 128) ? (s_zero - a_base) : kTileM * PA;
+      const uint64_t aw0 = make_sdesc(a_base, lbo, 8 * PA, umma_layout_code(PA));
+      const uint64_t bw0 = mnmajor_base_desc<kTileM, NW>(b_base);
+      const uint32_t dw = tmem_base + Cfg::dw_col(l);
+#pragma unroll
+      for (int k = 0; k < kTileM / 16; ++k)
+        umma_f16(dw, aw0 + (mnmajor_koff<MW>(k) >> 4), bw0 + (mnmajor_koff<NW>(k) >> 4), idesc_w,
+                 (i > 0 || k > 0) ? 1u : 0u);
+    };
     bool ok = __all_sync(0xffffffffu, mbar_wait(bar_w_full, 0, abort_flag, kDevTimeoutMma));
     tc_fence_after();
-    for (int p = 0; ok; ++p) {
-      if (tile_of(p * NS) >= num_tiles) break;
-      static_for<0, L>([&](auto lc) {
-        constexpr int l = L - 1 - decltype(lc)::value;  // L-1 .. 0
-        constexpr int DI = NetT::template D<l>();      // d_l
-        constexpr int DO = NetT::template D<l + 1>();  // d_{l+1}
-#pragma unroll
-        for (int s = 0; s < NS; ++s) {
-          const int i = p * NS + s;
-          if (!ok || tile_of(i) >= num_tiles) break;
-          const uint32_t acc = tmem_base + Cfg::ACC_COL + s * Cfg::ACC_W;
-          const int ng = i * NLD;            // g
-          const int na = i * NLD + (L - l);  // h_l (x for l == 0)
-          // dz_{l+1}: g (a ring slot) for the last layer, else the slot's G
-          uint32_t zsrc = s_g(s);
+    if constexpr (H32) {
+      // One tile at a time.  Layer step l: dgrad(l) reads dz_{l+1} (g, or the
+      // high half-slot of h_{l+1} where the epilogue of step l+1 put it), then
+      // the weight gradient of layer l+1, whose operands the epilogue of step
+      // l+1 has just written (fp16 h_{l+1} in its low half-slot) -- the last
+      // read of h_{l+1}'s low slot and of dz_{l+2}'s slot.  After dgrad(0):
+      // wgrad(0) from x and dz_1.
+      const uint32_t acc = tmem_base + Cfg::ACC_COL;
+      for (int i = 0; ok; ++i) {
+        if (tile_of(i) >= num_tiles) break;
+        const int base = i * NLD;
+        auto slot_of = [&](int k) { return (base + k) % R; };
+        auto full_par = [&](int k) { return static_cast<uint32_t>(((base + k) / R) & 1); };
+        static_for<0, L>([&](auto sc) {
+          constexpr int l = L - 1 - decltype(sc)::value;  // L-1 .. 0
+          if (!ok) return;
+          uint32_t zsrc;
           if constexpr (l == L - 1) {
-            ok = __all_sync(0xffffffffu, mbar_wait(bar_slot_full(ng % R), (ng / R) & 1, abort_flag,
+            ok = __all_sync(0xffffffffu, mbar_wait(bar_slot_full(slot_of(0)), full_par(0), abort_flag,
                                                    kDevTimeoutMma)) &&
-                 __all_sync(0xffffffffu,
-                            mbar_wait(bar_acc_free(s), (p & 1) ^ 1, abort_flag, kDevTimeoutMma));
-            zsrc = slot_addr(ng % R);
+                 __all_sync(0xffffffffu, mbar_wait(bar_acc_free(0), (i & 1) ^ 1, abort_flag, kDevTimeoutMma));
+            zsrc = slot_addr(slot_of(0));
           } else {
-            ok = __all_sync(0xffffffffu, mbar_wait(bar_dz_full(s), (p * (L - 1) + (L - 2 - l)) & 1,
+            ok = __all_sync(0xffffffffu, mbar_wait(bar_dz_full(0), (i * (L - 1) + (L - 2 - l)) & 1,
                                                    abort_flag, kDevTimeoutMma));
+            zsrc = slot_addr(slot_of(Cfg::h_load(l + 1) + 1));  // dz_{l+1}: high half-slot of h_{l+1}
           }
-          if (!ok) break;
-          ok = __all_sync(0xffffffffu,
-                          mbar_wait(bar_slot_full(na % R), (na / R) & 1, abort_flag, kDevTimeoutMma));
-          if (!ok) break;
+          if (!ok) return;
           tc_fence_after();
-          const uint32_t a_h = slot_addr(na % R);
           if (issuer) {
-            // dgrad: dh_l[128 x d_l] = dz W_l^T: A = dz (K-major, K = d_{l+1}),
-            // B = W_l as stored ([d_l rows][d_{l+1}] = K-major W_l^T)
-            constexpr uint32_t idesc_d = make_idesc_f16(kTileM, DI, 0, 0);
-            const uint64_t ad0 = kmajor_base_desc<DO>(zsrc);
-            const uint64_t bd0 = kmajor_base_desc<DO>(s_w + NetT::template w_off<l>());
-#pragma unroll
-            for (int k = 0; k < DO / 16; ++k)
-              umma_f16(acc, ad0 + (kmajor_koff<kTileM, DO>(k) >> 4),
-                       bd0 + (kmajor_koff<DI, DO>(k) >> 4), idesc_d, k > 0 ? 1u : 0u);
-            umma_commit(bar_acc_full(s));
-            // wgrad over the 128 tile rows (K): dW_l += h_l^T dz (A = h_l, B = dz) or,
-            // transposed, dW_l^T += dz^T h_l (A = dz, B = h_l); both operands
-            // MN-major from shared memory; a 64-wide A is padded to M = 128 by
-            // pointing its second 64-column chunk (LBO) at the zero chunk.
-            constexpr bool TR = Cfg::wg_trans(l);
-            constexpr int MW = Cfg::wg_m(l);
-            constexpr int NW = Cfg::wg_n(l);
-            constexpr uint32_t idesc_w = make_idesc_f16(kTileM, NW, 1, 1);
-            const uint32_t a_base = TR ? zsrc : a_h;
-            const uint32_t b_base = TR ? a_h : zsrc;
-            constexpr int PA = pitch_bytes(MW);
-            const uint32_t lbo = (MW < 128) ? (s_zero - a_base) : kTileM * PA;
-            const uint64_t aw0 = make_sdesc(a_base, lbo, 8 * PA, umma_layout_code(PA));
-            const uint64_t bw0 = mnmajor_base_desc<kTileM, NW>(b_base);
-            const uint32_t dw = tmem_base + Cfg::dw_col(l);
-#pragma unroll
-            for (int k = 0; k < kTileM / 16; ++k)
-              umma_f16(dw, aw0 + (mnmajor_koff<MW>(k) >> 4), bw0 + (mnmajor_koff<NW>(k) >> 4), idesc_w,
-                       (i > 0 || k > 0) ? 1u : 0u);
-            umma_commit(bar_wg_done(s));
-            umma_commit(bar_slot_empty(na % R));
-            if constexpr (l == L - 1) umma_commit(bar_slot_empty(ng % R));
+            issue_dgrad(std::integral_constant<int, l>{}, acc, zsrc);
+            umma_commit(bar_acc_full(0));
+            if constexpr (l < L - 1) {
+              // weight gradient of layer l+1: A = fp16 h_{l+1} (low half-slot),
+              // B = dz_{l+2} (g, or the high half-slot of h_{l+2})
+              constexpr int kb = (l + 1 == L - 1) ? 0 : Cfg::h_load(l + 2) + 1;
+              constexpr int ka = Cfg::h_load(l + 1);
+              issue_wgrad(std::integral_constant<int, l + 1>{}, i, slot_addr(slot_of(ka)), slot_addr(slot_of(kb)));
+              umma_commit(bar_slot_empty(slot_of(ka)));
+              umma_commit(bar_slot_empty(slot_of(kb)));
+            }
           }
           __syncwarp();
-        }
-      });
+          if constexpr (l == 0) {
+            ok = __all_sync(0xffffffffu, mbar_wait(bar_slot_full(slot_of(NLD - 1)), full_par(NLD - 1),
+                                                   abort_flag, kDevTimeoutMma));
+            if (!ok) return;
+            tc_fence_after();
+            if (issuer) {
+              constexpr int kz = Cfg::h_load(1) + 1;  // dz_1: high half-slot of h_1
+              issue_wgrad(std::integral_constant<int, 0>{}, i, slot_addr(slot_of(NLD - 1)), slot_addr(slot_of(kz)));
+              umma_commit(bar_wg_done(0));  // x's slot may take dx
+              umma_commit(bar_slot_empty(slot_of(kz)));
+              umma_commit(bar_slot_empty(slot_of(NLD - 1)));
+            }
+            __syncwarp();
+          }
+        });
+      }
+    } else {
+      // Tiles i = p*NS + s of round p; per layer, every slot's step in turn.
+      // Per layer the dgrad is issued first and committed, then the wgrad:
+      // the epilogue's sigmoid multiply of layer l overlaps the wgrad of
+      // layer l, and only its stores into G wait for the wgrad to have read G.
+      for (int p = 0; ok; ++p) {
+        if (tile_of(p * NS) >= num_tiles) break;
+        static_for<0, L>([&](auto lc) {
+          constexpr int l = L - 1 - decltype(lc)::value;  // L-1 .. 0
+#pragma unroll
+          for (int s = 0; s < NS; ++s) {
+            const int i = p * NS + s;
+            if (!ok || tile_of(i) >= num_tiles) break;
+            const uint32_t acc = tmem_base + Cfg::ACC_COL + s * Cfg::ACC_W;
+            const int ng = i * NLD;            // g
+            const int na = i * NLD + (L - l);  // h_l (x for l == 0)
+            // dz_{l+1}: g (a ring slot) for the last layer, else the slot's G
+            uint32_t zsrc = s_g(s);
+            if constexpr (l == L - 1) {
+              ok = __all_sync(0xffffffffu, mbar_wait(bar_slot_full(ng % R), (ng / R) & 1, abort_flag,
+                                                     kDevTimeoutMma)) &&
+                   __all_sync(0xffffffffu,
+                              mbar_wait(bar_acc_free(s), (p & 1) ^ 1, abort_flag, kDevTimeoutMma));
+              zsrc = slot_addr(ng % R);
+            } else {
+              ok = __all_sync(0xffffffffu, mbar_wait(bar_dz_full(s), (p * (L - 1) + (L - 2 - l)) & 1,
+                                                     abort_flag, kDevTimeoutMma));
+            }
+            if (!ok) break;
+            ok = __all_sync(0xffffffffu,
+                            mbar_wait(bar_slot_full(na % R), (na / R) & 1, abort_flag, kDevTimeoutMma));
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t a_h = slot_addr(na % R);
+            if (issuer) {
+              issue_dgrad(lc_rev<L>(lc), acc, zsrc);
+              umma_commit(bar_acc_full(s));
+              issue_wgrad(lc_rev<L>(lc), i, a_h, zsrc);
+              umma_commit(bar_wg_done(s));
+              umma_commit(bar_slot_empty(na % R));
+              if constexpr (l == L - 1) umma_commit(bar_slot_empty(ng % R));
+            }
+            __syncwarp();
+          }
+        });
+      }
     }
+    // Drain: all issued MMAs complete before TMEM is freed.
     if (issuer) umma_commit(bar_mma_done);
     __syncwarp();
     {
@@ -462,7 +600,54 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
         uint32_t r[CW];
         tmem_ld_cols<CW>(acc + c0, r);
         uint32_t o[CW / 2];
-        if constexpr (l > 0) {
+        if constexpr (l > 0 && H32) {
+          // dz_l = dh_l * (1 - e^{-h_l}) with h_l in fp32 from its two
+          // half-slots; then, in place, the fp16 h_l (weight-gradient operand)
+          // into the low half-slot and dz_l into the high one
+          const int nlo = i * NLD + Cfg::h_load(l);
+          const uint32_t lo = slot_addr(nlo % R), hi = slot_addr((nlo + 1) % R);
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_slot_full(nlo % R), (nlo / R) & 1, abort_flag,
+                                                 kDevTimeoutEpi)) &&
+               __all_sync(0xffffffffu, mbar_wait(bar_slot_full((nlo + 1) % R), ((nlo + 1) / R) & 1,
+                                                 abort_flag, kDevTimeoutEpi));
+          if (!ok) return;
+          uint32_t hp[CW / 2];
+#pragma unroll
+          for (int u = 0; u < CW / 4; ++u) {
+            const int c = c0 + 4 * u;
+            const uint4 hv = c < DI / 2 ? ld_tile_row4_f32(lo, row, c) : ld_tile_row4_f32(hi, row, c - DI / 2);
+            const float2 h01 = make_float2(__uint_as_float(hv.x), __uint_as_float(hv.y));
+            const float2 h23 = make_float2(__uint_as_float(hv.z), __uint_as_float(hv.w));
+            const float2 d01 =
+                dsoftplus_mul_x2(make_float2(__uint_as_float(r[4 * u]), __uint_as_float(r[4 * u + 1])), h01);
+            const float2 d23 =
+                dsoftplus_mul_x2(make_float2(__uint_as_float(r[4 * u + 2]), __uint_as_float(r[4 * u + 3])), h23);
+            o[2 * u] = pack_half2(d01.x, d01.y);
+            o[2 * u + 1] = pack_half2(d23.x, d23.y);
+            hp[2 * u] = pack_half2(h01.x, h01.y);
+            hp[2 * u + 1] = pack_half2(h23.x, h23.y);
+          }
+          // every warp's fp32 reads of both half-slots are done before any
+          // warp overwrites them (the column groups share rows)
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_rd_done);
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_rd_done, (j * (L - 1) + (L - 1 - l)) & 1, abort_flag,
+                                                 kDevTimeoutEpi));
+          if (!ok) return;
+#pragma unroll
+          for (int u = 0; u < CW / 8; ++u) {
+            st_tile_row8<DI>(lo, row, c0 + 8 * u, hp[4 * u], hp[4 * u + 1], hp[4 * u + 2], hp[4 * u + 3]);
+            st_tile_row8<DI>(hi, row, c0 + 8 * u, o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
+          }
+          fence_proxy_async_smem();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(bar_dz_full(s));
+            mbar_arrive(bar_slot_empty(nlo % R));        // this warp is done with both
+            mbar_arrive(bar_slot_empty((nlo + 1) % R));  // half-slots; the MMAs still read them
+          }
+        } else if constexpr (l > 0) {
           // dz_l = dh_l * softplus'(z_l) = dh_l * (1 - e^{-h_l}), h_l from its slot
           const int nh = i * NLD + (L - l);
           const uint32_t hb = slot_addr(nh % R);
@@ -474,11 +659,11 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
             const uint4 hv = ld_tile_row8<DI>(hb, row, c0 + 8 * u);
             const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int jj = 0; jj < 4; ++jj) {
               const float2 dz = dsoftplus_mul_x2(
-                  make_float2(__uint_as_float(r[8 * u + 2 * j]), __uint_as_float(r[8 * u + 2 * j + 1])),
-                  half2_to_float2(hw[j]));
-              o[4 * u + j] = pack_half2(dz.x, dz.y);
+                  make_float2(__uint_as_float(r[8 * u + 2 * jj]), __uint_as_float(r[8 * u + 2 * jj + 1])),
+                  half2_to_float2(hw[jj]));
+              o[4 * u + jj] = pack_half2(dz.x, dz.y);
             }
           }
           __syncwarp();
@@ -497,9 +682,12 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
           // dx = dh_0 -> fp16, staged in x's slot (free once the wgrad read x) -> TMA store
 #pragma unroll
           for (int u = 0; u < CW / 8; ++u) pack_cols<4, false>(r + 8 * u, o + 4 * u);
-          const int nx = i * NLD + L;
+          const int nx = i * NLD + NLD - 1;
           const uint32_t xb = slot_addr(nx % R);
-          ok = __all_sync(0xffffffffu, mbar_wait(bar_wg_done(s), step & 1, abort_flag, kDevTimeoutEpi));
+          // wg_done completes once per layer step (fp16 h) or once per tile,
+          // after wgrad(0) (fp32 h)
+          const int wg_phase = H32 ? j : step;
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_wg_done(s), wg_phase & 1, abort_flag, kDevTimeoutEpi));
           if (!ok) return;
           // accumulator read.  Released only after the wg_done wait: the next
           // tile's first step (which needs acc_free) commits wg_done again, and
@@ -534,18 +722,18 @@ __global__ void __launch_bounds__(BwdCfg<NetT>::THREADS, 1)
         const uint32_t dw = tmem_base + lane_off + Cfg::dw_col(l);
 #pragma unroll 1
         for (int c = 16 * (s * NG + grp); c < NW; c += 16 * NS * NG) {
-          uint32_t r[16];
-          tmem_ld_wait_x16(dw + c, r);  // every lane takes part in the warp-wide load
+          uint32_t rr[16];
+          tmem_ld_wait_x16(dw + c, rr);  // every lane takes part in the warp-wide load
           if (row < static_cast<uint32_t>(MW)) {
             if constexpr (!TR) {
               float4* dst = reinterpret_cast<float4*>(part + off + row * DO + c);
 #pragma unroll
               for (int v = 0; v < 4; ++v)
-                dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                                     __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+                dst[v] = make_float4(__uint_as_float(rr[4 * v]), __uint_as_float(rr[4 * v + 1]),
+                                     __uint_as_float(rr[4 * v + 2]), __uint_as_float(rr[4 * v + 3]));
             } else {
 #pragma unroll
-              for (int v = 0; v < 16; ++v) part[off + (c + v) * DO + row] = __uint_as_float(r[v]);
+              for (int v = 0; v < 16; ++v) part[off + (c + v) * DO + row] = __uint_as_float(rr[v]);
             }
           }
         }

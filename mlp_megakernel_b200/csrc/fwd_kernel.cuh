@@ -94,8 +94,9 @@ struct alignas(64) FwdMaps {
   CUtensorMap x;       // [M, d0] fp16, box {chunk(d0), 128}
   CUtensorMap out;     // [M, dL] fp16, box {chunk(dL), 128}
   CUtensorMap w[L];    // [d_l, d_{l+1}] fp16, box {chunk(d_{l+1}), d_l}
-  // training forward only: the saved hidden activations h_1..h_{L-1} ([M, d_l]
-  // fp16 each, the exact values fed to the next GEMM), box {chunk(d_l), 128}
+  // training forward only: the saved hidden activations h_1..h_{L-1}, [M, d_l]
+  // each: fp16 (the exact values fed to the next GEMM), box {chunk(d_l), 128};
+  // or fp32 (H32), box {32, 32}
   CUtensorMap hsave[L > 1 ? L - 1 : 1];
   int M;
   // The caller's widths when they are smaller than the kernel's network (a
@@ -115,7 +116,9 @@ __host__ __device__ __forceinline__ void static_for(F&& f) {
   }
 }
 
-template <class NetT, int NS, int EPW>
+// H32: the training forward saves the hidden activations in fp32 (the
+// reference's storage, README.md:30) instead of the fp16 operand copy.
+template <class NetT, int NS, int EPW, bool H32 = false>
 struct FwdCfg {
   static constexpr int L = NetT::L;
   static constexpr int D0 = NetT::template D<0>();
@@ -124,8 +127,11 @@ struct FwdCfg {
   static constexpr int X_BYTES = align_up(tile_bytes(kTileM, D0), 1024);
   static constexpr int H1 = NetT::template D<1>();
   // staging tile of a slot: the output, and in the training forward also every
-  // hidden activation (both written to HBM by TMA stores)
-  static constexpr int O_BYTES = align_up(tile_bytes(kTileM, DL > H1 ? DL : H1), 1024);
+  // hidden activation (both written to HBM by TMA stores); with fp32 saved
+  // activations at least two 16 KB piece buffers (4 warps x 32 x 32 fp32)
+  static constexpr int O_BYTES_BASE = align_up(tile_bytes(kTileM, DL > H1 ? DL : H1), 1024);
+  static constexpr int O_BYTES = H32 && O_BYTES_BASE < 2 * 16384 ? 2 * 16384 : O_BYTES_BASE;
+  static constexpr int NPB = O_BYTES / 16384;  // fp32 piece buffers per slot (H32)
   static constexpr int W_TOTAL = NetT::w_total();
   static constexpr int OFF_X = W_TOTAL;
   static constexpr int OFF_O = OFF_X + NS * X_BYTES;
@@ -137,8 +143,9 @@ struct FwdCfg {
   static constexpr int SPC = (HMAX / (EPW / 4)) / 32 >= 4 ? 2 : 1;
   static constexpr int MAXCH = ((HMAX / (EPW / 4) + 31) / 32 + SPC - 1) / SPC;  // chunks/layer
   // x_full, x_empty, out_ready, store_free per slot; acc_full per slot and
-  // accumulator buffer; MAXCH h-chunk barriers per slot; w_full; mma_done
-  static constexpr int NUM_BARS = 6 * NS + NS * MAXCH + 2;
+  // accumulator buffer; MAXCH h-chunk barriers per slot; w_full; mma_done;
+  // (H32) pieces_done per slot
+  static constexpr int NUM_BARS = 6 * NS + NS * MAXCH + 2 + NS;
   static constexpr int OFF_MISC = OFF_BAR + 8 * NUM_BARS;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
   static constexpr int SLOT_COLS = align_up(HMAX, 32);   // one accumulator buffer
@@ -156,6 +163,8 @@ struct FwdCfg {
   static_assert(NetT::hidden_uniform(), "all hidden layers must have the same width");
   static_assert(TMEM_COLS_RAW <= 512, "accumulators exceed TMEM");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
+  static_assert(!H32 || EPW == 4, "fp32 saved activations: one column group (a warp owns 32 rows)");
+  static_assert(!H32 || H % 32 == 0, "fp32 saved activations are stored in 32-column pieces");
 };
 
 // TMEM column (relative to the accumulator buffer) where the fp16 activation
@@ -195,10 +204,49 @@ __device__ __forceinline__ void publish_chunk(uint32_t bar) {
 // column is always loaded before the packed activation overwrites it: a
 // stripe's packed columns lie in its own range, and the async load of the
 // next stripe is issued before this stripe's store.
-template <int N, int NG, int SPC, int SAVE = 0>
+// Where SAVE = 3 (fp32 saved activations) stages and stores one warp's
+// stripes: NPB piece buffers of 4 KB per warp (32 rows x 32 fp32, 128-byte
+// rows, 128B swizzle: the layout of a TMA box {32, 32} of an fp32 tensor).
+// Stripe k of the warp goes to piece buffer k % NPB at
+// base + (k % NPB) * (4 * 4096) + quarter * 4096; the warp's lane 0 stores it
+// to rows [row0, row0 + 32) and columns [col, col + 32) of the saved tensor
+// (TMA clips rows past M; a box that starts at or past M or past the
+// caller's width hcols is skipped) and keeps at most NPB stores in flight.
+struct F32Save {
+  const CUtensorMap* map;
+  uint32_t base;  // the slot's staging region (1024-aligned)
+  int quarter;    // this warp's TMEM lane quarter (its 32 rows of the tile)
+  int row0;       // first tile row of this warp in the tensor
+  int M;
+  int hcols;
+  int* count;     // pieces this warp has written so far (across layers and tiles)
+};
+
+template <int NPB>
+__device__ __forceinline__ uint32_t f32_piece_begin(const F32Save& fs) {
+  const int k = *fs.count;
+  if (k >= NPB) {  // the store that used this buffer NPB pieces ago must have read it
+    if (lane_id() == 0) bulk_wait_group_read<NPB - 1>();
+    __syncwarp();
+  }
+  return fs.base + static_cast<uint32_t>((k % NPB) * 4 + fs.quarter) * 4096u;
+}
+
+template <int NPB>
+__device__ __forceinline__ void f32_piece_end(const F32Save& fs, uint32_t buf, int col) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane_id() == 0) {
+    if (fs.row0 < fs.M && col < fs.hcols) tma_store_2d(fs.map, buf, col, fs.row0);
+    bulk_commit_group();  // one group per piece (possibly empty): the ring arithmetic stays exact
+  }
+  ++*fs.count;
+}
+
+template <int N, int NG, int SPC, int SAVE = 0, int NPB = 2>
 __device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chunk_bar0,
                                            uint8_t* hrow = nullptr, uint32_t stage_base = 0,
-                                           uint32_t row = 0) {
+                                           uint32_t row = 0, const F32Save* fs = nullptr) {
   static_assert(N % (32 * NG) == 0, "hidden width must be a multiple of 32 * column groups");
   constexpr int SUBS = N / (32 * NG);
   static_assert(SUBS % SPC == 0, "stripes per chunk must divide the stripes per group");
@@ -210,7 +258,24 @@ __device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chun
     uint32_t b[32];
     if (j + 1 < SUBS) tmem_ld_async_x32(tbuf + col + 32 * NG, b);
     uint32_t w[16];
-    pack_cols<16, true>(a, w);
+    if constexpr (SAVE == 3) {
+      // fp32 h of this stripe into the warp's piece buffer (row = lane), then
+      // one TMA store of the warp's 32 x 32 box; the fp16 pack feeds TMEM
+      const uint32_t buf = f32_piece_begin<NPB>(*fs);
+      const uint32_t lane = lane_id();
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float2 z0 = softplus_x2(make_float2(__uint_as_float(a[4 * u]), __uint_as_float(a[4 * u + 1])));
+        const float2 z1 = softplus_x2(make_float2(__uint_as_float(a[4 * u + 2]), __uint_as_float(a[4 * u + 3])));
+        st_shared_v4(buf + swz_off<128>(lane, u), __float_as_uint(z0.x), __float_as_uint(z0.y),
+                     __float_as_uint(z1.x), __float_as_uint(z1.y));
+        w[2 * u] = pack_half2(z0.x, z0.y);
+        w[2 * u + 1] = pack_half2(z1.x, z1.y);
+      }
+      f32_piece_end<NPB>(*fs, buf, col);
+    } else {
+      pack_cols<16, true>(a, w);
+    }
     tmem_st_x16(tbuf + h_tmem_col(col), w);
     if constexpr (SAVE == 1) {
       if (hrow != nullptr) {  // this thread's row exists (row < M): save h for backward
@@ -263,10 +328,11 @@ __device__ __forceinline__ void out_job(uint32_t tbuf, uint32_t tile_base, uint3
   }
 }
 
-template <class NetT, int NS, int EPW, bool TRAIN = false>
-__global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
+template <class NetT, int NS, int EPW, bool TRAIN = false, bool H32 = false>
+__global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW, H32>::THREADS, 1)
     mlp_fwd_kernel(const __grid_constant__ FwdMaps<NetT::L> maps, int num_tiles) {
-  using Cfg = FwdCfg<NetT, NS, EPW>;
+  using Cfg = FwdCfg<NetT, NS, EPW, H32>;
+  static_assert(TRAIN || !H32, "fp32 saved activations belong to the training forward");
   constexpr int L = Cfg::L;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -294,6 +360,9 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
   auto bar_chunk = [&](int s, int c) { return s_bar + 8u * (6 * NS + s * Cfg::MAXCH + c); };
   const uint32_t bar_w_full = s_bar + 8u * (6 * NS + NS * Cfg::MAXCH);
   const uint32_t bar_mma_done = bar_w_full + 8u;
+  // (H32) every warp of slot s has seen its fp32 piece stores read: the
+  // output tile may overwrite the staging region
+  auto bar_pieces_done = [&](int s) { return bar_mma_done + 8u + 8u * s; };
   const uint32_t s_tmem_slot = sbase + Cfg::OFF_MISC;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + Cfg::OFF_MISC + 4);
 
@@ -309,6 +378,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
       mbar_init(bar_out_ready(s), EPW);
       mbar_init(bar_store_free(s), 1);
       for (int c = 0; c < Cfg::MAXCH; ++c) mbar_init(bar_chunk(s, c), EPW);
+      mbar_init(bar_pieces_done(s), EPW);
     }
     mbar_init(bar_w_full, 1);
     mbar_init(bar_mma_done, 1);
@@ -478,6 +548,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
     constexpr int H = Cfg::H;
     constexpr int NCOL_H = H / Cfg::NG;
     constexpr int NCOL_O = Cfg::DL / Cfg::NG;
+    int pieces = 0;  // (H32) fp32 pieces this warp has staged
     for (int i = 0; ok; ++i) {
       const int t = tile_of(i, s);
       if (t >= num_tiles) break;
@@ -490,10 +561,13 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
         tc_fence_after();
         // obuf may still be the source of this slot's previous TMA store: the
         // leader waits for that store to finish reading, then frees it.  Uses
-        // of obuf: one per tile (the output) or, in the training forward, one
-        // per layer (every h_l, then the output).
-        const int use = TRAIN ? i * L + l : i;
-        if ((TRAIN || l == 0) && use > 0) {
+        // of obuf by the leader's stores: one per tile (the output) or, in the
+        // fp16 training forward, one per layer (every h_l, then the output).
+        // The fp32 training forward stages h in per-warp pieces, each warp
+        // pacing its own stores (F32Save), so only the output counts.
+        constexpr bool kLayerUses = TRAIN && !H32;
+        const int use = kLayerUses ? i * L + l : i;
+        if ((kLayerUses || l == 0) && use > 0) {
           if (leader) {
             bulk_wait_group_read<0>();
             mbar_arrive(bar_store_free(s));
@@ -504,7 +578,12 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
           if (!ok) break;
         }
         const uint32_t t_buf = t_lane + ((i * L + l) & 1) * Cfg::SLOT_COLS;
-        if constexpr (TRAIN) {
+        if constexpr (H32) {
+          // h_l -> TMEM (next layer's A, fp16) and, in fp32, per-warp pieces
+          // -> TMA stores
+          const F32Save fs{&maps.hsave[l], obuf, q, t * kTileM + q * 32, maps.M, maps.h_cols[l], &pieces};
+          hidden_job<H, Cfg::NG, Cfg::SPC, 3, Cfg::NPB>(t_buf, grp, bar_chunk(s, 0), nullptr, 0, row, &fs);
+        } else if constexpr (TRAIN) {
           // h_l -> TMEM (next layer's A) and the staging tile -> TMA store
           hidden_job<H, Cfg::NG, Cfg::SPC, 2>(t_buf, grp, bar_chunk(s, 0), nullptr, obuf, row);
           fence_proxy_async_smem();
@@ -535,8 +614,18 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
                                                ((i * L + l) >> 1) & 1, abort_flag, kDevTimeoutEpi));
         if (!ok) break;
         tc_fence_after();
-        const int use = TRAIN ? i * L + l : i;
-        if constexpr (TRAIN) {  // obuf held h_{L-1}: wait until its store has read it
+        constexpr bool kLayerUses = TRAIN && !H32;
+        const int use = kLayerUses ? i * L + l : i;
+        if constexpr (H32) {
+          // the output tile overlaps every warp's piece buffers: each warp
+          // waits for its own piece stores to have read them, then all warps
+          // of the slot meet
+          if (lane == 0) bulk_wait_group_read<0>();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_pieces_done(s));
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_pieces_done(s), i & 1, abort_flag, kDevTimeoutEpi));
+          if (!ok) break;
+        } else if constexpr (TRAIN) {  // obuf held h_{L-1}: wait until its store has read it
           if (leader) {
             bulk_wait_group_read<0>();
             mbar_arrive(bar_store_free(s));
@@ -564,7 +653,9 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW>::THREADS, 1)
         }
       }
     }
-    if (leader) bulk_wait_group<0>();
+    // every store this warp issued (the leader's tiles, and with fp32 saved
+    // activations every warp's pieces) completes before the CTA exits
+    if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
   }
 

@@ -113,22 +113,23 @@ EncodeFn get_encode() {
   return fn;
 }
 
-// 2-D fp16 tensor [outer][inner] (inner contiguous), box {box_inner, box_outer},
-// swizzle chosen from the box's row pitch (box_inner * 2 bytes).
+// 2-D tensor [outer][inner] (inner contiguous) of fp16 (elem_bytes 2) or fp32
+// (elem_bytes 4), box {box_inner, box_outer}, swizzle chosen from the box's
+// row pitch (box_inner * elem_bytes).
 int make_map_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer,
-                uint32_t box_inner, uint32_t box_outer) {
+                uint32_t box_inner, uint32_t box_outer, uint32_t elem_bytes = 2) {
   EncodeFn enc = get_encode();
   if (!enc) return driver_status("cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)", -1);
-  const uint32_t pitch = box_inner * 2;
+  const uint32_t pitch = box_inner * elem_bytes;
   CUtensorMapSwizzle swz = pitch == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
                            : pitch == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                          : CU_TENSOR_MAP_SWIZZLE_32B;
   cuuint64_t gdim[2] = {inner, outer};
-  cuuint64_t gstride[1] = {inner * 2};
+  cuuint64_t gstride[1] = {inner * elem_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estride[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), gdim, gstride,
-                   box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+  CUresult r = enc(map, elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                   const_cast<void*>(ptr), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return driver_status("cuTensorMapEncodeTiled", static_cast<int>(r));
 }
@@ -157,8 +158,9 @@ bool set_smem_once(Kern kern, int bytes, int dev) {
 // network's widths is the plain case).
 template <class NetT, int NS, int EPW>
 int launch_fwd(const int* rd, const void* x, const void* const* W, void* out, int64_t M,
-               void* const* hsave, cudaStream_t st) {
+               void* const* hsave, bool h32, cudaStream_t st) {
   using Cfg = FwdCfg<NetT, NS, EPW>;
+  using Cfg32 = FwdCfg<NetT, NS, EPW, true>;
   constexpr int L = NetT::L;
   DevInfo di;
   int dev = 0;
@@ -187,13 +189,20 @@ int launch_fwd(const int* rd, const void* x, const void* const* W, void* out, in
   if (hsave) {
     for (int l = 0; l + 1 < L; ++l) {
       if (!hsave[l]) return MLPK_ERR_NULL;
-      if ((rc = make_map_2d(&maps.hsave[l], hsave[l], rd[l + 1], M, mlpk::chunk_elems(Cfg::H), mlpk::kTileM)))
-        return rc;
+      // fp32: every warp stores its 32 rows x 32 columns per piece
+      rc = h32 ? make_map_2d(&maps.hsave[l], hsave[l], rd[l + 1], M, 32, 32, 4)
+               : make_map_2d(&maps.hsave[l], hsave[l], rd[l + 1], M, mlpk::chunk_elems(Cfg::H), mlpk::kTileM);
+      if (rc) return rc;
     }
   }
 
   const int num_tiles = static_cast<int>((M + mlpk::kTileM - 1) / mlpk::kTileM);
   const int grid = num_tiles < di.sm_count ? num_tiles : di.sm_count;
+  if (hsave && h32) {
+    auto kern = mlpk::mlp_fwd_kernel<NetT, NS, EPW, true, true>;
+    if (!set_smem_once(kern, Cfg32::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
+    return launch_kernel(kern, grid, Cfg32::THREADS, Cfg32::SMEM_BYTES, st, maps, num_tiles);
+  }
   if (hsave) {
     auto kern = mlpk::mlp_fwd_kernel<NetT, NS, EPW, true>;
     if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
@@ -212,7 +221,7 @@ int64_t bwd_grid(int64_t M, int sm_count) {
 }
 
 template <class NetT>
-size_t bwd_workspace(int64_t M, int sm_count) {
+size_t bwd_workspace(int64_t M, int sm_count) {  // the same for fp16 and fp32 saved activations
   return static_cast<size_t>(bwd_grid<NetT>(M, sm_count)) * mlpk::BwdCfg<NetT>::PARTIAL_FLOATS *
          sizeof(float);
 }
@@ -243,9 +252,10 @@ mlpk::DwLayout dw_layout(const int* rd) {
 }
 
 template <class NetT>
-int launch_bwd(const int* rd, const void* x, const void* const* W, const void* const* h, const void* g,
-               void* dx, float* ws, size_t ws_bytes, float* dw, int64_t M, cudaStream_t st) {
+int launch_bwd(const int* rd, const void* x, const void* const* W, const void* const* h, bool h32,
+               const void* g, void* dx, float* ws, size_t ws_bytes, float* dw, int64_t M, cudaStream_t st) {
   using Cfg = mlpk::BwdCfg<NetT>;
+  using Cfg32 = mlpk::BwdCfg<NetT, true>;
   constexpr int L = NetT::L;
   DevInfo di;
   int dev = 0;
@@ -268,16 +278,23 @@ int launch_bwd(const int* rd, const void* x, const void* const* W, const void* c
       constexpr int N = NetT::template D<l + 1>();
       if (wrc == MLPK_OK) wrc = make_map_2d(&maps.w[l], W[l], rd[l + 1], rd[l], mlpk::chunk_elems(N), K);
       if constexpr (l >= 1)
-        if (wrc == MLPK_OK)
-          wrc = make_map_2d(&maps.h[l - 1], h[l - 1], rd[l], M, mlpk::chunk_elems(K), mlpk::kTileM);
+        if (wrc == MLPK_OK)  // fp32: 32-column chunks of the two halves
+          wrc = h32 ? make_map_2d(&maps.h[l - 1], h[l - 1], rd[l], M, 32, mlpk::kTileM, 4)
+                    : make_map_2d(&maps.h[l - 1], h[l - 1], rd[l], M, mlpk::chunk_elems(K), mlpk::kTileM);
     });
     if (wrc) return wrc;
     maps.partials = ws;
     maps.dx_cols = rd[0];
-    auto kern = mlpk::mlp_bwd_kernel<NetT>;
-    if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
     const int num_tiles = static_cast<int>((M + mlpk::kTileM - 1) / mlpk::kTileM);
-    if ((rc = launch_kernel(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, st, maps, num_tiles))) return rc;
+    if (h32) {
+      auto kern = mlpk::mlp_bwd_kernel<NetT, true>;
+      if (!set_smem_once(kern, Cfg32::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
+      if ((rc = launch_kernel(kern, grid, Cfg32::THREADS, Cfg32::SMEM_BYTES, st, maps, num_tiles))) return rc;
+    } else {
+      auto kern = mlpk::mlp_bwd_kernel<NetT>;
+      if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
+      if ((rc = launch_kernel(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, st, maps, num_tiles))) return rc;
+    }
   }
   return launch_kernel(mlpk::mlp_reduce_kernel, (nfloats + mlpk::kReduceElems - 1) / mlpk::kReduceElems,
                        mlpk::kReduceElems * mlpk::kReduceSlices, 0, st,
@@ -290,7 +307,8 @@ constexpr int kStreamEpw = 8;
 
 template <class NetT>
 int launch_stream_fwd(const int* rd, const void* x, const void* const* W, void* out, int64_t M,
-                      void* const* hsave, cudaStream_t st) {
+                      void* const* hsave, bool h32, cudaStream_t st) {
+  if (hsave && h32) return MLPK_ERR_UNSUPPORTED;  // streamed networks save fp16 activations
   using Cfg = mlpk::StreamCfg<NetT, kStreamEpw>;
   constexpr int L = NetT::L;
   DevInfo di;
@@ -357,9 +375,10 @@ size_t stream_bwd_workspace(int64_t M, int sm_count) {
 }
 
 template <class NetT>
-int launch_stream_bwd(const int* rd, const void* x, const void* const* W, const void* const* h,
+int launch_stream_bwd(const int* rd, const void* x, const void* const* W, const void* const* h, bool h32,
                       const void* g, void* dx, float* ws, size_t ws_bytes, float* dw, int64_t M,
                       cudaStream_t st) {
+  if (h32) return MLPK_ERR_UNSUPPORTED;  // streamed networks save fp16 activations
   using Lay = StreamBwdLayout<NetT>;
   using Chain = mlpk::NetReverse<NetT>;
   using Cfg = mlpk::StreamCfg<Chain, kStreamEpw>;
@@ -440,16 +459,17 @@ int launch_stream_bwd(const int* rd, const void* x, const void* const* W, const 
 }
 
 // ------------------------------------------------------------------ dispatch
-using Fwd = int (*)(const int*, const void*, const void* const*, void*, int64_t, void* const*,
+using Fwd = int (*)(const int*, const void*, const void* const*, void*, int64_t, void* const*, bool,
                    cudaStream_t);
-using Bwd = int (*)(const int*, const void*, const void* const*, const void* const*, const void*, void*,
-                    float*, size_t, float*, int64_t, cudaStream_t);
+using Bwd = int (*)(const int*, const void*, const void* const*, const void* const*, bool, const void*,
+                    void*, float*, size_t, float*, int64_t, cudaStream_t);
 using BwdWs = size_t (*)(int64_t, int);
 
 struct ShapeOps {
   Fwd fwd = nullptr;
   Bwd bwd = nullptr;
   BwdWs bwd_ws = nullptr;
+  bool h32 = false;  // fp32 saved activations served (the fused kernels)
 };
 
 // The compiled networks, smallest first.  A caller's network is served by the
@@ -491,10 +511,12 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.fwd = &launch_fwd<N64, 3, 4>;
     o.bwd = &launch_bwd<N64>;
     o.bwd_ws = &bwd_workspace<N64>;
+    o.h32 = true;
   } else if (covers<N3>(s)) {
     o.fwd = &launch_fwd<N3, 2, 4>;
     o.bwd = &launch_bwd<N3>;
     o.bwd_ws = &bwd_workspace<N3>;
+    o.h32 = true;
   } else if (covers<N256>(s)) {
     o.fwd = &launch_stream_fwd<N256>;
     o.bwd = &launch_stream_bwd<N256>;
@@ -503,10 +525,12 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.fwd = &launch_fwd<N5, 3, 4>;
     o.bwd = &launch_bwd<N5>;
     o.bwd_ws = &bwd_workspace<N5>;
+    o.h32 = true;
   } else if (covers<N5w64>(s)) {
     o.fwd = &launch_fwd<N5w64, 3, 4>;
     o.bwd = &launch_bwd<N5w64>;
     o.bwd_ws = &bwd_workspace<N5w64>;
+    o.h32 = true;
   } else if (covers<N5w128>(s)) {
     o.fwd = &launch_stream_fwd<N5w128>;
     o.bwd = &launch_stream_bwd<N5w128>;
@@ -519,10 +543,12 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.fwd = &launch_fwd<N2w64, 3, 4>;
     o.bwd = &launch_bwd<N2w64>;
     o.bwd_ws = &bwd_workspace<N2w64>;
+    o.h32 = true;
   } else if (covers<N2w128>(s)) {
     o.fwd = &launch_fwd<N2w128, 2, 4>;
     o.bwd = &launch_bwd<N2w128>;
     o.bwd_ws = &bwd_workspace<N2w128>;
+    o.h32 = true;
   } else if (covers<N2w256>(s)) {
     o.fwd = &launch_stream_fwd<N2w256>;
     o.bwd = &launch_stream_bwd<N2w256>;
@@ -531,6 +557,7 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.fwd = &launch_fwd<N4w64, 3, 4>;
     o.bwd = &launch_bwd<N4w64>;
     o.bwd_ws = &bwd_workspace<N4w64>;
+    o.h32 = true;
   } else if (covers<N4w128>(s)) {
     o.fwd = &launch_stream_fwd<N4w128>;
     o.bwd = &launch_stream_bwd<N4w128>;
@@ -576,11 +603,14 @@ int mlpk_shape_supported(const mlpk_shape* shape) {
   return pick_ops(shape, false).fwd != nullptr ? 1 : 0;
 }
 
-int mlpk_train_supported(const mlpk_shape* shape) {
+int mlpk_train_supported_ex(const mlpk_shape* shape, int h_dtype) {
   if (check_shape(shape) != MLPK_OK) return 0;
+  if (h_dtype != MLPK_H_F16 && h_dtype != MLPK_H_F32) return 0;
   const ShapeOps o = pick_ops(shape, true);
-  return (o.fwd != nullptr && o.bwd != nullptr) ? 1 : 0;
+  return (o.fwd != nullptr && o.bwd != nullptr && (h_dtype == MLPK_H_F16 || o.h32)) ? 1 : 0;
 }
+
+int mlpk_train_supported(const mlpk_shape* shape) { return mlpk_train_supported_ex(shape, MLPK_H_F16); }
 
 namespace {
 int check_fwd_args(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
@@ -605,21 +635,27 @@ int mlpk_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* cons
   if (rc) return rc;
   Fwd f = pick_ops(shape, false).fwd;
   if (!f) return MLPK_ERR_UNSUPPORTED;
-  return f(shape->dims, x, W, out, M, nullptr, static_cast<cudaStream_t>(stream));
+  return f(shape->dims, x, W, out, M, nullptr, false, static_cast<cudaStream_t>(stream));
 }
 
-int mlpk_train_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
-                   void* out, void* const* h_saved, mlpk_stream_t stream) {
+int mlpk_train_fwd_ex(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
+                      void* out, void* const* h_saved, int h_dtype, mlpk_stream_t stream) {
   int rc = check_fwd_args(shape, M, x, W, out);
   if (rc) return rc;
+  if (h_dtype != MLPK_H_F16 && h_dtype != MLPK_H_F32) return MLPK_ERR_SHAPE;
   if (!h_saved) return MLPK_ERR_NULL;
   for (int l = 0; l + 1 < shape->num_layers; ++l) {
     if (M > 0 && !h_saved[l]) return MLPK_ERR_NULL;
     if (!aligned16(h_saved[l])) return MLPK_ERR_ALIGN;
   }
   const ShapeOps o = pick_ops(shape, true);
-  if (!o.fwd || !o.bwd) return MLPK_ERR_UNSUPPORTED;
-  return o.fwd(shape->dims, x, W, out, M, h_saved, static_cast<cudaStream_t>(stream));
+  if (!o.fwd || !o.bwd || (h_dtype == MLPK_H_F32 && !o.h32)) return MLPK_ERR_UNSUPPORTED;
+  return o.fwd(shape->dims, x, W, out, M, h_saved, h_dtype == MLPK_H_F32, static_cast<cudaStream_t>(stream));
+}
+
+int mlpk_train_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
+                   void* out, void* const* h_saved, mlpk_stream_t stream) {
+  return mlpk_train_fwd_ex(shape, M, x, W, out, h_saved, MLPK_H_F16, stream);
 }
 
 int64_t mlpk_bwd_workspace_size(const mlpk_shape* shape, int64_t M) {
@@ -631,11 +667,12 @@ int64_t mlpk_bwd_workspace_size(const mlpk_shape* shape, int64_t M) {
   return static_cast<int64_t>(o.bwd_ws(M, di.sm_count));
 }
 
-int mlpk_bwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
-             const void* const* h_saved, const void* grad_out, void* dx, void* workspace,
-             int64_t workspace_bytes, float* dW, mlpk_stream_t stream) {
+int mlpk_bwd_ex(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
+                const void* const* h_saved, int h_dtype, const void* grad_out, void* dx, void* workspace,
+                int64_t workspace_bytes, float* dW, mlpk_stream_t stream) {
   int rc = check_fwd_args(shape, M, x, W, grad_out);
   if (rc) return rc;
+  if (h_dtype != MLPK_H_F16 && h_dtype != MLPK_H_F32) return MLPK_ERR_SHAPE;
   if (!dW || (M > 0 && (!dx || !h_saved || !workspace))) return MLPK_ERR_NULL;
   if (!aligned16(dx) || !aligned16(dW) || !aligned16(workspace)) return MLPK_ERR_ALIGN;
   for (int l = 0; M > 0 && l + 1 < shape->num_layers; ++l) {
@@ -644,9 +681,15 @@ int mlpk_bwd(const mlpk_shape* shape, int64_t M, const void* x, const void* cons
   }
   if (workspace_bytes < 0) return MLPK_ERR_SHAPE;
   const ShapeOps o = pick_ops(shape, true);
-  if (!o.bwd) return MLPK_ERR_UNSUPPORTED;
-  return o.bwd(shape->dims, x, W, h_saved, grad_out, dx, static_cast<float*>(workspace),
+  if (!o.bwd || (h_dtype == MLPK_H_F32 && !o.h32)) return MLPK_ERR_UNSUPPORTED;
+  return o.bwd(shape->dims, x, W, h_saved, h_dtype == MLPK_H_F32, grad_out, dx, static_cast<float*>(workspace),
                static_cast<size_t>(workspace_bytes), dW, M, static_cast<cudaStream_t>(stream));
+}
+
+int mlpk_bwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,
+             const void* const* h_saved, const void* grad_out, void* dx, void* workspace,
+             int64_t workspace_bytes, float* dW, mlpk_stream_t stream) {
+  return mlpk_bwd_ex(shape, M, x, W, h_saved, MLPK_H_F16, grad_out, dx, workspace, workspace_bytes, dW, stream);
 }
 
 namespace {
@@ -871,7 +914,7 @@ int mlpk_fwd_host(const mlpk_shape* shape, int64_t M, const void* x_host, const 
     // forward of chunk k: its input has arrived and its output buffer is free
     if ((rc = cuda_status(cudaStreamWaitEvent(st, p->in_ready[b], 0)))) return rc;
     if (k >= kPipeBufs && (rc = cuda_status(cudaStreamWaitEvent(st, p->out_done[b], 0)))) return rc;
-    if ((rc = f(shape->dims, xbuf(b), W, obuf(b), rows_of(k), nullptr, st))) return rc;
+    if ((rc = f(shape->dims, xbuf(b), W, obuf(b), rows_of(k), nullptr, false, st))) return rc;
     if ((rc = cuda_status(cudaEventRecord(p->comp_done[b], st)))) return rc;
     // copy out chunk k
     if ((rc = cuda_status(cudaStreamWaitEvent(p->d2h, p->comp_done[b], 0))) ||

@@ -18,7 +18,14 @@ from mlp_fused.md:52-172 and mlp_fused.md:461-486, and is restated here:
   layer in one launch per direction.
 
 ``num_layers`` selects the depth (3 or 5 in the reference; README.md:9); all
-hidden layers have width H.  Data-parallel training: pass a
+hidden layers have width H.  ``activation_dtype`` is the precision of the
+hidden activations saved for the backward: ``torch.float32`` as the
+reference stores them (README.md:30; the backward computes softplus' from the
+fp32 value and rounds it to fp16 only as its weight-gradient operand) or
+``torch.float16`` (the fp16 operand copy: half the traffic).  The default,
+None, is fp32 where the network's kernels offer it (every network of the
+fused backward) and fp16 on the streamed-weight networks (256 wide; 128 wide
+at 4 and 5 layers), which save fp16 only.  Data-parallel training: pass a
 ``torch.distributed`` process group and the fp32 weight gradients are summed
 over the ranks on the current stream between the backward kernel and the
 weight-norm backward (so every rank applies the same update): on one node by
@@ -48,17 +55,34 @@ def _stream(dev):
     return torch.cuda.current_stream(dev).cuda_stream
 
 
-def _train_forward(x: torch.Tensor, ws, dims):
-    """Launch mlpk_train_fwd: returns (out, [h_1..h_{L-1}])."""
+_H_CODE = {torch.float16: _lib.H_F16, torch.float32: _lib.H_F32}
+
+
+def _resolve_activation_dtype(dims, activation_dtype):
+    """The saved-activation dtype of a network: the requested one (raising if
+    its kernels do not offer it), or fp32 where offered and else fp16."""
+    if activation_dtype is None:
+        return torch.float32 if _lib.train_supported(dims, _lib.H_F32) else torch.float16
+    if activation_dtype not in _H_CODE:
+        raise TypeError(f"activation_dtype must be torch.float32 or torch.float16, got {activation_dtype}")
+    if not _lib.train_supported(dims, _H_CODE[activation_dtype]):
+        raise ValueError(f"no training kernels for dims {tuple(dims)} with {activation_dtype} saved activations")
+    return activation_dtype
+
+
+def _train_forward(x: torch.Tensor, ws, dims, h_dtype=torch.float16):
+    """Launch mlpk_train_fwd_ex: returns (out, [h_1..h_{L-1}]), the saved
+    activations in ``h_dtype`` (fp16 or fp32)."""
     M = x.shape[0]
     out = torch.empty((M, dims[-1]), device=x.device, dtype=torch.float16)
-    hs = [torch.empty((M, d), device=x.device, dtype=torch.float16) for d in dims[1:-1]]
+    hs = [torch.empty((M, d), device=x.device, dtype=h_dtype) for d in dims[1:-1]]
     if M > 0:
         lib = _lib.lib()
-        rc = lib.mlpk_train_fwd(ctypes.byref(_lib.shape_struct(dims)), M, x.data_ptr(),
-                                _lib.ptr_array([w.data_ptr() for w in ws]), out.data_ptr(),
-                                _lib.ptr_array([h.data_ptr() for h in hs]), _stream(x.device))
-        _lib.check("mlpk_train_fwd", rc)
+        rc = lib.mlpk_train_fwd_ex(ctypes.byref(_lib.shape_struct(dims)), M, x.data_ptr(),
+                                   _lib.ptr_array([w.data_ptr() for w in ws]), out.data_ptr(),
+                                   _lib.ptr_array([h.data_ptr() for h in hs]), _H_CODE[h_dtype],
+                                   _stream(x.device))
+        _lib.check("mlpk_train_fwd_ex", rc)
     return out, hs
 
 
@@ -80,8 +104,9 @@ class _GradSum:
 
 
 def _backward(x, ws, hs, grad_out, dims, grad_sum: _GradSum = None):
-    """Launch mlpk_bwd: returns (dx fp16, dW_flat fp32), dW summed over the
-    ranks when ``grad_sum`` is given."""
+    """Launch mlpk_bwd_ex (the saved activations' dtype read from ``hs``):
+    returns (dx fp16, dW_flat fp32), dW summed over the ranks when
+    ``grad_sum`` is given."""
     M = x.shape[0]
     lib = _lib.lib()
     shape = _lib.shape_struct(dims)
@@ -95,11 +120,12 @@ def _backward(x, ws, hs, grad_out, dims, grad_sum: _GradSum = None):
     if wsb < 0:
         raise _lib.MlpkError("mlpk_bwd_workspace_size", 2)
     work = torch.empty(max(int(wsb), 16), device=x.device, dtype=torch.uint8)
-    rc = lib.mlpk_bwd(ctypes.byref(shape), M, x.data_ptr(),
-                      _lib.ptr_array([w.data_ptr() for w in ws]),
-                      _lib.ptr_array([h.data_ptr() for h in hs]), g.data_ptr(), dx.data_ptr(),
-                      work.data_ptr(), int(work.numel()), local.data_ptr(), _stream(x.device))
-    _lib.check("mlpk_bwd", rc)
+    h_code = _H_CODE[hs[0].dtype] if hs else _lib.H_F16
+    rc = lib.mlpk_bwd_ex(ctypes.byref(shape), M, x.data_ptr(),
+                         _lib.ptr_array([w.data_ptr() for w in ws]),
+                         _lib.ptr_array([h.data_ptr() for h in hs]), h_code, g.data_ptr(), dx.data_ptr(),
+                         work.data_ptr(), int(work.numel()), local.data_ptr(), _stream(x.device))
+    _lib.check("mlpk_bwd_ex", rc)
     if red is not None:
         red.reduce(local, dw)
     return dx, dw
@@ -124,10 +150,10 @@ def _check_input(x: torch.Tensor, d0: int) -> torch.Tensor:
 class _FusedMLPFn(torch.autograd.Function):
     @staticmethod
     @torch.amp.custom_fwd(device_type="cuda", cast_inputs=torch.float16)
-    def forward(ctx, x, dims, grad_sum, *weights):
+    def forward(ctx, x, dims, grad_sum, h_dtype, *weights):
         x = _check_input(x, dims[0])
         ws = [_aligned(w.to(torch.float16)) for w in weights]
-        out, hs = _train_forward(x, ws, dims)
+        out, hs = _train_forward(x, ws, dims, h_dtype)
         ctx.dims = dims
         ctx.grad_sum = grad_sum
         ctx.w_dtypes = [w.dtype for w in weights]
@@ -143,13 +169,13 @@ class _FusedMLPFn(torch.autograd.Function):
         x, ws, hs = saved[0], list(saved[1:1 + L]), list(saved[1 + L:])
         dx, dw = _backward(x, ws, hs, grad_out, dims, ctx.grad_sum)
         dws = [d.to(t) for d, t in zip(_split_flat(dw, dims), ctx.w_dtypes)]
-        return (dx if ctx.needs_input_grad[0] else None, None, None, *dws)
+        return (dx if ctx.needs_input_grad[0] else None, None, None, None, *dws)
 
 
 class _FusedMLPWNFn(torch.autograd.Function):
     @staticmethod
     @torch.amp.custom_fwd(device_type="cuda", cast_inputs=torch.float16)
-    def forward(ctx, x, dims, grad_sum, v_all, g_all):
+    def forward(ctx, x, dims, grad_sum, h_dtype, v_all, g_all):
         x = _check_input(x, dims[0])
         lib = _lib.lib()
         shape = _lib.shape_struct(dims)
@@ -162,7 +188,7 @@ class _FusedMLPWNFn(torch.autograd.Function):
                              _lib.ptr_array([w.data_ptr() for w in ws]), inv.data_ptr(),
                              _stream(x.device))
         _lib.check("mlpk_wn_fwd", rc)
-        out, hs = _train_forward(x, ws, dims)
+        out, hs = _train_forward(x, ws, dims, h_dtype)
         ctx.dims = dims
         ctx.grad_sum = grad_sum
         ctx.dtypes = (v_all.dtype, g_all.dtype)
@@ -185,7 +211,7 @@ class _FusedMLPWNFn(torch.autograd.Function):
                              g32.data_ptr(), inv.data_ptr(), dv.data_ptr(), dg.data_ptr(),
                              _stream(x.device))
         _lib.check("mlpk_wn_bwd", rc)
-        return (dx if ctx.needs_input_grad[0] else None, None, None,
+        return (dx if ctx.needs_input_grad[0] else None, None, None, None,
                 dv.to(ctx.dtypes[0]), dg.to(ctx.dtypes[1]))
 
 
@@ -193,13 +219,13 @@ class _FusedMLPWNFn(torch.autograd.Function):
 # trace into them.  Marked opaque, they run eagerly at a graph break and their
 # backward is recorded by autograd as usual.
 @torch.compiler.disable
-def _apply_fused(x, dims, grad_sum, *weights):
-    return _FusedMLPFn.apply(x, dims, grad_sum, *weights)
+def _apply_fused(x, dims, grad_sum, h_dtype, *weights):
+    return _FusedMLPFn.apply(x, dims, grad_sum, h_dtype, *weights)
 
 
 @torch.compiler.disable
-def _apply_fused_wn(x, dims, grad_sum, v_all, g_all):
-    return _FusedMLPWNFn.apply(x, dims, grad_sum, v_all, g_all)
+def _apply_fused_wn(x, dims, grad_sum, h_dtype, v_all, g_all):
+    return _FusedMLPWNFn.apply(x, dims, grad_sum, h_dtype, v_all, g_all)
 
 
 class FusedMLPSoftplus(nn.Module):
@@ -210,9 +236,10 @@ class FusedMLPSoftplus(nn.Module):
     """
 
     def __init__(self, D: int = 128, H: int = 128, out_features: int = 128, num_layers: int = 3,
-                 process_group=None, grad_reduce: str = "auto"):
+                 process_group=None, grad_reduce: str = "auto", activation_dtype=None):
         super().__init__()
         self.dims = _dims(D, H, out_features, num_layers)
+        self.activation_dtype = _resolve_activation_dtype(self.dims, activation_dtype)
         self.process_group = process_group
         self._grad_sum = _GradSum(process_group, grad_reduce) if process_group is not None else None
         for i, (a, b) in enumerate(zip(self.dims[:-1], self.dims[1:])):
@@ -225,7 +252,7 @@ class FusedMLPSoftplus(nn.Module):
         return [getattr(self, f"w{i + 1}") for i in range(len(self.dims) - 1)]
 
     def forward(self, x):
-        return _apply_fused(x, self.dims, self._grad_sum, *self.weights)
+        return _apply_fused(x, self.dims, self._grad_sum, self.activation_dtype, *self.weights)
 
 
 class FusedMLPSoftplusWN(nn.Module):
@@ -238,9 +265,10 @@ class FusedMLPSoftplusWN(nn.Module):
     """
 
     def __init__(self, D: int = 128, H: int = 128, out_features: int = 128, num_layers: int = 3,
-                 process_group=None, grad_reduce: str = "auto"):
+                 process_group=None, grad_reduce: str = "auto", activation_dtype=None):
         super().__init__()
         self.dims = _dims(D, H, out_features, num_layers)
+        self.activation_dtype = _resolve_activation_dtype(self.dims, activation_dtype)
         self.process_group = process_group
         self._grad_sum = _GradSum(process_group, grad_reduce) if process_group is not None else None
         vs, gs = [], []
@@ -273,4 +301,4 @@ class FusedMLPSoftplusWN(nn.Module):
             self.g(l).copy_(w.float().norm(dim=0))
 
     def forward(self, x):
-        return _apply_fused_wn(x, self.dims, self._grad_sum, self.v_all, self.g_all)
+        return _apply_fused_wn(x, self.dims, self._grad_sum, self.activation_dtype, self.v_all, self.g_all)

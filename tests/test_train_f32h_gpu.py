@@ -1,0 +1,149 @@
+"""GPU parity of the training path with fp32 saved activations.
+
+The reference stores the hidden activations in fp32 for the backward's
+softplus derivative (README.md:30); mlpk_train_fwd_ex / mlpk_bwd_ex with
+MLPK_H_F32 do the same: the training forward writes h in fp32, the backward
+computes 1 - e^{-h} from it and rounds h to fp16 only as its weight-gradient
+operand.  Checked here against the oracle (oracle/mlp_oracle.py: its saved h
+are the fp32 values and its backward uses them in the sigmoid, i.e. exactly
+this storage), and against the fp16-storage path.
+
+Tolerances (north star): outputs max|d| <= 1e-2 * max|ref|; gradients
+relative L2 <= 1e-2; the saved fp32 h within 1e-4 (relative to max|h|) of
+the float64 softplus (the kernel's softplus is accurate to ~1e-5 relative).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from mlp_megakernel_b200 import FusedMLPSoftplusWN, _lib, fused_mlp_fwd
+from mlp_megakernel_b200.modules import _backward, _train_forward
+from mlp_megakernel_b200.synthetic import make_grad, make_weights, make_x
+
+pytestmark = pytest.mark.gpu
+
+GRAD_TOL = 1e-2
+OUT_TOL = 1e-2
+H_TOL = 1e-4
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
+
+
+def rel_max(a, b):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return np.abs(a - b).max() / max(np.abs(b).max(), 1e-30)
+
+
+@pytest.fixture(autouse=True)
+def _status(built_lib):
+    _lib.device_status(clear=True)
+    yield
+    assert _lib.device_status() == 0, "a kernel recorded a device-side timeout"
+
+
+def _split(dw, dims):
+    out, off = [], 0
+    for a, b in zip(dims[:-1], dims[1:]):
+        out.append(dw[off:off + a * b].reshape(a, b))
+        off += a * b
+    return out
+
+
+def _inputs(dims, M, seed, w_scale=1.0, x_dist="normal"):
+    x = make_x(M, dims[0], x_dist, seed)
+    ws = [(w.float() * w_scale).half() for w in make_weights(dims, seed=seed + 100)]
+    g = make_grad(M, dims[-1], seed=seed + 200)
+    return x, ws, g
+
+
+def _check(dims, x, ws, g, h_dtype=torch.float32):
+    xg, wg, gg = x.cuda(), [w.cuda() for w in ws], g.cuda()
+    out, hs = _train_forward(xg, wg, dims, h_dtype)
+    dx, dw = _backward(xg, wg, hs, gg, dims)
+    torch.cuda.synchronize()
+    assert all(h.dtype == h_dtype for h in hs)
+    # the training forward's output equals the inference forward, bitwise
+    assert torch.equal(out, fused_mlp_fwd(xg, *wg))
+    ref_out, ref_hs = oracle.mlp_forward_train(x.numpy(), [w.numpy() for w in ws])
+    assert rel_max(out.cpu().numpy(), ref_out) <= OUT_TOL
+    if h_dtype == torch.float32:
+        for h, rh in zip(hs, ref_hs):
+            assert rel_max(h.cpu().numpy(), rh) <= H_TOL
+    ref_dx, ref_dws = oracle.mlp_backward(x.numpy(), [w.numpy() for w in ws], ref_hs, g.numpy())
+    errs = [rel_l2(dx.cpu().numpy(), ref_dx)]
+    errs += [rel_l2(d, rd) for d, rd in zip(_split(dw.cpu().numpy(), dims), ref_dws)]
+    assert max(errs) <= GRAD_TOL, errs
+    return dx, dw, max(errs)
+
+
+NETS = {
+    "3L128": (128, 128, 128, 128),
+    "5L": (32, 64, 64, 64, 64, 16),
+    "3L64": (64, 64, 64, 64),
+    "2L128": (128, 128, 128),
+    "4L64": (64, 64, 64, 64, 64),
+    "5L64": (64, 64, 64, 64, 64, 64),
+    "covered_96": (48, 96, 96, 24),  # served by the 128-wide kernels through TMA zero fill
+}
+
+
+@pytest.mark.parametrize("M", [1, 129, 5000])
+@pytest.mark.parametrize("net", sorted(NETS))
+def test_f32h_training_matches_oracle(net, M):
+    dims = NETS[net]
+    x, ws, g = _inputs(dims, M, seed=31, x_dist="uniform" if net == "5L" else "normal")
+    _check(dims, x, ws, g)
+
+
+def test_f32h_split_k_regime_and_determinism():
+    """BASELINE config 3 at M = 262,144: gradients against the oracle, and
+    bitwise-identical dW and dx over repeated backward launches."""
+    dims = NETS["3L128"]
+    x, ws, g = _inputs(dims, 262144, seed=0)
+    dx, dw, _ = _check(dims, x, ws, g)
+    xg, wg, gg = x.cuda(), [w.cuda() for w in ws], g.cuda()
+    _, hs = _train_forward(xg, wg, dims, torch.float32)
+    dx2, dw2 = _backward(xg, wg, hs, gg, dims)
+    torch.cuda.synchronize()
+    assert torch.equal(dw, dw2) and torch.equal(dx, dx2)
+
+
+def test_f16_vs_f32_storage_error_with_large_preactivations():
+    """Weights x8 push many pre-activations far below zero, where h is tiny
+    and fp16 storage loses its relative precision (subnormals): both
+    storages stay within tolerance of the oracle, and fp32 storage is at least
+    as close as fp16 storage."""
+    dims = NETS["3L128"]
+    x, ws, g = _inputs(dims, 20000, seed=41, w_scale=8.0)
+    _, _, err32 = _check(dims, x, ws, g, torch.float32)
+    _, _, err16 = _check(dims, x, ws, g, torch.float16)
+    assert err32 <= err16 * 1.05 + 1e-6, (err32, err16)
+
+
+def test_f32h_refused_on_streamed_networks():
+    """The streamed-weight networks save fp16 only: fp32 storage is refused
+    with MLPK_ERR_UNSUPPORTED, and the module default picks fp16 for them."""
+    dims = (256, 256, 256, 256)
+    assert not _lib.train_supported(dims, _lib.H_F32) and _lib.train_supported(dims, _lib.H_F16)
+    M = 256
+    x = make_x(M, 256, "normal", 3).cuda()
+    ws = [w.cuda() for w in make_weights(dims)]
+    out = torch.empty((M, 256), dtype=torch.float16, device="cuda")
+    hs = [torch.empty((M, 256), dtype=torch.float32, device="cuda") for _ in range(2)]
+    rc = _lib.lib().mlpk_train_fwd_ex(ctypes.byref(_lib.shape_struct(dims)), M, x.data_ptr(),
+                                      _lib.ptr_array([w.data_ptr() for w in ws]), out.data_ptr(),
+                                      _lib.ptr_array([h.data_ptr() for h in hs]), _lib.H_F32,
+                                      torch.cuda.current_stream().cuda_stream)
+    assert _lib.STATUS_NAMES[rc] == "MLPK_ERR_UNSUPPORTED"
+    assert FusedMLPSoftplusWN(D=256, H=256, out_features=256).activation_dtype == torch.float16
+    assert FusedMLPSoftplusWN(D=128, H=128, out_features=128).activation_dtype == torch.float32
+    with pytest.raises(ValueError):
+        FusedMLPSoftplusWN(D=256, H=256, out_features=256, activation_dtype=torch.float32)
