@@ -181,7 +181,13 @@ int mlpk_fwd_host(const mlpk_shape* shape, int64_t M, const void* x_host, const 
                   mlpk_stream_t stream);
 
 /* Reads (and optionally clears) the device-side status word of the current
- * device: bit flags set by bounded waits that expired.  Synchronises. */
+ * device: bit flags set by bounded waits that expired (each wait gives up
+ * after 1 s, records its flag and lets the kernel return).  Synchronises. */
+#define MLPK_DEVST_TIMEOUT_FULL 1   /* a consumer waited too long for data */
+#define MLPK_DEVST_TIMEOUT_EMPTY 2  /* a producer waited too long for a free buffer */
+#define MLPK_DEVST_TIMEOUT_MMA 4    /* the tensor-core issuer waited too long */
+#define MLPK_DEVST_TIMEOUT_EPI 8    /* an epilogue warp waited too long */
+#define MLPK_DEVST_TIMEOUT_FLAG 16  /* a cross-CTA or cross-GPU flag wait expired */
 int mlpk_device_status(int clear, int* status_out);
 
 /* ---- fp32 <-> fp16 casts (round to nearest even), for the fp32-input
@@ -204,8 +210,8 @@ int mlpk_cast_f16_f32(const void* src_f16, float* dst, int64_t n, mlpk_stream_t 
  * once per step, in the same order; the step count lives in device memory, so
  * the call can be captured in a CUDA graph.  When it returns (on the stream),
  * every rank has finished reading this rank's buffer.  If a peer does not
- * arrive within the bounded wait (1 s), the kernel sets bit 16 (cross-GPU flag
- * timeout) of the device status word (mlpk_device_status).  At most 8 ranks;
+ * arrive within the bounded wait (1 s), the kernel sets MLPK_DEVST_TIMEOUT_FLAG
+ * (16) in the device status word (mlpk_device_status).  At most 8 ranks;
  * mlpk_peer_alloc and mlpk_peer_open allocate / map device memory (set-up
  * calls, not per step). */
 #define MLPK_PEER_HANDLE_BYTES 64

@@ -28,14 +28,8 @@ import ctypes
 import torch
 import torch.nn as nn
 
-from . import _lib
-
-
-def _aligned(t: torch.Tensor) -> torch.Tensor:
-    t = t.contiguous()
-    if t.data_ptr() % 16 != 0:
-        t = t.clone()
-    return t
+from . import _lib, ops  # noqa: F401  (ops registers torch.ops.mlpk.*)
+from .ops import _aligned
 
 
 def _check_operands(x: torch.Tensor, weights) -> list:
@@ -61,7 +55,6 @@ def _check_operands(x: torch.Tensor, weights) -> list:
     return dims
 
 
-@torch.compiler.disable  # launches through ctypes: opaque to torch.compile (runs at a graph break)
 def fused_mlp_fwd(x: torch.Tensor, *weights: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
     """``softplus(...softplus(x @ W_0)...) @ W_{L-1}`` in one kernel launch.
 
@@ -70,46 +63,19 @@ def fused_mlp_fwd(x: torch.Tensor, *weights: torch.Tensor, out: torch.Tensor = N
     (kernel.py:110, kernel.py:117).  Like the reference (kernel.py:136) the
     result is a new tensor unless ``out`` (contiguous, ``[M, out_features]``,
     x's dtype and device) is given, which lets a serving loop reuse one buffer.
+    Runs as the custom operator ``torch.ops.mlpk.fwd`` (``fwd_out`` with
+    ``out``), so torch.compile traces it as one operator.
     """
     dims = _check_operands(x, weights)
-    x = _aligned(x)
-    ws = [_aligned(w) for w in weights]
     M = x.shape[0]
     if out is None:
-        out = torch.empty((M, dims[-1]), device=x.device, dtype=x.dtype)
-    elif (out.shape != (M, dims[-1]) or out.dtype != x.dtype or out.device != x.device
-          or not out.is_contiguous() or out.data_ptr() % 16 != 0):
+        return torch.ops.mlpk.fwd(x, list(weights))
+    if (out.shape != (M, dims[-1]) or out.dtype != x.dtype or out.device != x.device
+            or not out.is_contiguous()):
         raise ValueError("out must be a contiguous, 16-byte aligned "
                          f"[{M}, {dims[-1]}] {x.dtype} tensor on {x.device}")
-    if M == 0:
-        return out
-    lib = _lib.lib()
-    shape = _lib.shape_struct(dims)
-    with torch.cuda.device(x.device):
-        stream = torch.cuda.current_stream(x.device).cuda_stream
-        if x.dtype == torch.float32:
-            if not lib.mlpk_shape_supported(ctypes.byref(shape)):
-                _lib.check("mlpk_fwd", 2)
-            x16 = _cast(lib, x, torch.float16, stream)
-            ws = [_cast(lib, w, torch.float16, stream) for w in ws]
-            out16 = torch.empty((M, dims[-1]), device=x.device, dtype=torch.float16)
-            wptr = _lib.ptr_array([w.data_ptr() for w in ws])
-            _lib.check("mlpk_fwd", lib.mlpk_fwd(ctypes.byref(shape), M, x16.data_ptr(), wptr, out16.data_ptr(),
-                                                stream))
-            _lib.check("mlpk_cast_f16_f32", lib.mlpk_cast_f16_f32(out16.data_ptr(), out.data_ptr(),
-                                                                  out.numel(), stream))
-            return out
-        wptr = _lib.ptr_array([w.data_ptr() for w in ws])
-        rc = lib.mlpk_fwd(ctypes.byref(shape), M, x.data_ptr(), wptr, out.data_ptr(), stream)
-    _lib.check("mlpk_fwd", rc)
+    torch.ops.mlpk.fwd_out(x, list(weights), out)
     return out
-
-
-def _cast(lib, t: torch.Tensor, dtype, stream) -> torch.Tensor:
-    """fp32 -> fp16 copy of a contiguous tensor with the library's cast kernel."""
-    dst = torch.empty(t.shape, device=t.device, dtype=dtype)
-    _lib.check("mlpk_cast_f32_f16", lib.mlpk_cast_f32_f16(t.data_ptr(), dst.data_ptr(), t.numel(), stream))
-    return dst
 
 
 @torch.compiler.disable

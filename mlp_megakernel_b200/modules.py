@@ -34,15 +34,13 @@ this library's NVLink peer-memory kernel, otherwise by NCCL (``grad_reduce``
 """
 from __future__ import annotations
 
-import ctypes
 import math
 
 import torch
 import torch.nn as nn
 
-from . import _lib
+from . import _lib, ops
 from .dp import make_grad_reducer
-from .functional import _aligned
 
 
 def _dims(D: int, H: int, out_features: int, num_layers: int):
@@ -71,19 +69,10 @@ def _resolve_activation_dtype(dims, activation_dtype):
 
 
 def _train_forward(x: torch.Tensor, ws, dims, h_dtype=torch.float16):
-    """Launch mlpk_train_fwd_ex: returns (out, [h_1..h_{L-1}]), the saved
-    activations in ``h_dtype`` (fp16 or fp32)."""
-    M = x.shape[0]
-    out = torch.empty((M, dims[-1]), device=x.device, dtype=torch.float16)
-    hs = [torch.empty((M, d), device=x.device, dtype=h_dtype) for d in dims[1:-1]]
-    if M > 0:
-        lib = _lib.lib()
-        rc = lib.mlpk_train_fwd_ex(ctypes.byref(_lib.shape_struct(dims)), M, x.data_ptr(),
-                                   _lib.ptr_array([w.data_ptr() for w in ws]), out.data_ptr(),
-                                   _lib.ptr_array([h.data_ptr() for h in hs]), _H_CODE[h_dtype],
-                                   _stream(x.device))
-        _lib.check("mlpk_train_fwd_ex", rc)
-    return out, hs
+    """The training forward (torch.ops.mlpk.train_fwd): returns
+    (out, [h_1..h_{L-1}]), the saved activations in ``h_dtype``."""
+    res = torch.ops.mlpk.train_fwd(x, list(ws), h_dtype == torch.float32)
+    return res[0], list(res[1:])
 
 
 class _GradSum:
@@ -104,30 +93,21 @@ class _GradSum:
 
 
 def _backward(x, ws, hs, grad_out, dims, grad_sum: _GradSum = None):
-    """Launch mlpk_bwd_ex (the saved activations' dtype read from ``hs``):
-    returns (dx fp16, dW_flat fp32), dW summed over the ranks when
-    ``grad_sum`` is given."""
-    M = x.shape[0]
-    lib = _lib.lib()
-    shape = _lib.shape_struct(dims)
-    g = _aligned(grad_out.to(torch.float16))
-    dx = torch.empty_like(x)
+    """The fused backward: returns (dx fp16, dW_flat fp32).  Without a
+    gradient sum it is the operator torch.ops.mlpk.bwd; with one, the backward
+    writes this rank's dW where the reducer wants it and the reducer sums it
+    over the ranks."""
+    g = grad_out.to(torch.float16)
+    if grad_sum is None:
+        dx, dw = torch.ops.mlpk.bwd(x, list(ws), list(hs), g)
+        return dx, dw
+    dx = torch.empty(x.shape, device=x.device, dtype=torch.float16)
     nflat = sum(a * b for a, b in zip(dims[:-1], dims[1:]))
     dw = torch.empty(nflat, device=x.device, dtype=torch.float32)
-    red = grad_sum.reducer(nflat) if grad_sum is not None else None
-    local = red.local_buffer(dw) if red is not None else dw
-    wsb = lib.mlpk_bwd_workspace_size(ctypes.byref(shape), M)
-    if wsb < 0:
-        raise _lib.MlpkError("mlpk_bwd_workspace_size", 2)
-    work = torch.empty(max(int(wsb), 16), device=x.device, dtype=torch.uint8)
-    h_code = _H_CODE[hs[0].dtype] if hs else _lib.H_F16
-    rc = lib.mlpk_bwd_ex(ctypes.byref(shape), M, x.data_ptr(),
-                         _lib.ptr_array([w.data_ptr() for w in ws]),
-                         _lib.ptr_array([h.data_ptr() for h in hs]), h_code, g.data_ptr(), dx.data_ptr(),
-                         work.data_ptr(), int(work.numel()), local.data_ptr(), _stream(x.device))
-    _lib.check("mlpk_bwd_ex", rc)
-    if red is not None:
-        red.reduce(local, dw)
+    red = grad_sum.reducer(nflat)
+    local = red.local_buffer(dw)
+    ops.backward_into(x, ws, hs, g, dx, local)
+    red.reduce(local, dw)
     return dx, dw
 
 
@@ -144,7 +124,7 @@ def _check_input(x: torch.Tensor, d0: int) -> torch.Tensor:
         raise RuntimeError("fused MLP runs on CUDA (sm_100) only; got a CPU tensor")
     if x.dim() != 2 or x.shape[1] != d0:
         raise ValueError(f"x must be [M, {d0}]")
-    return _aligned(x.to(torch.float16))
+    return x.to(torch.float16).contiguous()
 
 
 class _FusedMLPFn(torch.autograd.Function):
@@ -152,7 +132,7 @@ class _FusedMLPFn(torch.autograd.Function):
     @torch.amp.custom_fwd(device_type="cuda", cast_inputs=torch.float16)
     def forward(ctx, x, dims, grad_sum, h_dtype, *weights):
         x = _check_input(x, dims[0])
-        ws = [_aligned(w.to(torch.float16)) for w in weights]
+        ws = [w.to(torch.float16).contiguous() for w in weights]
         out, hs = _train_forward(x, ws, dims, h_dtype)
         ctx.dims = dims
         ctx.grad_sum = grad_sum
@@ -177,17 +157,10 @@ class _FusedMLPWNFn(torch.autograd.Function):
     @torch.amp.custom_fwd(device_type="cuda", cast_inputs=torch.float16)
     def forward(ctx, x, dims, grad_sum, h_dtype, v_all, g_all):
         x = _check_input(x, dims[0])
-        lib = _lib.lib()
-        shape = _lib.shape_struct(dims)
-        v32 = _aligned(v_all.detach().to(torch.float32))
-        g32 = _aligned(g_all.detach().to(torch.float32))
-        ws = [torch.empty((a, b), device=x.device, dtype=torch.float16)
-              for a, b in zip(dims[:-1], dims[1:])]
-        inv = torch.empty_like(g32)
-        rc = lib.mlpk_wn_fwd(ctypes.byref(shape), v32.data_ptr(), g32.data_ptr(),
-                             _lib.ptr_array([w.data_ptr() for w in ws]), inv.data_ptr(),
-                             _stream(x.device))
-        _lib.check("mlpk_wn_fwd", rc)
+        v32 = v_all.detach().to(torch.float32).contiguous()
+        g32 = g_all.detach().to(torch.float32).contiguous()
+        res = torch.ops.mlpk.wn_fwd(v32, g32, list(dims))
+        ws, inv = list(res[:-1]), res[-1]
         out, hs = _train_forward(x, ws, dims, h_dtype)
         ctx.dims = dims
         ctx.grad_sum = grad_sum
@@ -204,28 +177,36 @@ class _FusedMLPWNFn(torch.autograd.Function):
         x, v32, g32, inv = saved[:4]
         ws, hs = list(saved[4:4 + L]), list(saved[4 + L:])
         dx, dw = _backward(x, ws, hs, grad_out, dims, ctx.grad_sum)
-        dv = torch.empty_like(v32)
-        dg = torch.empty_like(g32)
-        lib = _lib.lib()
-        rc = lib.mlpk_wn_bwd(ctypes.byref(_lib.shape_struct(dims)), dw.data_ptr(), v32.data_ptr(),
-                             g32.data_ptr(), inv.data_ptr(), dv.data_ptr(), dg.data_ptr(),
-                             _stream(x.device))
-        _lib.check("mlpk_wn_bwd", rc)
+        dv, dg = torch.ops.mlpk.wn_bwd(dw, v32, g32, inv, list(dims))
         return (dx if ctx.needs_input_grad[0] else None, None, None, None,
                 dv.to(ctx.dtypes[0]), dg.to(ctx.dtypes[1]))
 
 
-# The autograd Functions launch kernels through ctypes: torch.compile must not
-# trace into them.  Marked opaque, they run eagerly at a graph break and their
-# backward is recorded by autograd as usual.
+# The autograd Functions call the library through torch.ops.mlpk.* custom
+# operators, so torch.compile traces them (fullgraph).  With a data-parallel
+# gradient sum the backward also runs the reducer, a Python object over
+# peer-memory buffers or NCCL: that case stays opaque to torch.compile and
+# runs eagerly at a graph break.
 @torch.compiler.disable
-def _apply_fused(x, dims, grad_sum, h_dtype, *weights):
+def _apply_fused_dp(x, dims, grad_sum, h_dtype, *weights):
     return _FusedMLPFn.apply(x, dims, grad_sum, h_dtype, *weights)
 
 
 @torch.compiler.disable
-def _apply_fused_wn(x, dims, grad_sum, h_dtype, v_all, g_all):
+def _apply_fused_wn_dp(x, dims, grad_sum, h_dtype, v_all, g_all):
     return _FusedMLPWNFn.apply(x, dims, grad_sum, h_dtype, v_all, g_all)
+
+
+def _apply_fused(x, dims, grad_sum, h_dtype, *weights):
+    if grad_sum is not None:
+        return _apply_fused_dp(x, dims, grad_sum, h_dtype, *weights)
+    return _FusedMLPFn.apply(x, dims, None, h_dtype, *weights)
+
+
+def _apply_fused_wn(x, dims, grad_sum, h_dtype, v_all, g_all):
+    if grad_sum is not None:
+        return _apply_fused_wn_dp(x, dims, grad_sum, h_dtype, v_all, g_all)
+    return _FusedMLPWNFn.apply(x, dims, None, h_dtype, v_all, g_all)
 
 
 class FusedMLPSoftplus(nn.Module):

@@ -405,23 +405,46 @@ def test_training_step_in_cuda_graph():
     assert torch.equal(gv, model.v_all.grad) and torch.equal(gg, model.g_all.grad)
 
 
-def test_module_under_torch_compile():
-    """torch.compile of a model holding the fused module (the custom
-    autograd.Function calls the C ABI, which dynamo runs eagerly): same
+@pytest.mark.parametrize("wn", [False, True])
+def test_module_under_torch_compile(wn):
+    """torch.compile(fullgraph=True) of the fused modules: the autograd
+    Function calls the library through torch.ops.mlpk.* custom operators,
+    so dynamo traces forward and backward without a graph break; same
     outputs and gradients as eager."""
     torch.manual_seed(13)
-    model = FusedMLPSoftplus(D=128, H=128, out_features=128).cuda().half()
+    if wn:
+        model = FusedMLPSoftplusWN(D=128, H=128, out_features=128).cuda()
+        params = [model.v_all, model.g_all]
+    else:
+        model = FusedMLPSoftplus(D=128, H=128, out_features=128).cuda().half()
+        params = list(model.weights)
     x, _, g = make_inputs("3L128", 4000, with_grad=True)
     x, g = x.cuda(), g.cuda()
     out_e = model(x)
     out_e.backward(g)
-    grads_e = [w.grad.clone() for w in model.weights]
-    for w in model.weights:
-        w.grad = None
-    compiled = torch.compile(model)
+    grads_e = [p.grad.clone() for p in params]
+    for p in params:
+        p.grad = None
+    torch._dynamo.reset()
+    compiled = torch.compile(model, fullgraph=True)
     out_c = compiled(x)
     out_c.backward(g)
     torch.cuda.synchronize()
     assert torch.equal(out_c, out_e)
-    for w, ge in zip(model.weights, grads_e):
-        assert torch.equal(w.grad, ge)
+    for p, ge in zip(params, grads_e):
+        assert torch.equal(p.grad, ge)
+
+
+def test_functional_forward_under_torch_compile():
+    """fused_mlp_fwd inside a compiled function (fullgraph): one mlpk::fwd
+    operator between ordinary torch ops."""
+    x, ws = make_inputs("3L128", 3000)
+    xg, wg = x.cuda(), [w.cuda() for w in ws]
+
+    def f(a):
+        return fused_mlp_fwd(a * 2, *wg).float().sum(dim=1)
+
+    torch._dynamo.reset()
+    ref = f(xg)
+    got = torch.compile(f, fullgraph=True)(xg)
+    assert torch.equal(ref, got)
