@@ -54,15 +54,17 @@ const char* mlpk_status_string(int status);
 
 /* 1 if a kernel serves this shape, else 0.  Compiled networks: 2, 3 and 4
  * layers at 64, 128 and 256 wide; 5 layers at 32-64-64-64-64-16 and 64, 128
- * and 256 wide (the networks whose weights do not fit in shared memory --
- * 256 wide, and 128 wide at 4 and 5 layers -- run the streamed-weight
+ * and 256 wide; 6 and 7 layers at 64, 128 and 256 wide; 8 layers at 128 and
+ * 256 wide (the networks whose weights or weight gradients do not fit on the
+ * SM -- 256 wide, and 128 wide from 4 layers on -- run the streamed-weight
  * kernels).  A network of the
  * same depth whose every width is a multiple of 8 and at most the compiled
  * width is served by the smallest such kernel (its missing rows / columns are
  * zero-filled on load and clipped on store; results are those of the
  * caller's network).  Hidden widths need not be equal.  The reference's
  * kernel takes the widths its tiles divide (kernel.py:25-53); all of them
- * up to 256 wide are served, at 3 and 5 layers (and 2 and 4). */
+ * up to 256 wide are served, at 3 and 5 layers and every depth from 2 to
+ * MLPK_MAX_LAYERS. */
 int mlpk_shape_supported(const mlpk_shape* shape);
 
 /* Inference forward: out[M, dL] = MLP(x[M, d0]).

@@ -506,6 +506,18 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
   using N4w64 = Net<64, 64, 64, 64, 64>;
   using N4w128 = Net<128, 128, 128, 128, 128>;
   using N4w256 = Net<256, 256, 256, 256, 256>;
+  // deeper uniform networks, up to MLPK_MAX_LAYERS: 64 wide on the fused
+  // kernels while the backward's weight gradients fit in TMEM (6 and 7
+  // layers; an 8-layer 64-wide network runs on the 128-wide kernels), 128 and
+  // 256 wide on the streamed-weight kernels
+  using N6w64 = Net<64, 64, 64, 64, 64, 64, 64>;
+  using N7w64 = Net<64, 64, 64, 64, 64, 64, 64, 64>;
+  using N6w128 = Net<128, 128, 128, 128, 128, 128, 128>;
+  using N7w128 = Net<128, 128, 128, 128, 128, 128, 128, 128>;
+  using N8w128 = Net<128, 128, 128, 128, 128, 128, 128, 128, 128>;
+  using N6w256 = Net<256, 256, 256, 256, 256, 256, 256>;
+  using N7w256 = Net<256, 256, 256, 256, 256, 256, 256, 256>;
+  using N8w256 = Net<256, 256, 256, 256, 256, 256, 256, 256, 256>;
   ShapeOps o;
   if (covers<N64>(s)) {
     o.fwd = &launch_fwd<N64, 3, 4>;
@@ -566,6 +578,40 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.fwd = &launch_stream_fwd<N4w256>;
     o.bwd = &launch_stream_bwd<N4w256>;
     o.bwd_ws = &stream_bwd_workspace<N4w256>;
+  } else if (covers<N6w64>(s)) {  // five hidden layers
+    o.fwd = &launch_fwd<N6w64, 3, 4>;
+    o.bwd = &launch_bwd<N6w64>;
+    o.bwd_ws = &bwd_workspace<N6w64>;
+    o.h32 = true;
+  } else if (covers<N6w128>(s)) {
+    o.fwd = &launch_stream_fwd<N6w128>;
+    o.bwd = &launch_stream_bwd<N6w128>;
+    o.bwd_ws = &stream_bwd_workspace<N6w128>;
+  } else if (covers<N6w256>(s)) {
+    o.fwd = &launch_stream_fwd<N6w256>;
+    o.bwd = &launch_stream_bwd<N6w256>;
+    o.bwd_ws = &stream_bwd_workspace<N6w256>;
+  } else if (covers<N7w64>(s)) {  // six hidden layers
+    o.fwd = &launch_fwd<N7w64, 3, 4>;
+    o.bwd = &launch_bwd<N7w64>;
+    o.bwd_ws = &bwd_workspace<N7w64>;
+    o.h32 = true;
+  } else if (covers<N7w128>(s)) {
+    o.fwd = &launch_stream_fwd<N7w128>;
+    o.bwd = &launch_stream_bwd<N7w128>;
+    o.bwd_ws = &stream_bwd_workspace<N7w128>;
+  } else if (covers<N7w256>(s)) {
+    o.fwd = &launch_stream_fwd<N7w256>;
+    o.bwd = &launch_stream_bwd<N7w256>;
+    o.bwd_ws = &stream_bwd_workspace<N7w256>;
+  } else if (covers<N8w128>(s)) {  // seven hidden layers (64 wide included)
+    o.fwd = &launch_stream_fwd<N8w128>;
+    o.bwd = &launch_stream_bwd<N8w128>;
+    o.bwd_ws = &stream_bwd_workspace<N8w128>;
+  } else if (covers<N8w256>(s)) {
+    o.fwd = &launch_stream_fwd<N8w256>;
+    o.bwd = &launch_stream_bwd<N8w256>;
+    o.bwd_ws = &stream_bwd_workspace<N8w256>;
   }
   return o;
 }

@@ -63,12 +63,32 @@ def test_status_strings(built_lib):
     ((256, 256, 256), True),
     ((64, 64, 64, 64, 64), True),
     ((200, 128, 64, 256, 8), True),
-    ((64, 64, 64, 64, 64, 64, 64), False),  # 6 layers: no kernel of that depth
+    # 6 to 8 layers (MLPK_MAX_LAYERS): uniform 64 (6, 7 layers), 128 and 256
+    # wide compiled; 64-wide 8-layer networks run on the 128-wide kernels
+    ((64, 64, 64, 64, 64, 64, 64), True),
+    ((32, 64, 16, 64, 48, 64, 8), True),
+    ((64,) * 8, True),
+    ((64,) * 9, True),
+    ((128,) * 7, True),
+    ((96, 128, 128, 64, 128, 128, 128, 128, 24), True),
+    ((256,) * 9, True),
+    ((200, 256, 8, 256, 64, 256, 256), True),
+    ((264,) * 7, False),
     ((128, 128), False),
 ])
 def test_shape_supported(built_lib, dims, ok):
     assert _lib.shape_supported(dims) == ok
     assert _lib.train_supported(dims) == ok
+
+
+def test_depth_beyond_max_layers_rejected(built_lib):
+    """9 layers is more than MLPK_MAX_LAYERS: the C ABI reports no kernel and
+    the Python binding refuses to build the shape."""
+    s = _lib.MlpkShape()
+    s.num_layers = 9
+    assert built_lib.mlpk_shape_supported(ctypes.byref(s)) == 0
+    with pytest.raises(ValueError):
+        _lib.shape_struct((64,) * 10)
 
 
 def test_fwd_rejects_bad_arguments_without_touching_the_device(built_lib):

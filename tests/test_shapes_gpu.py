@@ -1,8 +1,8 @@
 """GPU parity for networks served by a larger compiled network (zero padding
 through TMA): the caller's widths need only be multiples of 8 and at most the
 compiled widths of the same depth (64, 128 and 256 wide for 2, 3 and 4 layers;
-32-64-64-64-64-16, 64, 128 and 256 wide for 5), hidden widths may differ from
-each other.
+32-64-64-64-64-16, 64, 128 and 256 wide for 5; 64 (6 and 7 layers), 128 and
+256 wide for 6 to 8), hidden widths may differ from each other.
 
 The reference's kernel accepts any widths its tl.dot tiles divide
 (kernel.py:25-53, kernel.py:130-156) and its modules take D, H, out_features
@@ -50,6 +50,14 @@ SHAPES = [
     ((32, 64, 48, 64, 8), "4-layer 64-wide"),
     ((128, 96, 128, 112, 16), "4-layer 128-wide streamed"),
     ((200, 128, 64, 256, 8), "4-layer 256-wide streamed"),
+    ((64,) * 7, "6-layer 64-wide (exact)"),
+    ((32, 64, 16, 64, 48, 64, 8), "6-layer 64-wide"),
+    ((64,) * 8, "7-layer 64-wide (exact)"),
+    ((64,) * 9, "8-layer 64-wide, on the 128-wide kernels"),
+    ((128,) * 7, "6-layer 128-wide streamed (exact)"),
+    ((96, 128, 128, 64, 128, 128, 128, 128, 24), "8-layer 128-wide streamed"),
+    ((256,) * 8, "7-layer 256-wide streamed (exact)"),
+    ((200, 256, 8, 256, 64, 256, 256), "6-layer 256-wide streamed"),
 ]
 
 
