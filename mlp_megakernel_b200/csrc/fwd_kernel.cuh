@@ -143,9 +143,9 @@ struct FwdCfg {
   static constexpr int SPC = (HMAX / (EPW / 4)) / 32 >= 4 ? 2 : 1;
   static constexpr int MAXCH = ((HMAX / (EPW / 4) + 31) / 32 + SPC - 1) / SPC;  // chunks/layer
   // x_full, x_empty, out_ready, store_free per slot; acc_full per slot and
-  // accumulator buffer; MAXCH h-chunk barriers per slot; w_full; mma_done;
-  // (H32) pieces_done per slot
-  static constexpr int NUM_BARS = 6 * NS + NS * MAXCH + 2 + NS;
+  // accumulator buffer; MAXCH h-chunk barriers per slot; w_full per layer;
+  // mma_done; (H32) pieces_done per slot
+  static constexpr int NUM_BARS = 6 * NS + NS * MAXCH + L + 1 + NS;
   static constexpr int OFF_MISC = OFF_BAR + 8 * NUM_BARS;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
   static constexpr int SLOT_COLS = align_up(HMAX, 32);   // one accumulator buffer
@@ -358,8 +358,10 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW, H32>::THREADS, 1)
   auto bar_store_free = [&](int s) { return s_bar + 8u * (5 * NS + s); };
   // h chunk c of slot s: activation columns [32c, 32c+32), packed in TMEM
   auto bar_chunk = [&](int s, int c) { return s_bar + 8u * (6 * NS + s * Cfg::MAXCH + c); };
-  const uint32_t bar_w_full = s_bar + 8u * (6 * NS + NS * Cfg::MAXCH);
-  const uint32_t bar_mma_done = bar_w_full + 8u;
+  // layer l's weights have landed (one barrier per layer, so layer 0 of the
+  // first tile starts while the later layers' weights are still in flight)
+  auto bar_w_full = [&](int l) { return s_bar + 8u * (6 * NS + NS * Cfg::MAXCH + l); };
+  const uint32_t bar_mma_done = bar_w_full(L);
   // (H32) every warp of slot s has seen its fp32 piece stores read: the
   // output tile may overwrite the staging region
   auto bar_pieces_done = [&](int s) { return bar_mma_done + 8u + 8u * s; };
@@ -380,7 +382,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW, H32>::THREADS, 1)
       for (int c = 0; c < Cfg::MAXCH; ++c) mbar_init(bar_chunk(s, c), EPW);
       mbar_init(bar_pieces_done(s), EPW);
     }
-    mbar_init(bar_w_full, 1);
+    for (int l = 0; l < L; ++l) mbar_init(bar_w_full(l), 1);
     mbar_init(bar_mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -402,17 +404,23 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW, H32>::THREADS, 1)
     if (lane == 0) {
       tma_prefetch_desc(&maps.x);
       tma_prefetch_desc(&maps.out);
-      mbar_arrive_expect_tx(bar_w_full, NetT::w_bytes_exact());
-      static_for<0, L>([&](auto lc) {
-        constexpr int l = decltype(lc)::value;
-        constexpr int K = NetT::template D<l>();
-        constexpr int N = NetT::template D<l + 1>();
-        constexpr int C = chunk_elems(N);
-        constexpr int P = pitch_bytes(N);
+      // weights of layers [l0, l1), each on its own barrier
+      auto load_weights = [&](auto l0c, auto l1c) {
+        static_for<decltype(l0c)::value, decltype(l1c)::value>([&](auto lc) {
+          constexpr int l = decltype(lc)::value;
+          constexpr int K = NetT::template D<l>();
+          constexpr int N = NetT::template D<l + 1>();
+          constexpr int C = chunk_elems(N);
+          constexpr int P = pitch_bytes(N);
+          mbar_arrive_expect_tx(bar_w_full(l), tile_bytes(K, N));
 #pragma unroll
-        for (int c = 0; c < N / C; ++c)
-          tma_load_2d(s_w + NetT::template w_off<l>() + c * K * P, &maps.w[l], bar_w_full, c * C, 0);
-      });
+          for (int c = 0; c < N / C; ++c)
+            tma_load_2d(s_w + NetT::template w_off<l>() + c * K * P, &maps.w[l], bar_w_full(l), c * C, 0);
+        });
+      };
+      // layer 0's weights, then the first round of x tiles, then the rest
+      load_weights(std::integral_constant<int, 0>{}, std::integral_constant<int, 1>{});
+      bool rest_loaded = false;
       constexpr int C0 = chunk_elems(Cfg::D0);
       constexpr int P0 = pitch_bytes(Cfg::D0);
       bool ok = true;
@@ -438,10 +446,15 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW, H32>::THREADS, 1)
             tma_load_2d(s_x + s * Cfg::X_BYTES + c * kTileM * P0, &maps.x, bar_x_full(s), c * C0,
                         t * kTileM);
         }
+        if (!rest_loaded) {
+          load_weights(std::integral_constant<int, 1>{}, std::integral_constant<int, L>{});
+          rest_loaded = true;
+        }
       }
+      if (!rest_loaded) load_weights(std::integral_constant<int, 1>{}, std::integral_constant<int, L>{});
       // Drain: never leave the CTA with a TMA load still writing shared memory.
       volatile int no_abort = 0;
-      mbar_wait(bar_w_full, 0, &no_abort, kDevTimeoutFull);
+      for (int l = 0; l < L; ++l) mbar_wait(bar_w_full(l), 0, &no_abort, kDevTimeoutFull);
 #pragma unroll
       for (int s = 0; s < NS; ++s)
         if (issued[s] > 0) mbar_wait(bar_x_full(s), (issued[s] - 1) & 1, &no_abort, kDevTimeoutFull);
@@ -456,8 +469,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW, H32>::THREADS, 1)
     // The whole warp runs the loop (waits and descriptors are warp-uniform, so
     // they live in uniform registers); lane 0 issues the tcgen05 instructions.
     const bool issuer = (lane == 0);
-    bool ok = __all_sync(0xffffffffu, mbar_wait(bar_w_full, 0, abort_flag, kDevTimeoutMma));
-    tc_fence_after();
+    bool ok = true;
     for (int i = 0; ok; ++i) {
       if (tile_of(i, 0) >= num_tiles) break;
       static_for<0, L>([&](auto lc) {
@@ -466,6 +478,10 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW, H32>::THREADS, 1)
         constexpr int N = NetT::template D<l + 1>();
         constexpr uint32_t idesc = make_idesc_f16(kTileM, N, 0, 1);
         const uint64_t bdesc0 = mnmajor_base_desc<K, N>(s_w + NetT::template w_off<l>());
+        if (i == 0 && ok) {  // this layer's weights, before their first use
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_w_full(l), 0, abort_flag, kDevTimeoutMma));
+          tc_fence_after();
+        }
 #pragma unroll
         for (int s = 0; s < NS; ++s) {
           if (!ok || tile_of(i, s) >= num_tiles) break;

@@ -150,6 +150,37 @@ bool set_smem_once(Kern kern, int bytes, int dev) {
   return true;
 }
 
+// ------------------------------------------------------------------ descriptor cache
+// Encoded tensor maps of recent calls, per host thread: a serving loop calls
+// the forward again and again on the same buffers, and re-encoding every TMA
+// descriptor would be most of the host work of a small call.  The key holds
+// everything the maps encode (device, rows, every pointer, the caller's
+// widths, the saved-activation precision); four entries, replaced round robin.
+template <class Maps>
+struct MapCache {
+  static constexpr int kEntries = 4;
+  static constexpr int kKey = 40;
+  struct Entry {
+    bool valid = false;
+    uint64_t key[kKey];
+    Maps maps;
+  };
+  Entry e[kEntries];
+  int next = 0;
+  const Maps* find(const uint64_t* key) const {
+    for (const Entry& x : e)
+      if (x.valid && std::memcmp(x.key, key, sizeof(x.key)) == 0) return &x.maps;
+    return nullptr;
+  }
+  void insert(const uint64_t* key, const Maps& m) {
+    Entry& x = e[next];
+    next = (next + 1) % kEntries;
+    std::memcpy(x.key, key, sizeof(x.key));
+    x.maps = m;
+    x.valid = true;
+  }
+};
+
 // ------------------------------------------------------------------ forward
 // Every launcher takes the caller's widths rd[0..L] (each at most the kernel
 // network's width, a multiple of 8): tensor maps of the caller's tensors carry
@@ -169,35 +200,64 @@ int launch_fwd(const int* rd, const void* x, const void* const* W, void* out, in
   if (M == 0) return MLPK_OK;
   if (M > (int64_t(1) << 31) - 256) return MLPK_ERR_SHAPE;
 
-  FwdMaps<L> maps;
-  std::memset(&maps, 0, sizeof(maps));
-  rc = make_map_2d(&maps.x, x, rd[0], M, mlpk::chunk_elems(Cfg::D0), mlpk::kTileM);
-  if (rc) return rc;
-  rc = make_map_2d(&maps.out, out, rd[L], M, mlpk::chunk_elems(Cfg::DL), mlpk::kTileM);
-  if (rc) return rc;
-  int wrc = MLPK_OK;
-  mlpk::static_for<0, L>([&](auto lc) {
-    constexpr int l = decltype(lc)::value;
-    constexpr int K = NetT::template D<l>();
-    constexpr int N = NetT::template D<l + 1>();
-    if (wrc == MLPK_OK) wrc = make_map_2d(&maps.w[l], W[l], rd[l + 1], rd[l], mlpk::chunk_elems(N), K);
-  });
-  if (wrc) return wrc;
-  maps.M = static_cast<int>(M);
-  maps.out_cols = rd[L];
-  for (int l = 0; l + 1 < L; ++l) maps.h_cols[l] = rd[l + 1];
-  if (hsave) {
-    for (int l = 0; l + 1 < L; ++l) {
-      if (!hsave[l]) return MLPK_ERR_NULL;
-      // fp32: every warp stores its 32 rows x 32 columns per piece
-      rc = h32 ? make_map_2d(&maps.hsave[l], hsave[l], rd[l + 1], M, 32, 32, 4)
-               : make_map_2d(&maps.hsave[l], hsave[l], rd[l + 1], M, mlpk::chunk_elems(Cfg::H), mlpk::kTileM);
-      if (rc) return rc;
-    }
+  thread_local MapCache<FwdMaps<L>> cache;
+  uint64_t key[MapCache<FwdMaps<L>>::kKey] = {};
+  {
+    int k = 0;
+    key[k++] = static_cast<uint64_t>(dev);
+    key[k++] = static_cast<uint64_t>(M);
+    key[k++] = reinterpret_cast<uintptr_t>(x);
+    key[k++] = reinterpret_cast<uintptr_t>(out);
+    key[k++] = (hsave ? 1u : 0u) | (h32 ? 2u : 0u);
+    for (int l = 0; l < L; ++l) key[k++] = reinterpret_cast<uintptr_t>(W[l]);
+    for (int l = 0; hsave && l + 1 < L; ++l) key[k++] = reinterpret_cast<uintptr_t>(hsave[l]);
+    for (int i = 0; i <= L; ++i) key[k++] = static_cast<uint64_t>(rd[i]);
   }
-
   const int num_tiles = static_cast<int>((M + mlpk::kTileM - 1) / mlpk::kTileM);
   const int grid = num_tiles < di.sm_count ? num_tiles : di.sm_count;
+  FwdMaps<L> maps;
+  if (const FwdMaps<L>* hit = cache.find(key)) {
+    maps = *hit;
+  } else {
+    std::memset(&maps, 0, sizeof(maps));
+    rc = make_map_2d(&maps.x, x, rd[0], M, mlpk::chunk_elems(Cfg::D0), mlpk::kTileM);
+    if (rc) return rc;
+    rc = make_map_2d(&maps.out, out, rd[L], M, mlpk::chunk_elems(Cfg::DL), mlpk::kTileM);
+    if (rc) return rc;
+    int wrc = MLPK_OK;
+    mlpk::static_for<0, L>([&](auto lc) {
+      constexpr int l = decltype(lc)::value;
+      constexpr int K = NetT::template D<l>();
+      constexpr int N = NetT::template D<l + 1>();
+      if (wrc == MLPK_OK) wrc = make_map_2d(&maps.w[l], W[l], rd[l + 1], rd[l], mlpk::chunk_elems(N), K);
+    });
+    if (wrc) return wrc;
+    maps.M = static_cast<int>(M);
+    maps.out_cols = rd[L];
+    for (int l = 0; l + 1 < L; ++l) maps.h_cols[l] = rd[l + 1];
+    if (hsave) {
+      for (int l = 0; l + 1 < L; ++l) {
+        if (!hsave[l]) return MLPK_ERR_NULL;
+        // fp32: every warp stores its 32 rows x 32 columns per piece
+        rc = h32 ? make_map_2d(&maps.hsave[l], hsave[l], rd[l + 1], M, 32, 32, 4)
+                 : make_map_2d(&maps.hsave[l], hsave[l], rd[l + 1], M, mlpk::chunk_elems(Cfg::H), mlpk::kTileM);
+        if (rc) return rc;
+      }
+    }
+    cache.insert(key, maps);
+  }
+  if (!hsave && num_tiles <= di.sm_count) {
+    // Small batches (every CTA gets at most one row tile): the latency
+    // configuration -- one tile in flight and up to four column groups of
+    // epilogue warps, so each warp runs one 32-column stripe of a layer
+    // instead of all of them (the tile's MMA -> softplus -> MMA chain is the
+    // whole kernel time here, not the throughput of several tiles).
+    constexpr int kLatEpw = 4 * (Cfg::H / 32 < 4 ? Cfg::H / 32 : 4);
+    using CfgL = FwdCfg<NetT, 1, kLatEpw>;
+    auto kern = mlpk::mlp_fwd_kernel<NetT, 1, kLatEpw, false>;
+    if (!set_smem_once(kern, CfgL::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
+    return launch_kernel(kern, grid, CfgL::THREADS, CfgL::SMEM_BYTES, st, maps, num_tiles);
+  }
   if (hsave && h32) {
     auto kern = mlpk::mlp_fwd_kernel<NetT, NS, EPW, true, true>;
     if (!set_smem_once(kern, Cfg32::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;

@@ -10,14 +10,16 @@ Mirrors the reference's functional surface:
 * ``ModelNew`` -- the nn.Module shim of kernel.py:174-180.
 
 Every call runs the sm_100a kernel in libmlpk through its C ABI on the current
-CUDA stream.  x and the weights are fp16, or fp32 as the reference also
-accepts (kernel.py:37-43, 134-138): fp32 operands are rounded to fp16 by the
-library's cast kernel, the fused fp16 kernel runs, and its fp16-rounded result
-is widened into the fp32 output -- the reference's own rounding points for the
-hidden activations (kernel.py:110, 117) and the output (kernel.py:121-124).
-(The reference rounds fp32 x and W to tf32 for its first GEMM: the same 10
-mantissa bits, but fp32's exponent range; fp16 here turns magnitudes above
-65,504 into infinities.)
+CUDA stream.  x and the weights are fp16, or fp32: the reference's launcher
+selects fp32 tile configurations (kernel.py:37-43, 138), though its kernel
+fails on fp32 operands at the second GEMM (it casts h1 to fp16 and dots it
+with the fp32 W2: "Both operands must be same dtype", kernel.py:110).  Here
+fp32 operands are rounded to fp16 by the library's cast kernel, the fused
+fp16 kernel runs, and its fp16-rounded result is widened into the fp32
+output -- the reference's rounding points for the hidden activations
+(kernel.py:110, 117) and the output (kernel.py:121-124).  fp16 keeps tf32's
+10 mantissa bits but not fp32's exponent range: magnitudes above 65,504
+become infinite and below 6.1e-5 lose precision.
 There is no CPU or PyTorch fallback: CPU tensors, other dtypes or unsupported
 shapes raise.
 """
@@ -37,14 +39,16 @@ def _check_operands(x: torch.Tensor, weights) -> list:
         raise ValueError("x must be a 2-D tensor [M, in_features]")
     if not x.is_cuda:
         raise RuntimeError("fused MLP runs on CUDA (sm_100) only; got a CPU tensor")
-    if x.dtype not in (torch.float16, torch.float32):
+    dt = x.dtype
+    if dt is not torch.float16 and dt is not torch.float32:
         raise TypeError(f"fused MLP takes fp16 or fp32 inputs (fp16 operands, fp32 accumulate); "
                         f"got x.dtype={x.dtype}")
     if len(weights) < 1:
         raise ValueError("need at least one weight matrix")
+    dev = x.device
     dims = [x.shape[1]]
     for i, w in enumerate(weights):
-        if w.dim() != 2 or w.device != x.device or w.dtype != x.dtype:
+        if w.dim() != 2 or w.dtype is not dt or w.device != dev:
             raise ValueError(f"weight {i} must be a 2-D {x.dtype} tensor on {x.device}")
         if w.shape[0] != dims[-1]:
             raise ValueError(
@@ -55,6 +59,38 @@ def _check_operands(x: torch.Tensor, weights) -> list:
     return dims
 
 
+def _current_stream(dev_index: int) -> int:
+    """Raw handle of the current CUDA stream of a device."""
+    try:
+        return torch._C._cuda_getCurrentRawStream(dev_index)
+    except AttributeError:  # older torch: through the Stream object
+        return torch.cuda.current_stream(dev_index).cuda_stream
+
+
+try:
+    from torch._subclasses.fake_tensor import is_fake as _is_fake
+except ImportError:  # no FakeTensor support: every tensor is real
+    def _is_fake(t) -> bool:
+        return False
+
+
+def _eager_fwd(x: torch.Tensor, weights, out: torch.Tensor) -> None:
+    """The fp16 forward straight through the C ABI (no operator dispatch):
+    the per-call cost of an eager call is the host work here, so it is kept to
+    one pointer array and one ctypes call."""
+    dev = x.get_device()
+    if dev != torch.cuda.current_device():
+        with torch.cuda.device(dev):
+            return _eager_fwd(x, weights, out)
+    x = _aligned(x)
+    ws = [_aligned(w) for w in weights]
+    dims = [x.shape[1]] + [w.shape[1] for w in ws]
+    lib = _lib.lib()
+    ptrs = (ctypes.c_void_p * len(ws))(*[w.data_ptr() for w in ws])
+    _lib.check("mlpk_fwd", lib.mlpk_fwd(ctypes.byref(_lib.shape_struct(dims)), x.shape[0], x.data_ptr(), ptrs,
+                                        out.data_ptr(), _current_stream(dev)))
+
+
 def fused_mlp_fwd(x: torch.Tensor, *weights: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
     """``softplus(...softplus(x @ W_0)...) @ W_{L-1}`` in one kernel launch.
 
@@ -63,18 +99,27 @@ def fused_mlp_fwd(x: torch.Tensor, *weights: torch.Tensor, out: torch.Tensor = N
     (kernel.py:110, kernel.py:117).  Like the reference (kernel.py:136) the
     result is a new tensor unless ``out`` (contiguous, ``[M, out_features]``,
     x's dtype and device) is given, which lets a serving loop reuse one buffer.
-    Runs as the custom operator ``torch.ops.mlpk.fwd`` (``fwd_out`` with
-    ``out``), so torch.compile traces it as one operator.
+    Under torch.compile it is the custom operator ``torch.ops.mlpk.fwd``
+    (``fwd_out`` with ``out``), traced as one operator; eager fp16 calls go
+    straight to the C ABI.
     """
     dims = _check_operands(x, weights)
     M = x.shape[0]
-    if out is None:
-        return torch.ops.mlpk.fwd(x, list(weights))
-    if (out.shape != (M, dims[-1]) or out.dtype != x.dtype or out.device != x.device
-            or not out.is_contiguous()):
+    if out is not None and (out.shape != (M, dims[-1]) or out.dtype != x.dtype or out.device != x.device
+                            or not out.is_contiguous()):
         raise ValueError("out must be a contiguous, 16-byte aligned "
                          f"[{M}, {dims[-1]}] {x.dtype} tensor on {x.device}")
-    torch.ops.mlpk.fwd_out(x, list(weights), out)
+    if torch.compiler.is_compiling() or x.dtype != torch.float16 or _is_fake(x):
+        if out is None:
+            return torch.ops.mlpk.fwd(x, list(weights))
+        torch.ops.mlpk.fwd_out(x, list(weights), out)
+        return out
+    if out is None:
+        out = torch.empty((M, dims[-1]), device=x.device, dtype=x.dtype)
+    elif out.data_ptr() % 16 != 0:
+        raise ValueError("out must be 16-byte aligned")
+    if M > 0:
+        _eager_fwd(x, weights, out)
     return out
 
 

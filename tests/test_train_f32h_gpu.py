@@ -9,8 +9,11 @@ are the fp32 values and its backward uses them in the sigmoid, i.e. exactly
 this storage), and against the fp16-storage path.
 
 Tolerances (north star): outputs max|d| <= 1e-2 * max|ref|; gradients
-relative L2 <= 1e-2; the saved fp32 h within 1e-4 (relative to max|h|) of
-the float64 softplus (the kernel's softplus is accurate to ~1e-5 relative).
+relative L2 <= 1e-2.  The saved fp32 h: rounded to fp16 it equals, bitwise,
+the h the fp16-storage path saves (both are the round-to-nearest of the same
+fp32 softplus value, the operand the next GEMM consumed); against the oracle
+within 1e-3 of max|h| (the oracle's pre-activations are float64, the
+kernel's fp32 accumulations in another order).
 """
 import ctypes
 
@@ -27,7 +30,7 @@ pytestmark = pytest.mark.gpu
 
 GRAD_TOL = 1e-2
 OUT_TOL = 1e-2
-H_TOL = 1e-4
+H_TOL = 1e-3
 
 
 def rel_l2(a, b):
@@ -77,6 +80,9 @@ def _check(dims, x, ws, g, h_dtype=torch.float32):
     if h_dtype == torch.float32:
         for h, rh in zip(hs, ref_hs):
             assert rel_max(h.cpu().numpy(), rh) <= H_TOL
+        _, hs16 = _train_forward(xg, wg, dims, torch.float16)
+        for h, h16 in zip(hs, hs16):
+            assert torch.equal(h.half(), h16)
     ref_dx, ref_dws = oracle.mlp_backward(x.numpy(), [w.numpy() for w in ws], ref_hs, g.numpy())
     errs = [rel_l2(dx.cpu().numpy(), ref_dx)]
     errs += [rel_l2(d, rd) for d, rd in zip(_split(dw.cpu().numpy(), dims), ref_dws)]

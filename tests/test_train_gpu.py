@@ -441,8 +441,8 @@ def test_functional_forward_under_torch_compile():
     x, ws = make_inputs("3L128", 3000)
     xg, wg = x.cuda(), [w.cuda() for w in ws]
 
-    def f(a):
-        return fused_mlp_fwd(a * 2, *wg).float().sum(dim=1)
+    def f(a):  # exact fp16 arithmetic around the operator: results bitwise comparable
+        return fused_mlp_fwd(a * 2, *wg) * 0.5
 
     torch._dynamo.reset()
     ref = f(xg)
