@@ -109,17 +109,18 @@ struct BwdCfg {
   static constexpr int ACC_W = align_up(DMAX, 32);
   static constexpr int TILE_BYTES = align_up(tile_bytes(kTileM, DMAX), 1024);
   static constexpr int W_TOTAL = NetT::w_total();
-  static constexpr int ZERO_BYTES = any_pad() ? 16384 : 0;  // 128 rows x 128 B
-  static constexpr int G_TILES = H32 ? 0 : 1;  // dz tiles (G) per tile slot
-  // ring slots that fit in shared memory next to the weights, `ns` dz tiles
-  // (G), the zero chunk and the barriers: w_full, slot_full[8],
+  // zero rows that pad a 64-wide weight-gradient M to 128: one UMMA reads 16
+  // K-rows of it, and every K-step's descriptor points at the same 16 rows
+  static constexpr int ZERO_BYTES = any_pad() ? 2048 : 0;  // 16 rows x 128 B
+  // ring slots that fit in shared memory next to the weights, `ns` x `ng` dz
+  // tiles (G), the zero rows and the barriers: w_full, slot_full[8],
   // slot_empty[8], then per tile slot acc_full, acc_free, wg_done, dz_full,
   // out_ready; mma_done; rd_done
-  __host__ __device__ static constexpr int ring_fit(int ns) {
-    return (232448 - 1024 - 16 - 8 * (3 + 2 * 8 + 5 * ns) - (W_TOTAL + ns * G_TILES * TILE_BYTES) -
-            ZERO_BYTES) /
+  __host__ __device__ static constexpr int ring_fit_g(int ns, int ng) {
+    return (232448 - 1024 - 16 - 8 * (3 + 2 * 8 + 5 * ns) - (W_TOTAL + ns * ng * TILE_BYTES) - ZERO_BYTES) /
            TILE_BYTES;
   }
+  __host__ __device__ static constexpr int ring_cap(int r) { return r > 8 ? 8 : r; }
   // every hidden width splits into two fp32 halves of whole 32-column chunks,
   // each fitting a ring slot
   __host__ __device__ static constexpr bool h32_ok() {
@@ -132,8 +133,18 @@ struct BwdCfg {
   // the first two of the next (see the producer); the MMA warp then
   // alternates the slots' layer steps so one slot's epilogue overlaps the
   // other slot's MMAs.
-  static constexpr int NS =
-      (!H32 && dw_col(L) + 2 * ACC_W <= 512 && (ring_fit(2) > 8 ? 8 : ring_fit(2)) >= L + 3) ? 2 : 1;
+  // Tiles in flight and dz tiles per tile slot: two tiles where TMEM holds a
+  // second dgrad accumulator and the ring keeps one tile's loads plus the
+  // first two of the next; two dz tiles per slot (the epilogue writes dz_l
+  // while the MMAs still read dz_{l+1}) where the ring keeps that depth with
+  // them (with one tile in flight: a ring of 4).  fp32 saved activations:
+  // one tile, no dz tile (dz lives in h's high half-slot).
+  static constexpr bool TMEM2 = dw_col(L) + 2 * ACC_W <= 512;
+  static constexpr int NS = (!H32 && TMEM2 && ring_cap(ring_fit_g(2, 1)) >= L + 3) ? 2 : 1;
+  static constexpr int G_TILES = H32 ? 0
+                                 : (NS == 2 ? (ring_cap(ring_fit_g(2, 2)) >= L + 3 ? 2 : 1)
+                                            : (ring_cap(ring_fit_g(1, 2)) >= 4 ? 2 : 1));
+  __host__ __device__ static constexpr int ring_fit(int ns) { return ring_fit_g(ns, G_TILES); }
   // loads per tile: g, then h_{L-1} .. h_1 (one slot each, or two fp32 halves
   // each), then x
   static constexpr int NLD = H32 ? 2 * L : L + 1;
@@ -148,7 +159,7 @@ struct BwdCfg {
     }
     return true;
   }
-  static constexpr int OFF_G = W_TOTAL;                  // G of slot s at OFF_G + s * TILE_BYTES
+  static constexpr int OFF_G = W_TOTAL;  // G b of slot s at OFF_G + (s * G_TILES + b) * TILE_BYTES
   static constexpr int OFF_RING = OFF_G + NS * G_TILES * TILE_BYTES;
   static constexpr int RING_FIT = ring_fit(NS);
   static constexpr int RING = RING_FIT > 8 ? 8 : RING_FIT;
@@ -253,7 +264,11 @@ __global__ void __launch_bounds__(BwdCfg<NetT, H32>::THREADS, 1)
   uint8_t* gbase = smem_raw + (sbase - raw);
 
   const uint32_t s_w = sbase;
-  auto s_g = [&](int s) { return sbase + Cfg::OFF_G + static_cast<uint32_t>(s) * Cfg::TILE_BYTES; };
+  // dz tile of slot s written at the slot's step st (read by the next step)
+  auto s_g = [&](int s, int st) {
+    const int b = Cfg::G_TILES > 1 ? (st & 1) : 0;
+    return sbase + Cfg::OFF_G + static_cast<uint32_t>(s * Cfg::G_TILES + b) * Cfg::TILE_BYTES;
+  };
   auto slot_addr = [&](int r) { return sbase + Cfg::OFF_RING + static_cast<uint32_t>(r) * Cfg::TILE_BYTES; };
   const uint32_t s_zero = sbase + Cfg::OFF_ZERO;
   const uint32_t s_bar = sbase + Cfg::OFF_BAR;
@@ -443,14 +458,17 @@ __global__ void __launch_bounds__(BwdCfg<NetT, H32>::THREADS, 1)
       const uint32_t a_base = TR ? zsrc : a_h;
       const uint32_t b_base = TR ? a_h : zsrc;
       constexpr int PA = pitch_bytes(MW);
-      const uint32_t lbo = (MW < 128) ? (s_zero - a_base) : kTileM * PA;
-      const uint64_t aw0 = make_sdesc(a_base, lbo, 8 * PA, umma_layout_code(PA));
       const uint64_t bw0 = mnmajor_base_desc<kTileM, NW>(b_base);
       const uint32_t dw = tmem_base + Cfg::dw_col(l);
 #pragma unroll
-      for (int k = 0; k < kTileM / 16; ++k)
-        umma_f16(dw, aw0 + (mnmajor_koff<MW>(k) >> 4), bw0 + (mnmajor_koff<NW>(k) >> 4), idesc_w,
-                 (i > 0 || k > 0) ? 1u : 0u);
+      for (int k = 0; k < kTileM / 16; ++k) {
+        // a 64-wide A: its second 64-column chunk (LBO) is the 16 zero rows,
+        // the same for every K-step
+        const uint32_t a_k = a_base + mnmajor_koff<MW>(k);
+        const uint32_t lbo = (MW < 128) ? (s_zero - a_k) : kTileM * PA;
+        umma_f16(dw, make_sdesc(a_k, lbo, 8 * PA, umma_layout_code(PA)), bw0 + (mnmajor_koff<NW>(k) >> 4),
+                 idesc_w, (i > 0 || k > 0) ? 1u : 0u);
+      }
     };
     bool ok = __all_sync(0xffffffffu, mbar_wait(bar_w_full, 0, abort_flag, kDevTimeoutMma));
     tc_fence_after();
@@ -529,8 +547,10 @@ __global__ void __launch_bounds__(BwdCfg<NetT, H32>::THREADS, 1)
             const uint32_t acc = tmem_base + Cfg::ACC_COL + s * Cfg::ACC_W;
             const int ng = i * NLD;            // g
             const int na = i * NLD + (L - l);  // h_l (x for l == 0)
-            // dz_{l+1}: g (a ring slot) for the last layer, else the slot's G
-            uint32_t zsrc = s_g(s);
+            const int st = p * L + (L - 1 - l);  // this slot's step count
+            // dz_{l+1}: g (a ring slot) for the last layer, else the G tile the
+            // epilogue of the previous step wrote
+            uint32_t zsrc = s_g(s, st - 1);
             if constexpr (l == L - 1) {
               ok = __all_sync(0xffffffffu, mbar_wait(bar_slot_full(ng % R), (ng / R) & 1, abort_flag,
                                                      kDevTimeoutMma)) &&
@@ -578,7 +598,6 @@ __global__ void __launch_bounds__(BwdCfg<NetT, H32>::THREADS, 1)
     const uint32_t row = q * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t acc = tmem_base + lane_off + Cfg::ACC_COL + s * Cfg::ACC_W;
-    const uint32_t sg = s_g(s);
     bool ok = true;
     for (int j = 0; ok; ++j) {
       const int i = j * NS + s;  // this slot's j-th tile
@@ -668,9 +687,15 @@ __global__ void __launch_bounds__(BwdCfg<NetT, H32>::THREADS, 1)
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(bar_slot_empty(nh % R));  // h_l read
-          // G still holds dz_{l+1} until this layer's wgrad has read it
-          ok = __all_sync(0xffffffffu, mbar_wait(bar_wg_done(s), step & 1, abort_flag, kDevTimeoutEpi));
-          if (!ok) return;
+          if constexpr (Cfg::G_TILES == 1) {
+            // G still holds dz_{l+1} until this layer's wgrad has read it
+            ok = __all_sync(0xffffffffu, mbar_wait(bar_wg_done(s), step & 1, abort_flag, kDevTimeoutEpi));
+            if (!ok) return;
+          }
+          // With two G tiles, this step's tile was last read by the previous
+          // step's MMAs, all complete: the accumulator's commit (waited above)
+          // tracks every MMA the issuing thread had issued before it.
+          const uint32_t sg = s_g(s, step);
 #pragma unroll
           for (int u = 0; u < CW / 8; ++u)
             st_tile_row8<DI>(sg, row, c0 + 8 * u, o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
