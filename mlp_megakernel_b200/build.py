@@ -47,6 +47,29 @@ def _stale() -> bool:
     return any(os.path.getmtime(f) > t for f in files if os.path.exists(f))
 
 
+DEVTEST_SRC = os.path.join(ROOT, "tests", "device_api", "devtest.cu")
+DEVTEST_LIB = os.path.join(ROOT, "tests", "device_api", "libmlpk_devtest.so")
+
+
+def build_devtest(force: bool = False, verbose: bool = False) -> str:
+    """Compile the device-API test kernels (tests/device_api/devtest.cu, a
+    user kernel calling include/mlpk_device.cuh) if missing or stale."""
+    deps = [DEVTEST_SRC, os.path.join(ROOT, "include", "mlpk_device.cuh")] + \
+        [os.path.join(CSRC, f) for f in DEPS + ["device_mlp.cuh"]]
+    if not force and os.path.exists(DEVTEST_LIB) and \
+            all(os.path.getmtime(f) <= os.path.getmtime(DEVTEST_LIB) for f in deps if os.path.exists(f)):
+        return DEVTEST_LIB
+    tmp = DEVTEST_LIB + ".tmp"
+    cmd = [nvcc_path(), *NVCC_FLAGS, "-o", tmp, DEVTEST_SRC]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError("nvcc failed:\n" + res.stdout + res.stderr)
+    os.replace(tmp, DEVTEST_LIB)
+    return DEVTEST_LIB
+
+
 def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> str:
     """Compile libmlpk.so if missing or older than its sources; return its path."""
     if not force and not _stale():
