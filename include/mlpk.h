@@ -73,6 +73,20 @@ int mlpk_shape_supported(const mlpk_shape* shape);
 int mlpk_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W, void* out,
              mlpk_stream_t stream);
 
+/* ---- fp32 inference on tf32 tensor cores.  The reference's design keeps
+ * fp32 operands fp32 through the whole chain (INPUT_DTYPE fp32,
+ * mlp_fused.md:159-166; its kernel.py selects fp32 tiles at kernel.py:37-43
+ * but fails at the second GEMM on them).  mlpk_fwd_ex with MLPK_DT_F32: x, W
+ * and out fp32; every GEMM is a tf32 tensor-core GEMM (the inputs' 10
+ * mantissa bits, fp32's exponent range) with fp32 accumulation, the hidden
+ * activations stay fp32.  Served for networks up to 128 wide
+ * (mlpk_shape_supported_ex); MLPK_DT_F16 is mlpk_fwd. */
+#define MLPK_DT_F16 0
+#define MLPK_DT_F32 1
+int mlpk_shape_supported_ex(const mlpk_shape* shape, int dtype);
+int mlpk_fwd_ex(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W, void* out, int dtype,
+                mlpk_stream_t stream);
+
 /* 1 if training (mlpk_train_fwd + mlpk_bwd) serves this shape (the same
  * rule as mlpk_shape_supported). */
 int mlpk_train_supported(const mlpk_shape* shape);

@@ -46,6 +46,8 @@ SIGNATURES = {
     "mlpk_train_supported": (ctypes.c_int, [_SHAPE_P]),
     "mlpk_train_fwd": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _vp, _VPP, _vp]),
     "mlpk_train_supported_ex": (ctypes.c_int, [_SHAPE_P, ctypes.c_int]),
+    "mlpk_shape_supported_ex": (ctypes.c_int, [_SHAPE_P, ctypes.c_int]),
+    "mlpk_fwd_ex": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _vp, ctypes.c_int, _vp]),
     "mlpk_train_fwd_ex": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _vp, _VPP, ctypes.c_int, _vp]),
     "mlpk_bwd_workspace_size": (ctypes.c_int64, [_SHAPE_P, ctypes.c_int64]),
     "mlpk_bwd": (ctypes.c_int, [_SHAPE_P, ctypes.c_int64, _vp, _VPP, _VPP, _vp, _vp, _vp,
@@ -72,6 +74,8 @@ SIGNATURES = {
 FWD_HOST_CHUNK_ROWS = 131072
 H_F16 = 0  # MLPK_H_F16: saved activations in fp16
 H_F32 = 1  # MLPK_H_F32: saved activations in fp32 (the reference's storage)
+DT_F16 = 0  # MLPK_DT_F16: fp16 operands
+DT_F32 = 1  # MLPK_DT_F32: fp32 operands on tf32 tensor cores
 PEER_HANDLE_BYTES = 64
 PEER_MAX_RANKS = 8
 

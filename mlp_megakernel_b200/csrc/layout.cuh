@@ -56,6 +56,15 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, int a_mn_maj
          | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Instruction descriptor, kind::tf32: A, B tf32 (format 2), D fp32.
+__host__ __device__ constexpr uint32_t make_idesc_tf32(int M, int N, int a_mn_major, int b_mn_major) {
+  return (1u << 4)                                    // D format: f32
+         | (2u << 7) | (2u << 10)                     // A, B format: tf32
+         | (static_cast<uint32_t>(a_mn_major) << 15)  // A major
+         | (static_cast<uint32_t>(b_mn_major) << 16)  // B major
+         | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
 // Byte offset of K-step `k` (16 elements of K) inside a K-major operand with
 // `ROWS` rows and K extent `KEXT` (see the chunk layout above).
 template <int ROWS, int KEXT>

@@ -409,6 +409,34 @@ int launch_stream_fwd(const int* rd, const void* x, const void* const* W, void* 
   return launch_kernel(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, st, maps, static_cast<int>(tiles));
 }
 
+// fp32 forward on tf32 tensor cores (networks up to 128 wide): x, W and out
+// fp32, every GEMM kind::tf32, hidden activations fp32 in TMEM.
+template <class NetT>
+int launch_stream_fwd_tf32(const int* rd, const void* x, const void* const* W, void* out, int64_t M,
+                           cudaStream_t st) {
+  using Cfg = mlpk::StreamCfg<NetT, kStreamEpw, true>;
+  constexpr int L = NetT::L;
+  DevInfo di;
+  int dev = 0;
+  int rc = current_device_info(&di, &dev);
+  if (rc != MLPK_OK) return rc;
+  if (M == 0) return MLPK_OK;
+  if (M > (int64_t(1) << 31) - 256) return MLPK_ERR_SHAPE;
+  mlpk::StreamMaps<L> maps;
+  std::memset(&maps, 0, sizeof(maps));
+  if ((rc = make_map_2d(&maps.in, x, rd[0], M, 32, mlpk::kTileM, 4))) return rc;
+  if ((rc = make_map_2d(&maps.out, out, rd[L], M, 32, mlpk::kTileM, 4))) return rc;
+  for (int l = 0; l < L; ++l)  // K-chunks of 64 rows, boxes {32 columns, 64 rows}
+    if ((rc = make_map_2d(&maps.w[l], W[l], rd[l + 1], rd[l], 32, mlpk::kStreamK, 4))) return rc;
+  maps.M = static_cast<int>(M);
+  maps.out_cols = rd[L];
+  const int64_t tiles = (M + mlpk::kTileM - 1) / mlpk::kTileM;
+  const int grid = static_cast<int>(tiles < di.sm_count ? tiles : di.sm_count);
+  auto kern = mlpk::mlp_stream_kernel<NetT, kStreamEpw, mlpk::kStreamFwd, false, true>;
+  if (!set_smem_once(kern, Cfg::SMEM_BYTES, dev)) return MLPK_ERR_CUDA;
+  return launch_kernel(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, st, maps, static_cast<int>(tiles));
+}
+
 // Workspace of the streamed backward: the data-gradient chain's dz_1..dz_{L-1}
 // (fp16 [M, H] each, read back by the weight-gradient kernel), then the fp32
 // partials of the weight-gradient CTAs.
@@ -524,12 +552,14 @@ using Fwd = int (*)(const int*, const void*, const void* const*, void*, int64_t,
 using Bwd = int (*)(const int*, const void*, const void* const*, const void* const*, bool, const void*,
                     void*, float*, size_t, float*, int64_t, cudaStream_t);
 using BwdWs = size_t (*)(int64_t, int);
+using Fwd32 = int (*)(const int*, const void*, const void* const*, void*, int64_t, cudaStream_t);
 
 struct ShapeOps {
   Fwd fwd = nullptr;
   Bwd bwd = nullptr;
   BwdWs bwd_ws = nullptr;
   bool h32 = false;  // fp32 saved activations served (the fused kernels)
+  Fwd32 fwd32 = nullptr;  // fp32 forward on tf32 tensor cores (up to 128 wide)
 };
 
 // The compiled networks, smallest first.  A caller's network is served by the
@@ -583,11 +613,13 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.fwd = &launch_fwd<N64, 3, 4>;
     o.bwd = &launch_bwd<N64>;
     o.bwd_ws = &bwd_workspace<N64>;
+    o.fwd32 = &launch_stream_fwd_tf32<N64>;
     o.h32 = true;
   } else if (covers<N3>(s)) {
     o.fwd = &launch_fwd<N3, 2, 4>;
     o.bwd = &launch_bwd<N3>;
     o.bwd_ws = &bwd_workspace<N3>;
+    o.fwd32 = &launch_stream_fwd_tf32<N3>;
     o.h32 = true;
   } else if (covers<N256>(s)) {
     o.fwd = &launch_stream_fwd<N256>;
@@ -597,16 +629,19 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.fwd = &launch_fwd<N5, 3, 4>;
     o.bwd = &launch_bwd<N5>;
     o.bwd_ws = &bwd_workspace<N5>;
+    o.fwd32 = &launch_stream_fwd_tf32<N5w64>;
     o.h32 = true;
   } else if (covers<N5w64>(s)) {
     o.fwd = &launch_fwd<N5w64, 3, 4>;
     o.bwd = &launch_bwd<N5w64>;
     o.bwd_ws = &bwd_workspace<N5w64>;
+    o.fwd32 = &launch_stream_fwd_tf32<N5w64>;
     o.h32 = true;
   } else if (covers<N5w128>(s)) {
     o.fwd = &launch_stream_fwd<N5w128>;
     o.bwd = &launch_stream_bwd<N5w128>;
     o.bwd_ws = &stream_bwd_workspace<N5w128>;
+    o.fwd32 = &launch_stream_fwd_tf32<N5w128>;
   } else if (covers<N5w256>(s)) {
     o.fwd = &launch_stream_fwd<N5w256>;
     o.bwd = &launch_stream_bwd<N5w256>;
@@ -615,11 +650,13 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.fwd = &launch_fwd<N2w64, 3, 4>;
     o.bwd = &launch_bwd<N2w64>;
     o.bwd_ws = &bwd_workspace<N2w64>;
+    o.fwd32 = &launch_stream_fwd_tf32<N2w64>;
     o.h32 = true;
   } else if (covers<N2w128>(s)) {
     o.fwd = &launch_fwd<N2w128, 2, 4>;
     o.bwd = &launch_bwd<N2w128>;
     o.bwd_ws = &bwd_workspace<N2w128>;
+    o.fwd32 = &launch_stream_fwd_tf32<N2w128>;
     o.h32 = true;
   } else if (covers<N2w256>(s)) {
     o.fwd = &launch_stream_fwd<N2w256>;
@@ -629,11 +666,13 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.fwd = &launch_fwd<N4w64, 3, 4>;
     o.bwd = &launch_bwd<N4w64>;
     o.bwd_ws = &bwd_workspace<N4w64>;
+    o.fwd32 = &launch_stream_fwd_tf32<N4w64>;
     o.h32 = true;
   } else if (covers<N4w128>(s)) {
     o.fwd = &launch_stream_fwd<N4w128>;
     o.bwd = &launch_stream_bwd<N4w128>;
     o.bwd_ws = &stream_bwd_workspace<N4w128>;
+    o.fwd32 = &launch_stream_fwd_tf32<N4w128>;
   } else if (covers<N4w256>(s)) {
     o.fwd = &launch_stream_fwd<N4w256>;
     o.bwd = &launch_stream_bwd<N4w256>;
@@ -642,11 +681,13 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.fwd = &launch_fwd<N6w64, 3, 4>;
     o.bwd = &launch_bwd<N6w64>;
     o.bwd_ws = &bwd_workspace<N6w64>;
+    o.fwd32 = &launch_stream_fwd_tf32<N6w64>;
     o.h32 = true;
   } else if (covers<N6w128>(s)) {
     o.fwd = &launch_stream_fwd<N6w128>;
     o.bwd = &launch_stream_bwd<N6w128>;
     o.bwd_ws = &stream_bwd_workspace<N6w128>;
+    o.fwd32 = &launch_stream_fwd_tf32<N6w128>;
   } else if (covers<N6w256>(s)) {
     o.fwd = &launch_stream_fwd<N6w256>;
     o.bwd = &launch_stream_bwd<N6w256>;
@@ -655,11 +696,13 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.fwd = &launch_fwd<N7w64, 3, 4>;
     o.bwd = &launch_bwd<N7w64>;
     o.bwd_ws = &bwd_workspace<N7w64>;
+    o.fwd32 = &launch_stream_fwd_tf32<N7w64>;
     o.h32 = true;
   } else if (covers<N7w128>(s)) {
     o.fwd = &launch_stream_fwd<N7w128>;
     o.bwd = &launch_stream_bwd<N7w128>;
     o.bwd_ws = &stream_bwd_workspace<N7w128>;
+    o.fwd32 = &launch_stream_fwd_tf32<N7w128>;
   } else if (covers<N7w256>(s)) {
     o.fwd = &launch_stream_fwd<N7w256>;
     o.bwd = &launch_stream_bwd<N7w256>;
@@ -668,6 +711,7 @@ ShapeOps pick_ops(const mlpk_shape* s, bool training) {
     o.fwd = &launch_stream_fwd<N8w128>;
     o.bwd = &launch_stream_bwd<N8w128>;
     o.bwd_ws = &stream_bwd_workspace<N8w128>;
+    o.fwd32 = &launch_stream_fwd_tf32<N8w128>;
   } else if (covers<N8w256>(s)) {
     o.fwd = &launch_stream_fwd<N8w256>;
     o.bwd = &launch_stream_bwd<N8w256>;
@@ -709,6 +753,14 @@ int mlpk_shape_supported(const mlpk_shape* shape) {
   return pick_ops(shape, false).fwd != nullptr ? 1 : 0;
 }
 
+int mlpk_shape_supported_ex(const mlpk_shape* shape, int dtype) {
+  if (check_shape(shape) != MLPK_OK) return 0;
+  const ShapeOps o = pick_ops(shape, false);
+  if (dtype == MLPK_DT_F16) return o.fwd != nullptr ? 1 : 0;
+  if (dtype == MLPK_DT_F32) return o.fwd32 != nullptr ? 1 : 0;
+  return 0;
+}
+
 int mlpk_train_supported_ex(const mlpk_shape* shape, int h_dtype) {
   if (check_shape(shape) != MLPK_OK) return 0;
   if (h_dtype != MLPK_H_F16 && h_dtype != MLPK_H_F32) return 0;
@@ -742,6 +794,17 @@ int mlpk_fwd(const mlpk_shape* shape, int64_t M, const void* x, const void* cons
   Fwd f = pick_ops(shape, false).fwd;
   if (!f) return MLPK_ERR_UNSUPPORTED;
   return f(shape->dims, x, W, out, M, nullptr, false, static_cast<cudaStream_t>(stream));
+}
+
+int mlpk_fwd_ex(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W, void* out, int dtype,
+                mlpk_stream_t stream) {
+  if (dtype == MLPK_DT_F16) return mlpk_fwd(shape, M, x, W, out, stream);
+  if (dtype != MLPK_DT_F32) return MLPK_ERR_SHAPE;
+  int rc = check_fwd_args(shape, M, x, W, out);
+  if (rc) return rc;
+  const Fwd32 f = pick_ops(shape, false).fwd32;
+  if (!f) return MLPK_ERR_UNSUPPORTED;
+  return f(shape->dims, x, W, out, M, static_cast<cudaStream_t>(stream));
 }
 
 int mlpk_train_fwd_ex(const mlpk_shape* shape, int64_t M, const void* x, const void* const* W,

@@ -73,7 +73,11 @@ struct alignas(64) StreamMaps {
   int hact_cols[L > 1 ? L - 1 : 1];
 };
 
-template <class ChainT, int EPW>
+// TF32: fp32 input, weights and output, tf32 tensor-core GEMMs and fp32
+// hidden activations (the reference's INPUT_DTYPE fp32 design,
+// mlp_fused.md:159-166); inference forward only.  Every shared-memory row is
+// 128 bytes: 32 fp32 columns per chunk instead of 64 fp16 ones.
+template <class ChainT, int EPW, bool TF32 = false>
 struct StreamCfg {
   static constexpr int L = ChainT::L;
   static constexpr int D0 = ChainT::template D<0>();
@@ -82,9 +86,12 @@ struct StreamCfg {
   static constexpr int HMAX = ChainT::max_hidden_or_out();
   static constexpr int NG = EPW / 4;  // column groups
   static constexpr int NWBUF = 3;
-  static constexpr int WCH_BYTES = kStreamK * HMAX * 2;
-  static constexpr int X_BYTES = align_up(tile_bytes(kTileM, D0), 1024);
-  static constexpr int O_BYTES = align_up(tile_bytes(kTileM, DL), 1024);
+  static constexpr int ES = TF32 ? 4 : 2;   // element bytes
+  static constexpr int CB = 128 / ES;       // columns of one 128-byte chunk
+  static constexpr int KSTEP = TF32 ? 8 : 16;  // K of one UMMA
+  static constexpr int WCH_BYTES = kStreamK * HMAX * ES;
+  static constexpr int X_BYTES = align_up(kTileM * D0 * ES, 1024);
+  static constexpr int O_BYTES = align_up(kTileM * DL * ES, 1024);
   static constexpr int OFF_W = 0;
   static constexpr int OFF_X = NWBUF * WCH_BYTES;
   static constexpr int OFF_O = OFF_X + X_BYTES;
@@ -105,11 +112,11 @@ struct StreamCfg {
   static constexpr int THREADS = (2 + EPW) * 32;
   __host__ __device__ static constexpr bool dims_ok() {
     for (int i = 0; i <= L; ++i)
-      if (ChainT::dim(i) % 64 != 0 || ChainT::dim(i) > 256) return false;
+      if (ChainT::dim(i) % CB != 0 || ChainT::dim(i) > (TF32 ? 128 : 256)) return false;
     return true;
   }
   static_assert(EPW % 4 == 0, "epilogue warps come in groups of 4");
-  static_assert(dims_ok(), "streamed chain needs every width a multiple of 64, at most 256");
+  static_assert(dims_ok(), "streamed chain needs every width a multiple of 64 (fp32: 32), at most 256 (fp32: 128)");
   static_assert(ChainT::hidden_uniform(), "all hidden layers must have the same width");
   static_assert(H % CH_COLS == 0, "hidden width vs publish chunks");
   static_assert(TMEM_COLS_RAW <= 512, "accumulators exceed TMEM");
@@ -179,10 +186,62 @@ __device__ __forceinline__ void dgrad_job(uint32_t tbuf, int grp, uint32_t chunk
   }
 }
 
-template <class ChainT, int EPW, int MODE, bool SAVE>
-__global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
+// fp32 hidden-stage job (TF32 chain) of one warp: like hidden_job, but the
+// softplus result stays fp32 and goes back into the accumulator columns it
+// came from (one 32-bit TMEM column per element: the next stage's tf32 A).
+template <int N, int NG, int SPC>
+__device__ __forceinline__ void hidden_job_f32(uint32_t tbuf, int grp, uint32_t chunk_bar0) {
+  static_assert(N % (32 * NG) == 0, "hidden width must be a multiple of 32 * column groups");
+  constexpr int SUBS = N / (32 * NG);
+  static_assert(SUBS % SPC == 0, "stripes per chunk must divide the stripes per group");
+  uint32_t a[32];
+  tmem_ld_wait_x32(tbuf + 32 * grp, a);
+#pragma unroll
+  for (int j = 0; j < SUBS; ++j) {
+    const int col = 32 * (j * NG + grp);
+    uint32_t b[32];
+    if (j + 1 < SUBS) tmem_ld_async_x32(tbuf + col + 32 * NG, b);
+#pragma unroll
+    for (int p = 0; p < 16; ++p) {
+      const float2 z = softplus_x2(make_float2(__uint_as_float(a[2 * p]), __uint_as_float(a[2 * p + 1])));
+      a[2 * p] = __float_as_uint(z.x);
+      a[2 * p + 1] = __float_as_uint(z.y);
+    }
+    tmem_st_x32(tbuf + col, a);
+    if ((j + 1) % SPC == 0) publish_chunk(chunk_bar0 + 8 * (j / SPC));
+    if (j + 1 < SUBS) {
+      tmem_wait_ld_bind_x32(b);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) a[i] = b[i];
+    }
+  }
+}
+
+// fp32 output job (TF32 chain): NCOL accumulator columns -> the fp32 staging
+// tile (32-column chunks, 128-byte rows, 128B swizzle: the TMA-store layout).
+template <int NCOL>
+__device__ __forceinline__ void out_job_f32(uint32_t tbuf, uint32_t tile_base, uint32_t row, int col0) {
+  constexpr int CH = NCOL < 32 ? NCOL : 32;
+  static_assert(NCOL % CH == 0 && (CH == 16 || CH == 32), "unsupported width");
+#pragma unroll
+  for (int c = 0; c < NCOL; c += CH) {
+    uint32_t r[CH];
+    if constexpr (CH == 32) tmem_ld_wait_x32(tbuf + col0 + c, r);
+    else tmem_ld_wait_x16(tbuf + col0 + c, r);
+#pragma unroll
+    for (int u = 0; u < CH / 4; ++u) {
+      const int cc = col0 + c + 4 * u;
+      st_shared_v4(tile_base + (cc / 32) * (kTileM * 128) + swz_off<128>(row, (cc % 32) / 4), r[4 * u],
+                   r[4 * u + 1], r[4 * u + 2], r[4 * u + 3]);
+    }
+  }
+}
+
+template <class ChainT, int EPW, int MODE, bool SAVE, bool TF32 = false>
+__global__ void __launch_bounds__(StreamCfg<ChainT, EPW, TF32>::THREADS, 1)
     mlp_stream_kernel(const __grid_constant__ StreamMaps<ChainT::L> maps, int num_tiles) {
-  using Cfg = StreamCfg<ChainT, EPW>;
+  using Cfg = StreamCfg<ChainT, EPW, TF32>;
+  static_assert(!TF32 || (MODE == kStreamFwd && !SAVE), "the tf32 chain is the inference forward");
   constexpr int L = Cfg::L;
   constexpr int NWBUF = Cfg::NWBUF;
   extern __shared__ uint8_t smem_raw[];
@@ -252,10 +311,10 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(bar_x_full, kTileM * Cfg::D0 * 2);
+        mbar_arrive_expect_tx(bar_x_full, kTileM * Cfg::D0 * Cfg::ES);
 #pragma unroll
-        for (int c = 0; c < Cfg::D0 / 64; ++c)
-          tma_load_2d(s_x + c * kTileM * 128, &maps.in, bar_x_full, c * 64, t * kTileM);
+        for (int c = 0; c < Cfg::D0 / Cfg::CB; ++c)
+          tma_load_2d(s_x + c * kTileM * 128, &maps.in, bar_x_full, c * Cfg::CB, t * kTileM);
         ++xs;
         if constexpr (MODE == kStreamDgrad) {
           // the epilogue reads the saved activations with plain loads: bring
@@ -279,13 +338,13 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(bar_w_full(slot), kStreamK * N * 2);
+            mbar_arrive_expect_tx(bar_w_full(slot), kStreamK * N * Cfg::ES);
             const uint32_t dst = s_w + slot * Cfg::WCH_BYTES;
             if constexpr (MODE == kStreamFwd) {
-              // W_s rows [64kc, 64kc+64), all N columns: N/64 boxes {64, 64}
+              // W_s rows [64kc, 64kc+64), all N columns: N/CB boxes {CB, 64}
 #pragma unroll
-              for (int c = 0; c < N / 64; ++c)
-                tma_load_2d(dst + c * kStreamK * 128, &maps.w[s], bar_w_full(slot), c * 64, kc * kStreamK);
+              for (int c = 0; c < N / Cfg::CB; ++c)
+                tma_load_2d(dst + c * kStreamK * 128, &maps.w[s], bar_w_full(slot), c * Cfg::CB, kc * kStreamK);
             } else {
               // W_l^T chunk: columns [64kc, 64kc+64) of W_l, all N = d_l rows
               tma_load_2d(dst, &maps.w[s], bar_w_full(slot), kc * kStreamK, 0);
@@ -314,7 +373,8 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
         constexpr int s = decltype(sc)::value;
         constexpr int K = ChainT::template D<s>();
         constexpr int N = ChainT::template D<s + 1>();
-        constexpr uint32_t idesc = make_idesc_f16(kTileM, N, 0, MODE == kStreamFwd ? 1 : 0);
+        constexpr uint32_t idesc = TF32 ? make_idesc_tf32(kTileM, N, 0, 1)
+                                        : make_idesc_f16(kTileM, N, 0, MODE == kStreamFwd ? 1 : 0);
         if (!ok) return;
         const int g = i * L + s;
         const uint32_t d_tmem = tmem_base + (g & 1) * Cfg::SLOT_COLS;
@@ -341,19 +401,32 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
           if (issuer) {
             const uint32_t wb = s_w + slot * Cfg::WCH_BYTES;
 #pragma unroll
-            for (int kk = 0; kk < kStreamK / 16; ++kk) {
-              const int k = kc * (kStreamK / 16) + kk;
-              uint64_t bdesc;
-              if constexpr (MODE == kStreamFwd)
-                bdesc = mnmajor_base_desc<kStreamK, N>(wb) + (mnmajor_koff<N>(kk) >> 4);
-              else
-                bdesc = kmajor_base_desc<kStreamK>(wb) + ((kk * 32) >> 4);
+            for (int kk = 0; kk < kStreamK / Cfg::KSTEP; ++kk) {
+              const int k = kc * (kStreamK / Cfg::KSTEP) + kk;
               const uint32_t accum = (kc > 0 || kk > 0) ? 1u : 0u;
-              if constexpr (s == 0)
-                umma_f16(d_tmem, kmajor_base_desc<Cfg::D0>(s_x) + (kmajor_koff<kTileM, Cfg::D0>(k) >> 4),
-                         bdesc, idesc, accum);
-              else
-                umma_f16_ts(d_tmem, a_tmem + h_tmem_col(16 * k), bdesc, idesc, accum);
+              if constexpr (TF32) {
+                // fp32 rows are 128 bytes per 32-column chunk, i.e. the byte
+                // layout of an fp16 operand twice as wide; a tf32 K-step (8)
+                // is 32 bytes, as an fp16 one (16)
+                const uint64_t bdesc = mnmajor_base_desc<kStreamK, 2 * N>(wb) + ((kk * Cfg::KSTEP * 128) >> 4);
+                if constexpr (s == 0)
+                  umma_tf32(d_tmem,
+                            kmajor_base_desc<2 * Cfg::D0>(s_x) + (kmajor_koff<kTileM, 2 * Cfg::D0>(k) >> 4),
+                            bdesc, idesc, accum);
+                else
+                  umma_tf32_ts(d_tmem, a_tmem + Cfg::KSTEP * k, bdesc, idesc, accum);
+              } else {
+                uint64_t bdesc;
+                if constexpr (MODE == kStreamFwd)
+                  bdesc = mnmajor_base_desc<kStreamK, N>(wb) + (mnmajor_koff<N>(kk) >> 4);
+                else
+                  bdesc = kmajor_base_desc<kStreamK>(wb) + ((kk * 32) >> 4);
+                if constexpr (s == 0)
+                  umma_f16(d_tmem, kmajor_base_desc<Cfg::D0>(s_x) + (kmajor_koff<kTileM, Cfg::D0>(k) >> 4),
+                           bdesc, idesc, accum);
+                else
+                  umma_f16_ts(d_tmem, a_tmem + h_tmem_col(16 * k), bdesc, idesc, accum);
+              }
             }
             umma_commit(bar_w_empty(slot));
           }
@@ -425,7 +498,9 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
           if (!ok) break;
         }
         const uint32_t t_buf = t_lane + (g & 1) * Cfg::SLOT_COLS;
-        if constexpr (MODE == kStreamFwd)
+        if constexpr (TF32)
+          hidden_job_f32<H, NG, Cfg::SPC>(t_buf, grp, bar_chunk(0));
+        else if constexpr (MODE == kStreamFwd)
           hidden_job<H, NG, Cfg::SPC, SAVE ? 2 : 0>(t_buf, grp, bar_chunk(0), nullptr, s_o, row);
         else
           dgrad_job<H, NG, Cfg::SPC, SAVE>(t_buf, grp, bar_chunk(0), hv, hrow, hcols, s_o, row);
@@ -466,7 +541,10 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
           if (!ok) break;
         }
         const uint32_t t_buf = t_lane + (g & 1) * Cfg::SLOT_COLS;
-        out_job<Cfg::DL, NCOL_O>(t_buf, s_o, row, grp * NCOL_O);
+        if constexpr (TF32)
+          out_job_f32<NCOL_O>(t_buf, s_o, row, grp * NCOL_O);
+        else
+          out_job<Cfg::DL, NCOL_O>(t_buf, s_o, row, grp * NCOL_O);
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
@@ -475,8 +553,9 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW>::THREADS, 1)
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (leader && ok) {
 #pragma unroll
-          for (int c = 0; c < Cfg::DL / 64; ++c)
-            if (c * 64 < maps.out_cols) tma_store_2d(&maps.out, s_o + c * kTileM * 128, c * 64, t * kTileM);
+          for (int c = 0; c < Cfg::DL / Cfg::CB; ++c)
+            if (c * Cfg::CB < maps.out_cols)
+              tma_store_2d(&maps.out, s_o + c * kTileM * 128, c * Cfg::CB, t * kTileM);
           bulk_commit_group();
         }
       }

@@ -10,16 +10,15 @@ Mirrors the reference's functional surface:
 * ``ModelNew`` -- the nn.Module shim of kernel.py:174-180.
 
 Every call runs the sm_100a kernel in libmlpk through its C ABI on the current
-CUDA stream.  x and the weights are fp16, or fp32: the reference's launcher
-selects fp32 tile configurations (kernel.py:37-43, 138), though its kernel
-fails on fp32 operands at the second GEMM (it casts h1 to fp16 and dots it
-with the fp32 W2: "Both operands must be same dtype", kernel.py:110).  Here
-fp32 operands are rounded to fp16 by the library's cast kernel, the fused
-fp16 kernel runs, and its fp16-rounded result is widened into the fp32
-output -- the reference's rounding points for the hidden activations
-(kernel.py:110, 117) and the output (kernel.py:121-124).  fp16 keeps tf32's
-10 mantissa bits but not fp32's exponent range: magnitudes above 65,504
-become infinite and below 6.1e-5 lose precision.
+CUDA stream.  x and the weights are fp16, or fp32.  fp32 operands run the
+reference's fp32 design (INPUT_DTYPE fp32 throughout, mlp_fused.md:159-166):
+every GEMM on tf32 tensor cores with fp32 accumulation, the hidden
+activations fp32, an fp32 output -- for networks up to 128 wide; wider ones
+are rounded to fp16 by the library's cast kernel around the fp16 kernel (the
+inference kernel's rounding points, kernel.py:110, 117, 121-124).  The
+reference's own kernel.py selects fp32 tile configurations (kernel.py:37-43,
+138) but fails on fp32 operands at the second GEMM (it dots the fp16-cast h1
+with the fp32 W2: "Both operands must be same dtype").
 There is no CPU or PyTorch fallback: CPU tensors, other dtypes or unsupported
 shapes raise.
 """

@@ -7,7 +7,9 @@ FakeTensor / meta tracing and CUDA-graph capture see an ordinary operator
 instead of an opaque Python call.  Operators:
 
 * ``mlpk::fwd(x, weights) -> out`` -- the inference forward (kernel.py:130-156),
-  fp16 or fp32 operands (fp32 is cast to fp16 around the fp16 kernel);
+  fp16 operands, or fp32 ones on tf32 tensor cores with fp32 activations
+  (networks up to 128 wide; wider ones are cast to fp16 around the fp16
+  kernel);
 * ``mlpk::fwd_out(x, weights, out) -> ()`` -- the same into a caller buffer;
 * ``mlpk::train_fwd(x, weights, h_fp32) -> [out, h_1, .., h_{L-1}]`` --
   the training forward, saved activations in fp32 or fp16;
@@ -75,9 +77,15 @@ def _forward_into(x: Tensor, weights, out: Tensor) -> None:
         stream = _stream(x.device)
         x = _aligned(x)
         ws = [_aligned(w) for w in weights]
+        if x.dtype == torch.float32 and lib.mlpk_shape_supported_ex(ctypes.byref(shape), _lib.DT_F32):
+            # fp32 operands on tf32 tensor cores, fp32 hidden activations
+            # (the reference's INPUT_DTYPE fp32 design, mlp_fused.md:159-166)
+            _lib.check("mlpk_fwd_ex", lib.mlpk_fwd_ex(ctypes.byref(shape), M, x.data_ptr(), _ptrs(ws),
+                                                      out.data_ptr(), _lib.DT_F32, stream))
+            return
         if x.dtype == torch.float32:
-            # the reference's fp32 path (kernel.py:37-43): operands rounded to
-            # fp16 by the library's cast kernel, the fp16 result widened
+            # networks wider than the tf32 kernels (256 wide): operands rounded
+            # to fp16 by the library's cast kernel, the fp16 result widened
             if not lib.mlpk_shape_supported(ctypes.byref(shape)):
                 _lib.check("mlpk_fwd", 2)
             x16 = _cast(lib, x, torch.float16, stream)

@@ -5,6 +5,8 @@ Tolerance (from the task's north star): max|out - ref| <= 1e-2 * max|ref|.
 The kernel is also held to a tighter implementation bar (3e-3) because it
 computes the same fp16-operand / fp32-accumulate chain as the reference.
 """
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -254,3 +256,53 @@ def test_fwd_host_rows_errors():
     with pytest.raises(ValueError):
         fused_mlp_fwd_host(x, *ws)          # CPU weights
     assert fused_mlp_fwd_host(x[:0], *wg).shape == (0, 128)
+
+
+# ---------------------------------------------------------------- fp32 on tf32 tensor cores
+TF32_TOL = 1e-2  # tf32 operands: 10 mantissa bits per GEMM input
+
+
+def _f64_forward(x, ws):
+    """The reference formula (kernel.py:163-171) in float64, no fp16 rounding."""
+    return oracle.mlp_forward(x, ws, round_h=False, round_out=False)
+
+
+@pytest.mark.parametrize("dims", [(128, 128, 128, 128), (32, 64, 64, 64, 64, 16), (64, 64, 64, 64),
+                                  (48, 128, 80, 24), (128, 128, 128, 128, 128, 128)])
+@pytest.mark.parametrize("M", [1, 300, 148 * 128 + 77])
+def test_fp32_forward_on_tf32_cores(dims, M):
+    """fp32 x and W: the tf32 chain (fp32 hidden activations, fp32 output)
+    against the formula in float64."""
+    assert _lib.lib().mlpk_shape_supported_ex(ctypes.byref(_lib.shape_struct(dims)), _lib.DT_F32)
+    x = make_x(M, dims[0], "normal", 5, dtype=torch.float32)
+    ws = make_weights(dims, seed=6, dtype=torch.float32)
+    out = fused_mlp_fwd(x.cuda(), *[w.cuda() for w in ws])
+    assert out.dtype == torch.float32
+    ref = _f64_forward(x.numpy(), [w.numpy() for w in ws])
+    assert _rel_max(out.cpu().numpy(), ref) <= TF32_TOL
+
+
+def test_fp32_forward_keeps_fp32_range():
+    """Inputs far beyond fp16's range (|x| ~ 1e6, weights ~ 1e-6 and 1e5):
+    fp16 operands would overflow or flush; the tf32 chain keeps fp32's
+    exponent range."""
+    dims = (128, 128, 128, 128)
+    M = 4096
+    x = make_x(M, 128, "normal", 7, dtype=torch.float32) * 1e6
+    ws = make_weights(dims, seed=8, dtype=torch.float32)
+    ws = [ws[0] * 1e-6, ws[1] * 1e5, ws[2] * 1e-5]
+    out = fused_mlp_fwd(x.cuda(), *[w.cuda() for w in ws])
+    assert torch.isfinite(out).all()
+    ref = _f64_forward(x.numpy(), [w.numpy() for w in ws])
+    assert _rel_max(out.cpu().numpy(), ref) <= TF32_TOL
+
+
+def test_fp32_forward_wide_network_uses_fp16_operands():
+    """256-wide networks have no tf32 kernel: fp32 operands are rounded to
+    fp16 around the fp16 kernel (the inference kernel's rounding points)."""
+    dims = (256, 256, 256, 256)
+    assert not _lib.lib().mlpk_shape_supported_ex(ctypes.byref(_lib.shape_struct(dims)), _lib.DT_F32)
+    x, ws = make_inputs("W256", 500)
+    out = fused_mlp_fwd(x.float().cuda(), *[w.float().cuda() for w in ws])
+    ref = oracle.mlp_forward(x.numpy(), [w.numpy() for w in ws])
+    assert out.dtype == torch.float32 and _rel_max(out.cpu().numpy(), ref) <= TIGHT
