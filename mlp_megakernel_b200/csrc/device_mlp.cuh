@@ -12,13 +12,13 @@
 // Usage, inside a kernel launched with at least 128 threads per CTA and
 // SMEM_BYTES of dynamic shared memory:
 //
-//   using MLP = mlpk::device::FusedMLP<32, 64, 64, 16>;   // widths d0 .. dL
+//   using MLP = mlpk::device::FusedMLP<64, 64, 64, 16>;   // widths d0 .. dL
 //   extern __shared__ uint8_t smem[];
 //   MLP mlp;
 //   mlp.init(smem, weights);             // every thread of the CTA; W_l [d_l][d_{l+1}] fp16, global
 //   for (each group of 128 rows) {
 //     if (threadIdx.x < 128) {           // one row per thread of the first warpgroup
-//       float x[32] = ...;               // the caller's encoding of its row
+//       float x[64] = ...;               // the caller's encoding of its row
 //       float y[16];
 //       bool ok = mlp.forward(x, row_valid, y);
 //       ...                              // the caller's use of y
@@ -30,8 +30,9 @@
 // TMEM lanes 32w..32w+31, i.e. rows 32w..32w+31 of the tile); it uses named
 // barrier 15 among them and returns false if one of its bounded waits on the
 // tensor core expired (the outputs are then zeros).  Constraints: every
-// width a multiple of 16 and at most 256, hidden widths multiples of 32,
-// the weights and one 128-row input tile in shared memory (SMEM_BYTES).
+// width 16, 32 or a multiple of 64 and at most 256 (pad a narrower encoding
+// with zero columns), hidden widths 32 or multiples of 64, the weights and one
+// 128-row input tile in shared memory (SMEM_BYTES).
 #pragma once
 #include "fwd_kernel.cuh"
 
@@ -58,15 +59,19 @@ class FusedMLP {
                                    : 2 * SLOT <= 256 ? 256 : 512;
   static constexpr int THREADS = 128;
 
+  // every operand row must be a swizzle-layout pitch: 16, 32 or a multiple
+  // of 64 fp16 columns (32, 64 or 128-byte chunks)
   __host__ __device__ static constexpr bool dims_ok() {
-    for (int i = 0; i <= L; ++i)
-      if (NetT::dim(i) % 16 != 0 || NetT::dim(i) > 256 || NetT::dim(i) < 16) return false;
+    for (int i = 0; i <= L; ++i) {
+      const int d = NetT::dim(i);
+      if (!(d == 16 || d == 32 || d % 64 == 0) || d > 256) return false;
+    }
     for (int i = 1; i < L; ++i)
       if (NetT::dim(i) % 32 != 0) return false;
     return true;
   }
   static_assert(L >= 1, "at least one layer");
-  static_assert(dims_ok(), "widths: multiples of 16 (hidden: of 32), 16 .. 256");
+  static_assert(dims_ok(), "widths: 16, 32 or multiples of 64, at most 256 (hidden: 32 or multiples of 64)");
   static_assert(SMEM_BYTES <= 232448, "weights and input tile exceed shared memory");
 
   // Copies the weights into shared memory (UMMA layout), allocates TMEM and

@@ -10,10 +10,10 @@
 
 namespace {
 
-constexpr int kFreqs = 5;                 // 3 coords x (1 + 2 x 5) = 33 -> padded to 48 features
-constexpr int kEnc = 48;
-using SmallMLP = mlpk::device::FusedMLP<48, 64, 64, 16>;
-using WideMLP = mlpk::device::FusedMLP<48, 128, 128, 128, 32>;
+constexpr int kFreqs = 5;                 // 3 coords x (1 + 2 x 5) = 33 -> padded to 64 features
+constexpr int kEnc = 64;
+using SmallMLP = mlpk::device::FusedMLP<64, 64, 64, 16>;
+using WideMLP = mlpk::device::FusedMLP<64, 128, 128, 128, 32>;
 
 template <class MLP>
 __global__ void __launch_bounds__(128, 1)
@@ -75,7 +75,7 @@ int run(const float* pts, int M, const void* const* W, float* out, float* loss, 
 
 // pts [M, 3] fp32; W: device array of device pointers to W_l fp16 [d_l][d_{l+1}];
 // out [M, dL] fp32; loss [M] fp32; failed: device int set to 1 on a wait
-// timeout.  net 0: 48-64-64-16, net 1: 48-128-128-128-32.  Returns a
+// timeout.  net 0: 64-64-64-16, net 1: 64-128-128-128-32.  Returns a
 // cudaError_t value.
 extern "C" int mlpk_devtest_encode_mlp_loss(int net, const float* pts, int M, const void* const* W_dev,
                                             float* out, float* loss, int* failed, int grid, void* stream) {

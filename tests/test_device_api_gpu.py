@@ -15,7 +15,7 @@ import torch
 
 import oracle
 
-NETS = {0: (48, 64, 64, 16), 1: (48, 128, 128, 128, 32)}
+NETS = {0: (64, 64, 64, 16), 1: (64, 128, 128, 128, 32)}
 FREQS = 5
 
 
@@ -38,9 +38,9 @@ def test_devtest_library_builds_and_exports(devlib):
 
 def _encode(pts: np.ndarray) -> np.ndarray:
     """The kernel's frequency encoding in float64: [p, sin(2^k p), cos(2^k p)]
-    per coordinate, zero-padded to 48 features."""
+    per coordinate, zero-padded to 64 features."""
     M = pts.shape[0]
-    x = np.zeros((M, 48))
+    x = np.zeros((M, 64))
     x[:, :3] = pts
     for k in range(FREQS):
         f = 2.0 ** k
