@@ -89,6 +89,17 @@ __device__ __forceinline__ uint64_t mnmajor_base_desc(uint32_t base) {
                     umma_layout_code(pitch_bytes(NEXT)));
 }
 
+// MN-major tf32 operand [K rows][N cols] (fp32, N contiguous) stored as
+// chunks of 32 columns x KROWS rows (128-byte rows).  For 32-bit MN-major
+// operands the tensor core takes one swizzle only: 128 bytes with 32-byte
+// atoms (layout code 1), where 32-byte granule g of row r sits at g ^ (r % 4)
+// -- what a TMA load with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B writes.  A K
+// group is 4 rows (SBO 512 B); chunks follow each other (LBO).
+template <int KROWS>
+__device__ __forceinline__ uint64_t mnmajor_tf32_base_desc(uint32_t base) {
+  return make_sdesc(base, KROWS * 128, 4 * 128, 1u);
+}
+
 // Descriptor for K-step `k` (16 elements of K) of a K-major operand with
 // `rows` rows and K extent `kext`, stored as chunks (see above).
 template <int ROWS, int KEXT>

@@ -115,15 +115,18 @@ EncodeFn get_encode() {
 
 // 2-D tensor [outer][inner] (inner contiguous) of fp16 (elem_bytes 2) or fp32
 // (elem_bytes 4), box {box_inner, box_outer}, swizzle chosen from the box's
-// row pitch (box_inner * elem_bytes).
+// row pitch (box_inner * elem_bytes); atom32: 128-byte rows swizzled in
+// 32-byte granules (the MN-major tf32 operand layout, layout.cuh).
 int make_map_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer,
-                uint32_t box_inner, uint32_t box_outer, uint32_t elem_bytes = 2) {
+                uint32_t box_inner, uint32_t box_outer, uint32_t elem_bytes = 2, bool atom32 = false) {
   EncodeFn enc = get_encode();
   if (!enc) return driver_status("cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)", -1);
   const uint32_t pitch = box_inner * elem_bytes;
-  CUtensorMapSwizzle swz = pitch == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
-                           : pitch == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                         : CU_TENSOR_MAP_SWIZZLE_32B;
+  if (atom32 && pitch != 128) return MLPK_ERR_SHAPE;
+  CUtensorMapSwizzle swz = atom32         ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                           : pitch == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                           : pitch == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
+                                          : CU_TENSOR_MAP_SWIZZLE_32B;
   cuuint64_t gdim[2] = {inner, outer};
   cuuint64_t gstride[1] = {inner * elem_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
@@ -426,8 +429,8 @@ int launch_stream_fwd_tf32(const int* rd, const void* x, const void* const* W, v
   std::memset(&maps, 0, sizeof(maps));
   if ((rc = make_map_2d(&maps.in, x, rd[0], M, 32, mlpk::kTileM, 4))) return rc;
   if ((rc = make_map_2d(&maps.out, out, rd[L], M, 32, mlpk::kTileM, 4))) return rc;
-  for (int l = 0; l < L; ++l)  // K-chunks of 64 rows, boxes {32 columns, 64 rows}
-    if ((rc = make_map_2d(&maps.w[l], W[l], rd[l + 1], rd[l], 32, mlpk::kStreamK, 4))) return rc;
+  for (int l = 0; l < L; ++l)  // K-chunks of 64 rows, boxes {32 columns, 64 rows}, 32-byte atoms
+    if ((rc = make_map_2d(&maps.w[l], W[l], rd[l + 1], rd[l], 32, mlpk::kStreamK, 4, true))) return rc;
   maps.M = static_cast<int>(M);
   maps.out_cols = rd[L];
   const int64_t tiles = (M + mlpk::kTileM - 1) / mlpk::kTileM;

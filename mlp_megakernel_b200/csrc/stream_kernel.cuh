@@ -405,10 +405,9 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW, TF32>::THREADS, 1)
               const int k = kc * (kStreamK / Cfg::KSTEP) + kk;
               const uint32_t accum = (kc > 0 || kk > 0) ? 1u : 0u;
               if constexpr (TF32) {
-                // fp32 rows are 128 bytes per 32-column chunk, i.e. the byte
-                // layout of an fp16 operand twice as wide; a tf32 K-step (8)
-                // is 32 bytes, as an fp16 one (16)
-                const uint64_t bdesc = mnmajor_base_desc<kStreamK, 2 * N>(wb) + ((kk * Cfg::KSTEP * 128) >> 4);
+                // W chunks in the 32-byte-atom swizzle (the one MN-major
+                // tf32 layout); a K-step is 8 rows of 128 bytes
+                const uint64_t bdesc = mnmajor_tf32_base_desc<kStreamK>(wb) + ((kk * Cfg::KSTEP * 128) >> 4);
                 if constexpr (s == 0)
                   umma_tf32(d_tmem,
                             kmajor_base_desc<2 * Cfg::D0>(s_x) + (kmajor_koff<kTileM, 2 * Cfg::D0>(k) >> 4),

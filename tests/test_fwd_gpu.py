@@ -21,6 +21,7 @@ pytestmark = pytest.mark.gpu
 
 TOL = 1e-2      # north-star parity tolerance, relative to max|ref|
 TIGHT = 3e-3    # implementation bar
+TF32_TOL = 1e-2  # tf32 operands: 10 mantissa bits per GEMM input
 
 
 def _rel_max(got, ref):
@@ -202,17 +203,18 @@ def test_fwd_errors_are_loud():
 @pytest.mark.parametrize("config,M", [("3L128", 4096), ("3L128", 300), ("5L", 5000)])
 def test_fwd_fp32_inputs(config, M):
     """fp32 x and W (the reference accepts them, kernel.py:134-138): the result
-    is fp32, equals the fp16 path on the fp16-rounded operands exactly, and
-    matches the oracle on the fp32 operands."""
+    is fp32 from the tf32 chain (fp32 hidden activations), within tf32's
+    tolerance of the formula in float64 on the fp32 operands and of the fp16
+    path on the fp16-rounded operands; the out= form gives the same bits."""
     x, ws = make_inputs(config, M)
     x32 = (x.float() + 1e-4 * torch.randn(x.shape, generator=torch.Generator().manual_seed(3))).cuda()
     w32 = [(w.float() * 1.0003).cuda() for w in ws]
     out = fused_mlp_fwd(x32, *w32)
     assert out.dtype == torch.float32 and out.shape == (M, ws[-1].shape[1])
+    ref = _f64_forward(x32.cpu().numpy(), [w.cpu().numpy() for w in w32])
+    assert _rel_max(out.cpu().numpy(), ref) <= TF32_TOL
     ref16 = fused_mlp_fwd(x32.half(), *[w.half() for w in w32]).float()
-    assert torch.equal(out, ref16)
-    ref = oracle.mlp_forward(x32.cpu().numpy(), [w.cpu().numpy() for w in w32])
-    assert _rel_max(out.cpu().numpy(), ref) <= TIGHT
+    assert _rel_max(out.cpu().numpy(), ref16.cpu().numpy()) <= TF32_TOL
     buf = torch.empty_like(out)
     assert fused_mlp_fwd(x32, *w32, out=buf) is buf and torch.equal(buf, out)
 
@@ -259,7 +261,6 @@ def test_fwd_host_rows_errors():
 
 
 # ---------------------------------------------------------------- fp32 on tf32 tensor cores
-TF32_TOL = 1e-2  # tf32 operands: 10 mantissa bits per GEMM input
 
 
 def _f64_forward(x, ws):
