@@ -135,15 +135,16 @@ struct BwdCfg {
   // other slot's MMAs.
   // Tiles in flight and dz tiles per tile slot: two tiles where TMEM holds a
   // second dgrad accumulator and the ring keeps one tile's loads plus the
-  // first two of the next; two dz tiles per slot (the epilogue writes dz_l
-  // while the MMAs still read dz_{l+1}) where the ring keeps that depth with
-  // them (with one tile in flight: a ring of 4).  fp32 saved activations:
-  // one tile, no dz tile (dz lives in h's high half-slot).
+  // first two of the next.  With one tile in flight, two dz tiles (the
+  // epilogue writes dz_l while the MMAs still read dz_{l+1}) where the ring
+  // keeps 4 slots beside them (3L128 backward 97.2 -> 95.8 us at 262,144
+  // rows); with two tiles in flight the other tile's step already covers that
+  // wait, and a second dz tile per slot measured slower (5-layer 227.8 ->
+  // 229.4 us at 1M rows).  fp32 saved activations: one tile, no dz tile (dz
+  // lives in h's high half-slot).
   static constexpr bool TMEM2 = dw_col(L) + 2 * ACC_W <= 512;
   static constexpr int NS = (!H32 && TMEM2 && ring_cap(ring_fit_g(2, 1)) >= L + 3) ? 2 : 1;
-  static constexpr int G_TILES = H32 ? 0
-                                 : (NS == 2 ? (ring_cap(ring_fit_g(2, 2)) >= L + 3 ? 2 : 1)
-                                            : (ring_cap(ring_fit_g(1, 2)) >= 4 ? 2 : 1));
+  static constexpr int G_TILES = H32 ? 0 : (NS == 2 ? 1 : (ring_cap(ring_fit_g(1, 2)) >= 4 ? 2 : 1));
   __host__ __device__ static constexpr int ring_fit(int ns) { return ring_fit_g(ns, G_TILES); }
   // loads per tile: g, then h_{L-1} .. h_1 (one slot each, or two fp32 halves
   // each), then x
@@ -460,14 +461,18 @@ __global__ void __launch_bounds__(BwdCfg<NetT, H32>::THREADS, 1)
       constexpr int PA = pitch_bytes(MW);
       const uint64_t bw0 = mnmajor_base_desc<kTileM, NW>(b_base);
       const uint32_t dw = tmem_base + Cfg::dw_col(l);
+      // a 64-wide A: its second 64-column chunk (LBO) is the 16 zero rows, the
+      // same for every K-step, so K-step k moves the start address up by
+      // koff and the LBO down by as much: one 64-bit add of a constant per
+      // K-step (no borrow: the zero rows lie past the ring and G, at least a
+      // tile beyond a_base, and koff < a tile)
+      const uint32_t lbo0 = (MW < 128) ? (s_zero - a_base) : kTileM * PA;
+      const uint64_t aw0 = make_sdesc(a_base, lbo0, 8 * PA, umma_layout_code(PA));
 #pragma unroll
       for (int k = 0; k < kTileM / 16; ++k) {
-        // a 64-wide A: its second 64-column chunk (LBO) is the 16 zero rows,
-        // the same for every K-step
-        const uint32_t a_k = a_base + mnmajor_koff<MW>(k);
-        const uint32_t lbo = (MW < 128) ? (s_zero - a_k) : kTileM * PA;
-        umma_f16(dw, make_sdesc(a_k, lbo, 8 * PA, umma_layout_code(PA)), bw0 + (mnmajor_koff<NW>(k) >> 4),
-                 idesc_w, (i > 0 || k > 0) ? 1u : 0u);
+        const uint64_t ko = mnmajor_koff<MW>(k) >> 4;
+        const uint64_t astep = (MW < 128) ? ko - (ko << 16) : ko;
+        umma_f16(dw, aw0 + astep, bw0 + (mnmajor_koff<NW>(k) >> 4), idesc_w, (i > 0 || k > 0) ? 1u : 0u);
       }
     };
     bool ok = __all_sync(0xffffffffu, mbar_wait(bar_w_full, 0, abort_flag, kDevTimeoutMma));
