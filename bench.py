@@ -24,6 +24,7 @@ summed over the ranks by the library's NVLink peer-memory kernel when N > 1):
 ``fwd_bwd`` (3L128 with weight norm and fp32 activation
 storage, 262,144 rows per GPU), ``fwd_bwd_h16`` (the same saving fp16
 activations, with its gradients' difference from the fp32-storage step),
+``fwd_bwd_small`` (config 3's small-batch regime: 16,384 rows per GPU),
 ``fwd_bwd_5l`` (config 4: 5-layer with weight norm, 1,048,576 rows in total,
 strong scaling), ``fwd_bwd_5l_weak`` (N > 1 only: the same with 1,048,576 rows
 per GPU) and ``fwd_bwd_w256`` (config 5: D = H = OUT = 256, 1,048,576 rows in
@@ -54,6 +55,7 @@ FLOP_PER_ROW = 2 * sum(a * b for a, b in zip(DIMS[:-1], DIMS[1:]))
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 FWD_KERNEL = "mlp_fwd_kernel"
 TRAIN_ROWS = 262144                                           # BASELINE config 3 (split-K regime)
+TRAIN_SMALL_ROWS = 16384                                      # BASELINE config 3 (small-batch regime)
 TRAIN5_ROWS = 1024 * 1024                                     # BASELINE config 4 (global)
 TRAIN256_ROWS = 1024 * 1024                                   # BASELINE config 5 (global)
 
@@ -512,7 +514,7 @@ def run_mlpk(args):
     if world == 1 and not args.no_sweep:
         sweep = run_sweep(x, ws, load_peaks())
 
-    train = train16 = train5 = train256 = train5w = None
+    train = train16 = train_small = train5 = train256 = train5w = None
     if not args.no_train:
         from mlp_megakernel_b200.dp import shard_rows
 
@@ -524,6 +526,9 @@ def run_mlpk(args):
         train16["grad_diff_vs_fp32_storage"] = {
             name: float((a16.double() - a32.double()).norm() / a32.double().norm().clamp_min(1e-30))
             for name, a32, a16 in zip(("dx", "dv", "dg"), g32, g16)}
+        # BASELINE config 3's small-batch regime (M = 16,384 per GPU)
+        train_small = run_training(args, world, rank, dist, barrier, "3L128", TRAIN_SMALL_ROWS)
+        train_small.pop("_grads")
         a, b = shard_rows(args.train5_rows, rank, world)
         train5 = run_training(args, world, rank, dist, barrier, "5L", b - a)
         a, b = shard_rows(args.train256_rows, rank, world)
@@ -596,6 +601,8 @@ def run_mlpk(args):
         line["fwd_bwd"] = train
     if train16 is not None:
         line["fwd_bwd_h16"] = train16
+    if train_small is not None:
+        line["fwd_bwd_small"] = train_small
     if train5 is not None:
         line["fwd_bwd_5l"] = train5
     if train256 is not None:
@@ -637,7 +644,7 @@ TRAIN_SPECS = {
                   "workload": "BASELINE config 3 shape with fp16 activation storage (not the config as "
                               "written): 3L D=H=OUT=128 training step with weight norm, M={M} rows per GPU"},
     # 5L 32-64-64-64-64-16 with weight norm, global M = 1,048,576
-    # split over the ranks (strong scaling, NCCL all-reduce of dW)
+    # split over the ranks (strong scaling, dW summed over the ranks)
     "5L": {"dims": (32, 64, 64, 64, 64, 16), "x_dist": "uniform", "x_seed": 3, "strong": True,
            "metric": "fused MLP fwd+bwd rows/s (5L 32-64-64-64-64-16 with weight norm)",
            "workload": "BASELINE config 4: 5L D=32 H=64 OUT=16 training step with weight norm, "
@@ -685,8 +692,9 @@ def step_traffic(name: str, rows: int):
 def run_training(args, world, rank, dist, barrier, name, rows):
     """One training step with weight norm per GPU through the C ABI on
     preallocated buffers: weight-norm forward, training forward, fused backward
-    + fixed-order dW reduction, (N > 1: NCCL all-reduce of dW), weight-norm
-    backward.  `rows` is the per-GPU batch."""
+    + fixed-order dW reduction, (N > 1: dW summed over the ranks by the
+    library's NVLink peer-memory kernel), weight-norm backward.  `rows` is the
+    per-GPU batch."""
     import ctypes
 
     import torch
@@ -825,7 +833,10 @@ def run_training(args, world, rank, dist, barrier, name, rows):
     if red is not None:
         red.close()
     peaks = load_peaks()
-    traffic, traffic_src = step_traffic(name, M)
+    l2_resident = M * dims[1] * 2 * (len(dims) - 2) <= 126e6
+    traffic, traffic_src = (step_traffic(name, M) if not l2_resident else
+                            (None, "not scaled: the step's working set stays in L2, so the DRAM bytes "
+                                   "of the full-size captures do not carry over"))
     per_step = ms / 1e3 / args.train_steps
     tflops = flop_per_row * M / per_step / 1e12
     gbs = bytes_per_row * M / per_step / 1e9
@@ -846,8 +857,7 @@ def run_training(args, world, rank, dist, barrier, name, rows):
                    "parallelism": f"dp{world}" + ((" (fp32 dW summed by the NVLink peer-memory kernel)" if peer
                                                    else " (NCCL all-reduce of fp32 dW)") if world > 1 else ""),
                    "launch": "eager" if args.no_graph else "CUDA graph of the whole step",
-                   "l2": "per-step inputs and saved activations larger than L2"
-                         if M * dims[1] * 2 * (len(dims) - 2) > 126e6 else
+                   "l2": "per-step inputs and saved activations larger than L2" if not l2_resident else
                          "working set partly L2-resident (no flush between steps)"},
         "roofline": {"bound": "tensor" if tensor_rows <= hbm_rows else "hbm",
                      "achieved": tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",

@@ -136,12 +136,13 @@ struct BwdCfg {
   // Tiles in flight and dz tiles per tile slot: two tiles where TMEM holds a
   // second dgrad accumulator and the ring keeps one tile's loads plus the
   // first two of the next.  With one tile in flight, two dz tiles (the
-  // epilogue writes dz_l while the MMAs still read dz_{l+1}) where the ring
-  // keeps 4 slots beside them (3L128 backward 97.2 -> 95.8 us at 262,144
-  // rows); with two tiles in flight the other tile's step already covers that
-  // wait, and a second dz tile per slot measured slower (5-layer 227.8 ->
-  // 229.4 us at 1M rows).  fp32 saved activations: one tile, no dz tile (dz
-  // lives in h's high half-slot).
+  // epilogue writes dz_l while the MMAs still read dz_{l+1}, no wait for the
+  // weight gradient) where the ring keeps 4 slots beside them (the 6- and
+  // 7-layer 64-wide networks; 3L128 and the 2-layer 128-wide network have
+  // room for one); with two tiles in flight the other tile's step already
+  // covers that wait, and a second dz tile per slot measured slower (5-layer
+  // backward 227.8 vs 229.4 us at 1M rows).  fp32 saved activations: one
+  // tile, no dz tile (dz lives in h's high half-slot).
   static constexpr bool TMEM2 = dw_col(L) + 2 * ACC_W <= 512;
   static constexpr int NS = (!H32 && TMEM2 && ring_cap(ring_fit_g(2, 1)) >= L + 3) ? 2 : 1;
   static constexpr int G_TILES = H32 ? 0 : (NS == 2 ? 1 : (ring_cap(ring_fit_g(1, 2)) >= 4 ? 2 : 1));
