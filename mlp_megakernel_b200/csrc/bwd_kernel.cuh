@@ -112,15 +112,18 @@ struct BwdCfg {
   // zero rows that pad a 64-wide weight-gradient M to 128: one UMMA reads 16
   // K-rows of it, and every K-step's descriptor points at the same 16 rows
   static constexpr int ZERO_BYTES = any_pad() ? 2048 : 0;  // 16 rows x 128 B
+  // deepest load ring (5-layer backward at 1M rows: 227.5 us with 8 slots,
+  // 224 us with the 10 that fit)
+  static constexpr int kMaxRing = 12;
   // ring slots that fit in shared memory next to the weights, `ns` x `ng` dz
-  // tiles (G), the zero rows and the barriers: w_full, slot_full[8],
-  // slot_empty[8], then per tile slot acc_full, acc_free, wg_done, dz_full,
+  // tiles (G), the zero rows and the barriers: w_full, slot_full[kMaxRing],
+  // slot_empty[kMaxRing], then per tile slot acc_full, acc_free, wg_done, dz_full,
   // out_ready; mma_done; rd_done
   __host__ __device__ static constexpr int ring_fit_g(int ns, int ng) {
-    return (232448 - 1024 - 16 - 8 * (3 + 2 * 8 + 5 * ns) - (W_TOTAL + ns * ng * TILE_BYTES) - ZERO_BYTES) /
+    return (232448 - 1024 - 16 - 8 * (3 + 2 * kMaxRing + 5 * ns) - (W_TOTAL + ns * ng * TILE_BYTES) - ZERO_BYTES) /
            TILE_BYTES;
   }
-  __host__ __device__ static constexpr int ring_cap(int r) { return r > 8 ? 8 : r; }
+  __host__ __device__ static constexpr int ring_cap(int r) { return r > kMaxRing ? kMaxRing : r; }
   // every hidden width splits into two fp32 halves of whole 32-column chunks,
   // each fitting a ring slot
   __host__ __device__ static constexpr bool h32_ok() {
@@ -164,7 +167,7 @@ struct BwdCfg {
   static constexpr int OFF_G = W_TOTAL;  // G b of slot s at OFF_G + (s * G_TILES + b) * TILE_BYTES
   static constexpr int OFF_RING = OFF_G + NS * G_TILES * TILE_BYTES;
   static constexpr int RING_FIT = ring_fit(NS);
-  static constexpr int RING = RING_FIT > 8 ? 8 : RING_FIT;
+  static constexpr int RING = RING_FIT > kMaxRing ? kMaxRing : RING_FIT;
   static constexpr int OFF_ZERO = OFF_RING + RING * TILE_BYTES;
   static constexpr int OFF_BAR = OFF_ZERO + ZERO_BYTES;
   static constexpr int NUM_BARS = 2 + 2 * RING + 5 * NS + 1;

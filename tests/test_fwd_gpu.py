@@ -85,6 +85,21 @@ def test_fwd_multi_round_batches(M):
     assert _rel_max(out.cpu().numpy()[rows], ref) <= TIGHT
 
 
+@pytest.mark.parametrize("dims", [(128, 128, 128), (96, 128, 80, 40), (64, 128, 128, 16), (32, 128, 128, 128)])
+def test_fwd_throughput_config_networks(dims):
+    """Inference batches of more than one row tile per SM (the throughput
+    configuration) on networks served with 128-wide hidden layers: the 2-layer
+    network and narrower widths by zero fill, against the oracle, ragged last
+    tile included."""
+    M = 148 * 128 * 2 + 77
+    x = make_x(M, dims[0], "normal", 11)
+    ws = make_weights(dims, seed=12)
+    out = fused_mlp_fwd(x.cuda(), *_gpu(ws)).cpu().numpy()
+    ref = oracle.mlp_forward(x.numpy(), [w.numpy() for w in ws])
+    assert out.shape == (M, dims[-1])
+    assert _rel_max(out, ref) <= TIGHT
+
+
 def test_fwd_empty_batch():
     x, ws = make_inputs("3L128", 0)
     out = fused_mlp_fwd(x.cuda(), *_gpu(ws))
