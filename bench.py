@@ -877,6 +877,9 @@ def run_training(args, world, rank, dist, barrier, name, rows):
 
 def main():
     args = parse_args()
+    # the clock sampler is a Python thread: a short interpreter switch interval
+    # lets it run while the main thread launches a timed region of ~10 ms
+    sys.setswitchinterval(0.0002)
     if args.impl == "reference":
         run_reference(args)
     else:
