@@ -327,6 +327,7 @@ __global__ void __launch_bounds__(BwdCfg<NetT, H32>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(gbase + Cfg::OFF_MISC);
+  pdl_enter();
   const int G = gridDim.x;
   auto tile_of = [&](int i) { return static_cast<int>(blockIdx.x) + i * G; };
 
@@ -814,6 +815,7 @@ struct DwLayout {
 __global__ void __launch_bounds__(kReduceElems * kReduceSlices)
     mlp_reduce_kernel(const float* __restrict__ partials, int nparts, int nfloats,
                       float* __restrict__ dw, const __grid_constant__ DwLayout lay) {
+  pdl_enter();
   __shared__ float red[kReduceSlices][kReduceElems];
   partials += static_cast<size_t>(blockIdx.y) * nparts * nfloats;
   const int le = threadIdx.x % kReduceElems, sl = threadIdx.x / kReduceElems;

@@ -17,6 +17,7 @@ namespace mlpk {
 
 __global__ void __launch_bounds__(256) mlp_cast_f32_f16_kernel(const float* __restrict__ src,
                                                               __half* __restrict__ dst, int64_t n) {
+  pdl_enter();
   const int64_t n8 = n / 8;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8; i += stride) {
@@ -32,6 +33,7 @@ __global__ void __launch_bounds__(256) mlp_cast_f32_f16_kernel(const float* __re
 
 __global__ void __launch_bounds__(256) mlp_cast_f16_f32_kernel(const __half* __restrict__ src,
                                                               float* __restrict__ dst, int64_t n) {
+  pdl_enter();
   const int64_t n8 = n / 8;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8; i += stride) {

@@ -422,6 +422,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW, H32>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(gbase + Cfg::OFF_MISC);
+  pdl_enter();
 
   const int G = gridDim.x;
   auto tile_of = [&](int p, int s) { return static_cast<int>(blockIdx.x) + (p * NS + s) * G; };

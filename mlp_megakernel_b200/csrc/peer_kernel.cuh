@@ -76,6 +76,7 @@ __device__ __forceinline__ void peer_signal_all(const PeerPtrs& peers, int world
 
 __global__ void __launch_bounds__(256)
     mlp_peer_allreduce_kernel(PeerPtrs peers, int world, int rank, int n, float* __restrict__ out) {
+  pdl_enter();
   auto words = [&](int q) { return reinterpret_cast<uint32_t*>(peers.buf[q] + static_cast<size_t>(n)); };
   uint32_t* const ready = words(rank);                  // ready[kPeerMaxRanks]
   uint32_t* const done = ready + kPeerMaxRanks;         // done[kPeerMaxRanks]

@@ -97,6 +97,20 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while
+// the kernel before it on the stream is still running, so every kernel of the
+// library calls pdl_enter() after its own setup (barrier init, TMEM
+// allocation: shared memory and TMEM only) and before its first access to
+// global memory.  griddepcontrol.wait returns once the grids it depends on
+// have completed and their memory operations are visible (at once when there
+// are none); launch_dependents lets the next kernel's CTAs start their own
+// setup as SMs free up (they wait in turn before touching memory).
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -294,6 +294,7 @@ __global__ void __launch_bounds__(StreamCfg<ChainT, EPW, TF32>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(gbase + Cfg::OFF_MISC);
+  pdl_enter();
   const int G = gridDim.x;
 
   if (warp == 0) {

@@ -90,6 +90,7 @@ __global__ void __launch_bounds__(WgradCfg<DA, DB>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(gbase + Cfg::OFF_MISC);
+  pdl_enter();
 
   if (warp == 0) {
     if (lane == 0 && l < L) {

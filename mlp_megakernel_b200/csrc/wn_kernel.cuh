@@ -69,6 +69,7 @@ __device__ __forceinline__ float wn_col_sum(float v, float (*red)[kWnCols + 1], 
 __global__ void __launch_bounds__(kWnCols * kWnRowGroups)
     mlp_wn_fwd_kernel(WnShape s, const float* __restrict__ v_all, const float* __restrict__ g_all,
                       WnOut out, float* __restrict__ inv_norm) {
+  pdl_enter();
   __shared__ float red[kWnRowGroups][kWnCols + 1];
   const int c = threadIdx.x % kWnCols, r = threadIdx.x / kWnCols;
   int col0;
@@ -101,6 +102,7 @@ __global__ void __launch_bounds__(kWnCols * kWnRowGroups)
     mlp_wn_bwd_kernel(WnShape s, const float* __restrict__ dw_all, const float* __restrict__ v_all,
                       const float* __restrict__ g_all, const float* __restrict__ inv_norm,
                       float* __restrict__ dv_all, float* __restrict__ dg_all) {
+  pdl_enter();
   __shared__ float red[kWnRowGroups][kWnCols + 1];
   const int c = threadIdx.x % kWnCols, r = threadIdx.x / kWnCols;
   int col0;
