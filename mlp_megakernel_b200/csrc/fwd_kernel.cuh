@@ -157,15 +157,6 @@ struct FwdCfg {
                                                           : 512;
   static constexpr int THREADS = (2 + NS * EPW) * 32;
   static constexpr int NG = EPW / 4;  // column groups per slot
-  // HS_COL: hidden activation columns [0, HS_COL) are handed to the next
-  // layer packed in TMEM (TS UMMA), columns [HS_COL, H) through the slot's
-  // staging tile in shared memory (K-major A of an SS UMMA; the tile holds
-  // the output only at the end of a tile).  The epilogue's TMEM stores slow
-  // the tensor core's concurrent MMAs (3L128 at 4M rows: 0.545 ms with them,
-  // 0.375 ms with the stores left out, 0.365 ms with no epilogue work at
-  // all), SS UMMAs load shared memory (0.577 ms with every column through it).
-  // fp32 saved activations use the staging region for their pieces: TMEM only.
-  static constexpr int HS_COL = HMAX;  // first hidden column handed through shared memory
   static_assert(EPW % 4 == 0, "epilogue warps come in groups of 4 (one per TMEM lane quarter)");
   static_assert(L >= 2, "at least two layers");
   static constexpr int H = NetT::template D<1>();  // hidden width (all hidden layers)
@@ -205,10 +196,9 @@ __device__ __forceinline__ void publish_chunk(uint32_t bar) {
 // Hidden-layer job of one warp of column group `grp` (of NG): stripes
 // grp, grp+NG, grp+2NG, ... (32 columns each) of the accumulator buffer at
 // TMEM address tbuf (lane field = the warp's quarter) -> softplus -> fp16 back
-// into TMEM at h_tmem_col() -- or, for the columns from SMC on, into the
-// staging tile, which the next layer's UMMA reads from shared memory; after
-// every SPC stripes it arrives on the next chunk barrier (chunk_bar0 +
-// 8*(j/SPC)), which completes once all NG groups finished those stripes.  SAVE = 1 also writes the fp16 activation to this
+// into TMEM at h_tmem_col(); after every SPC stripes it arrives on the next
+// chunk barrier (chunk_bar0 + 8*(j/SPC)), which completes once all NG groups
+// finished those stripes.  SAVE = 1 also writes the fp16 activation to this
 // thread's row in global memory (hrow), SAVE = 2 into the swizzled staging
 // tile at stage_base (row `row`) for a TMA store.  A
 // column is always loaded before the packed activation overwrites it: a
@@ -253,15 +243,13 @@ __device__ __forceinline__ void f32_piece_end(const F32Save& fs, uint32_t buf, i
   ++*fs.count;
 }
 
-template <int N, int NG, int SPC, int SAVE = 0, int NPB = 2, int SMC = N>
+template <int N, int NG, int SPC, int SAVE = 0, int NPB = 2>
 __device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chunk_bar0,
                                            uint8_t* hrow = nullptr, uint32_t stage_base = 0,
                                            uint32_t row = 0, const F32Save* fs = nullptr) {
   static_assert(N % (32 * NG) == 0, "hidden width must be a multiple of 32 * column groups");
   constexpr int SUBS = N / (32 * NG);
   static_assert(SUBS % SPC == 0, "stripes per chunk must divide the stripes per group");
-  static_assert(SMC == N || SAVE == 0 || SAVE == 2, "shared-memory hand-off: no fp32 or row saves");
-  bool chunk_tm = false, chunk_sm = false;  // media written since the last publish
   uint32_t a[32];
   tmem_ld_wait_x32(tbuf + 32 * grp, a);
 #pragma unroll
@@ -288,11 +276,7 @@ __device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chun
     } else {
       pack_cols<16, true>(a, w);
     }
-    const bool to_smem = col >= SMC;  // warp-uniform
-    if (!to_smem) {
-      tmem_st_x16(tbuf + h_tmem_col(col), w);
-      chunk_tm = true;
-    }
+    tmem_st_x16(tbuf + h_tmem_col(col), w);
     if constexpr (SAVE == 1) {
       if (hrow != nullptr) {  // this thread's row exists (row < M): save h for backward
         uint4* dst = reinterpret_cast<uint4*>(hrow + 2 * col);
@@ -300,8 +284,7 @@ __device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chun
         for (int v = 0; v < 4; ++v)
           dst[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
       }
-    }
-    if (SAVE == 2 || to_smem) {
+    } else if constexpr (SAVE == 2) {
       constexpr int C = chunk_elems(N);
       constexpr int P = pitch_bytes(N);
 #pragma unroll
@@ -310,18 +293,8 @@ __device__ __forceinline__ void hidden_job(uint32_t tbuf, int grp, uint32_t chun
         st_shared_v4(stage_base + (cc / C) * (kTileM * P) + swz_off<P>(row, (cc % C) / 8), w[4 * v],
                      w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
       }
-      chunk_sm = chunk_sm || to_smem;
     }
-    if ((j + 1) % SPC == 0) {
-      // the chunk's TMEM stores complete / its shared-memory stores visible
-      // to the tensor core, then the arrive
-      if (chunk_tm) tmem_wait_st();
-      if (chunk_sm) fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane_id() == 0) mbar_arrive(chunk_bar0 + 8 * (j / SPC));
-      chunk_tm = chunk_sm = false;
-    }
+    if ((j + 1) % SPC == 0) publish_chunk(chunk_bar0 + 8 * (j / SPC));
     if (j + 1 < SUBS) {
       tmem_wait_ld_bind_x32(b);
 #pragma unroll
@@ -531,15 +504,13 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW, H32>::THREADS, 1)
           } else {
             // chunk j of h_{l-1} = stripe j of every column group (32*NG
             // columns), complete once all epilogue warps of the slot arrived.
-            // A comes from the slot's staging tile (K-steps from HS_COL on: K-major, SS UMMA) or
-            // from TMEM: the previous job's buffer, where the epilogue packed
-            // h_{l-1} (h_tmem_col).
+            // A comes from TMEM: the previous job's buffer, where the
+            // epilogue packed h_{l-1} (h_tmem_col).
             constexpr int NGRP = Cfg::NG;
             constexpr int SPC = Cfg::SPC;
             constexpr int NCH = K / (32 * NGRP * SPC);
             static_assert(NCH >= 1 && K % (32 * NGRP * SPC) == 0, "hidden width vs chunks");
             const uint32_t a_tmem = tmem_base + (2 * s + ((i * L + l - 1) & 1)) * Cfg::SLOT_COLS;
-            const uint64_t a_sdesc0 = kmajor_base_desc<K>(s_o + s * Cfg::O_BYTES);
             const uint32_t par = (i * (L - 1) + l - 1) & 1;
 #pragma unroll
             for (int j = 0; j < NCH; ++j) {
@@ -555,13 +526,9 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW, H32>::THREADS, 1)
 #pragma unroll
                     for (int kk = 0; kk < 2; ++kk) {
                       const int k = 2 * ((j * SPC + js) * NGRP + g) + kk;  // K-step
-                      const uint32_t acc = (j == 0 && js == 0 && g == 0 && kk == 0) ? 0u : 1u;
-                      if (16 * k >= Cfg::HS_COL)
-                        umma_f16(d_tmem, a_sdesc0 + (kmajor_koff<kTileM, K>(k) >> 4),
-                                 bdesc0 + (mnmajor_koff<N>(k) >> 4), idesc, acc);
-                      else
-                        umma_f16_ts(d_tmem, a_tmem + h_tmem_col(16 * k), bdesc0 + (mnmajor_koff<N>(k) >> 4),
-                                    idesc, acc);
+                      umma_f16_ts(d_tmem, a_tmem + h_tmem_col(16 * k),
+                                  bdesc0 + (mnmajor_koff<N>(k) >> 4), idesc,
+                                  (j == 0 && js == 0 && g == 0 && kk == 0) ? 0u : 1u);
                     }
                   }
                 }
@@ -634,8 +601,8 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW, H32>::THREADS, 1)
           const F32Save fs{&maps.hsave[l], obuf, q, t * kTileM + q * 32, maps.M, maps.h_cols[l], &pieces};
           hidden_job<H, Cfg::NG, Cfg::SPC, 3, Cfg::NPB>(t_buf, grp, bar_chunk(s, 0), nullptr, 0, row, &fs);
         } else if constexpr (TRAIN) {
-          // h_l -> the staging tile (next layer's A) -> TMA store
-          hidden_job<H, Cfg::NG, Cfg::SPC, 2, 2, Cfg::HS_COL>(t_buf, grp, bar_chunk(s, 0), nullptr, obuf, row);
+          // h_l -> TMEM (next layer's A) and the staging tile -> TMA store
+          hidden_job<H, Cfg::NG, Cfg::SPC, 2>(t_buf, grp, bar_chunk(s, 0), nullptr, obuf, row);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar_out_ready(s));
@@ -653,8 +620,7 @@ __global__ void __launch_bounds__(FwdCfg<NetT, NS, EPW, H32>::THREADS, 1)
           ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
           if (!ok) break;
         } else {
-          // h_l -> TMEM and / or the staging tile, the next layer's A
-          hidden_job<H, Cfg::NG, Cfg::SPC, 0, 2, Cfg::HS_COL>(t_buf, grp, bar_chunk(s, 0), nullptr, obuf, row);
+          hidden_job<H, Cfg::NG, Cfg::SPC>(t_buf, grp, bar_chunk(s, 0));
         }
       }
       if (!ok) break;
