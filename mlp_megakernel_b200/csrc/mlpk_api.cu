@@ -894,6 +894,8 @@ int make_wn_shape(const mlpk_shape* s, mlpk::WnShape* w) {
   long long vo = 0;
   int go = 0;
   for (int l = 0; l < s->num_layers; ++l) {
+    // a column's rows live in the registers of 32 row-group threads
+    if (s->dims[l] > mlpk::kWnRowGroups * mlpk::kWnMaxPer) return MLPK_ERR_UNSUPPORTED;
     w->din[l] = s->dims[l];
     w->dout[l] = s->dims[l + 1];
     w->voff[l] = vo;

@@ -37,11 +37,17 @@ struct WnOut {
   __half* w[8];
 };
 
-// Block = one layer x 32 output columns; 256 threads = 32 columns x 8 row
-// groups.  Thread (c, r) handles column c and rows r, r+8, r+16, ...; the
-// per-column sums are combined through shared memory in a fixed order.
+// Block = one layer x 32 output columns; 1024 threads = 32 columns x 32 row
+// groups.  Thread (c, r) holds rows r, r+32, ... (at most kWnMaxPer of them:
+// widths up to 256) of column c in registers, so every value is read from
+// global memory once, in one batch of independent loads; the per-column sums
+// are combined through shared memory in a fixed order (row group 0, 1, ...),
+// so the results are bitwise reproducible.  (The first version, 8 row groups
+// re-reading v in a second pass, took ~9 us per launch for 3L128, two
+// dependent chains of loads.)
 constexpr int kWnCols = 32;
-constexpr int kWnRowGroups = 8;
+constexpr int kWnRowGroups = 32;
+constexpr int kWnMaxPer = 8;  // rows per thread: 256 / 32
 
 __device__ __forceinline__ int wn_block_layer(const WnShape& s, int b, int& col0) {
   int l = 0, nb = 0;
@@ -78,21 +84,25 @@ __global__ void __launch_bounds__(kWnCols * kWnRowGroups)
   const int j = col0 + c;
   const bool valid = j < N;
   const float* v = v_all + s.voff[l];
-  float ss = 0.0f;
-  if (valid) {
-#pragma unroll 4
-    for (int i = r; i < K; i += kWnRowGroups) {
-      const float a = v[static_cast<size_t>(i) * N + j];
-      ss = fmaf(a, a, ss);
-    }
+  float a[kWnMaxPer];
+#pragma unroll
+  for (int u = 0; u < kWnMaxPer; ++u) {
+    const int i = r + u * kWnRowGroups;
+    a[u] = (valid && i < K) ? v[static_cast<size_t>(i) * N + j] : 0.0f;
   }
+  float ss = 0.0f;
+#pragma unroll
+  for (int u = 0; u < kWnMaxPer; ++u) ss = fmaf(a[u], a[u], ss);
   ss = wn_col_sum(ss, red, c, r);
   if (!valid) return;
   const float inv = 1.0f / sqrtf(ss);
   const float scale = g_all[s.goff[l] + j] * inv;
   __half* w = out.w[l];
-  for (int i = r; i < K; i += kWnRowGroups)
-    w[static_cast<size_t>(i) * N + j] = __float2half_rn(v[static_cast<size_t>(i) * N + j] * scale);
+#pragma unroll
+  for (int u = 0; u < kWnMaxPer; ++u) {
+    const int i = r + u * kWnRowGroups;
+    if (i < K) w[static_cast<size_t>(i) * N + j] = __float2half_rn(a[u] * scale);
+  }
   if (r == 0) inv_norm[s.goff[l] + j] = inv;
 }
 
@@ -113,14 +123,18 @@ __global__ void __launch_bounds__(kWnCols * kWnRowGroups)
   const float* v = v_all + s.voff[l];
   const float* dw = dw_all + s.voff[l];
   float* dv = dv_all + s.voff[l];
-  float dot = 0.0f;
-  if (valid) {
-#pragma unroll 4
-    for (int i = r; i < K; i += kWnRowGroups) {
-      const size_t e = static_cast<size_t>(i) * N + j;
-      dot = fmaf(dw[e], v[e], dot);
-    }
+  float gv[kWnMaxPer], vv[kWnMaxPer];
+#pragma unroll
+  for (int u = 0; u < kWnMaxPer; ++u) {
+    const int i = r + u * kWnRowGroups;
+    const bool in = valid && i < K;
+    const size_t e = static_cast<size_t>(i) * N + j;
+    gv[u] = in ? dw[e] : 0.0f;
+    vv[u] = in ? v[e] : 0.0f;
   }
+  float dot = 0.0f;
+#pragma unroll
+  for (int u = 0; u < kWnMaxPer; ++u) dot = fmaf(gv[u], vv[u], dot);
   dot = wn_col_sum(dot, red, c, r);
   if (!valid) return;
   const float inv = inv_norm[s.goff[l] + j];
@@ -128,9 +142,10 @@ __global__ void __launch_bounds__(kWnCols * kWnRowGroups)
   const float dg = dot * inv;
   const float a = gj * inv;
   const float b = gj * dg * inv * inv;
-  for (int i = r; i < K; i += kWnRowGroups) {
-    const size_t e = static_cast<size_t>(i) * N + j;
-    dv[e] = fmaf(a, dw[e], -b * v[e]);
+#pragma unroll
+  for (int u = 0; u < kWnMaxPer; ++u) {
+    const int i = r + u * kWnRowGroups;
+    if (i < K) dv[static_cast<size_t>(i) * N + j] = fmaf(a, gv[u], -b * vv[u]);
   }
   if (r == 0) dg_all[s.goff[l] + j] = dg;
 }
