@@ -786,12 +786,14 @@ __global__ void __launch_bounds__(BwdCfg<NetT, H32>::THREADS, 1)
   }
 }
 
-// Level-2 reduction of the per-CTA partials: a block covers kReduceElems
-// elements with kReduceSlices threads each; slice s sums partials p = s,
-// s + kReduceSlices, ... in increasing p, and the slices are added in slice
-// order.  The order is fixed, so dW is bitwise reproducible.  blockIdx.y
-// selects an independent group (nparts partials of nfloats each, written to
-// dw + y * nfloats), e.g. one group per layer of the split-K wgrad kernel.
+// Level-2 reduction of the per-CTA partials: a block covers kReduceElems x
+// VEC elements with kReduceSlices threads each (a thread reads VEC
+// neighbouring elements per load: 16-byte loads when nfloats is a multiple of
+// 4); slice s sums partials p = s, s + kReduceSlices, ... in increasing p, and
+// the slices are added in slice order.  The order is fixed, so dW is bitwise
+// reproducible (and independent of VEC).  blockIdx.y selects an independent
+// group (nparts partials of nfloats each, written to dw + y * nfloats), e.g.
+// one group per layer of the split-K wgrad kernel.
 constexpr int kReduceElems = 64;
 constexpr int kReduceSlices = 4;
 
@@ -812,44 +814,75 @@ struct DwLayout {
   long long roff[8];
 };
 
+template <int VEC>
+struct ReduceVec;
+template <>
+struct ReduceVec<1> {
+  using T = float;
+  static __device__ __forceinline__ void add(float* a, T v) { a[0] += v; }
+};
+template <>
+struct ReduceVec<4> {
+  using T = float4;
+  static __device__ __forceinline__ void add(float* a, T v) {
+    a[0] += v.x;
+    a[1] += v.y;
+    a[2] += v.z;
+    a[3] += v.w;
+  }
+};
+
+template <int VEC>
 __global__ void __launch_bounds__(kReduceElems * kReduceSlices)
     mlp_reduce_kernel(const float* __restrict__ partials, int nparts, int nfloats,
                       float* __restrict__ dw, const __grid_constant__ DwLayout lay) {
   pdl_enter();
-  __shared__ float red[kReduceSlices][kReduceElems];
+  using V = ReduceVec<VEC>;
+  using T = typename V::T;
+  __shared__ float red[kReduceSlices][kReduceElems * VEC];
   partials += static_cast<size_t>(blockIdx.y) * nparts * nfloats;
   const int le = threadIdx.x % kReduceElems, sl = threadIdx.x / kReduceElems;
-  const int e = blockIdx.x * kReduceElems + le;
-  float acc = 0.0f;
+  const int e = (blockIdx.x * kReduceElems + le) * VEC;  // nfloats is a multiple of VEC
+  float acc[VEC];
+#pragma unroll
+  for (int k = 0; k < VEC; ++k) acc[k] = 0.0f;
   if (e < nfloats) {
-    // 8 loads in flight, added in increasing p (the fixed order)
+    // U loads in flight, added in increasing p (the fixed order)
     constexpr int U = 8;
+    const size_t stride = static_cast<size_t>(nfloats) / VEC;
+    const T* src = reinterpret_cast<const T*>(partials) + e / VEC;
     int p = sl;
     for (; p + (U - 1) * kReduceSlices < nparts; p += U * kReduceSlices) {
-      float v[U];
+      T v[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u) v[u] = partials[static_cast<size_t>(p + u * kReduceSlices) * nfloats + e];
+      for (int u = 0; u < U; ++u) v[u] = src[static_cast<size_t>(p + u * kReduceSlices) * stride];
 #pragma unroll
-      for (int u = 0; u < U; ++u) acc += v[u];
+      for (int u = 0; u < U; ++u) V::add(acc, v[u]);
     }
-    for (; p < nparts; p += kReduceSlices) acc += partials[static_cast<size_t>(p) * nfloats + e];
+    for (; p < nparts; p += kReduceSlices) V::add(acc, src[static_cast<size_t>(p) * stride]);
   }
-  red[sl][le] = acc;
-  __syncthreads();
-  if (sl == 0 && e < nfloats) {
-    float t = red[0][le];
 #pragma unroll
-    for (int k = 1; k < kReduceSlices; ++k) t += red[k][le];
-    const long long eg = static_cast<long long>(blockIdx.y) * nfloats + e;
-    if (lay.layers == 0) {
-      dw[eg] = t;
-    } else {
-      int l = 0;
-      while (l + 1 < lay.layers && eg >= lay.koff[l + 1]) ++l;
-      const long long q = eg - lay.koff[l];
-      const int r = static_cast<int>(q / lay.kn[l]);
-      const int c = static_cast<int>(q % lay.kn[l]);
-      if (r < lay.rk[l] && c < lay.rn[l]) dw[lay.roff[l] + static_cast<long long>(r) * lay.rn[l] + c] = t;
+  for (int k = 0; k < VEC; ++k) red[sl][le * VEC + k] = acc[k];
+  __syncthreads();
+  // the first kReduceElems x VEC threads finish one element each
+  const int fe = threadIdx.x;
+  if (fe < kReduceElems * VEC) {
+    const int eo = blockIdx.x * kReduceElems * VEC + fe;
+    if (eo < nfloats) {
+      float t = red[0][fe];
+#pragma unroll
+      for (int k = 1; k < kReduceSlices; ++k) t += red[k][fe];
+      const long long eg = static_cast<long long>(blockIdx.y) * nfloats + eo;
+      if (lay.layers == 0) {
+        dw[eg] = t;
+      } else {
+        int l = 0;
+        while (l + 1 < lay.layers && eg >= lay.koff[l + 1]) ++l;
+        const long long q = eg - lay.koff[l];
+        const int r = static_cast<int>(q / lay.kn[l]);
+        const int c = static_cast<int>(q % lay.kn[l]);
+        if (r < lay.rk[l] && c < lay.rn[l]) dw[lay.roff[l] + static_cast<long long>(r) * lay.rn[l] + c] = t;
+      }
     }
   }
 }

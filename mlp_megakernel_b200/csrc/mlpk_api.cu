@@ -336,6 +336,22 @@ mlpk::DwLayout dw_layout(const int* rd) {
   return lay;
 }
 
+// Fixed-order sum of `groups` groups of nparts partials (nfloats each) into dw;
+// 16-byte loads when the partial rows stay 16-byte aligned (bitwise the same
+// sums either way).
+inline int launch_reduce(const float* partials, int nparts, int nfloats, int groups, float* dw,
+                         const mlpk::DwLayout& lay, cudaStream_t st) {
+  const int threads = mlpk::kReduceElems * mlpk::kReduceSlices;
+  if (nfloats % 4 == 0 && reinterpret_cast<uintptr_t>(partials) % 16 == 0) {
+    const int per = mlpk::kReduceElems * 4;
+    return launch_kernel(mlpk::mlp_reduce_kernel<4>, dim3((nfloats + per - 1) / per, groups, 1), threads, 0,
+                         st, partials, nparts, nfloats, dw, lay);
+  }
+  return launch_kernel(mlpk::mlp_reduce_kernel<1>,
+                       dim3((nfloats + mlpk::kReduceElems - 1) / mlpk::kReduceElems, groups, 1), threads, 0,
+                       st, partials, nparts, nfloats, dw, lay);
+}
+
 template <class NetT>
 int launch_bwd(const int* rd, const void* x, const void* const* W, const void* const* h, bool h32,
                const void* g, void* dx, float* ws, size_t ws_bytes, float* dw, int64_t M, cudaStream_t st) {
@@ -381,9 +397,7 @@ int launch_bwd(const int* rd, const void* x, const void* const* W, const void* c
       if ((rc = launch_kernel(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, st, maps, num_tiles))) return rc;
     }
   }
-  return launch_kernel(mlpk::mlp_reduce_kernel, (nfloats + mlpk::kReduceElems - 1) / mlpk::kReduceElems,
-                       mlpk::kReduceElems * mlpk::kReduceSlices, 0, st,
-                       static_cast<const float*>(ws), grid, nfloats, dw, dw_layout<NetT>(rd));
+  return launch_reduce(static_cast<const float*>(ws), grid, nfloats, 1, dw, dw_layout<NetT>(rd), st);
 }
 
 // ------------------------------------------------------------------ streamed weights
@@ -565,10 +579,7 @@ int launch_stream_bwd(const int* rd, const void* x, const void* const* W, const 
   }
   // 3. fixed-order sum of each layer's P partials
   constexpr int nfloats = Lay::DA * Lay::DB;
-  return launch_kernel(mlpk::mlp_reduce_kernel,
-                       dim3((nfloats + mlpk::kReduceElems - 1) / mlpk::kReduceElems, L, 1),
-                       mlpk::kReduceElems * mlpk::kReduceSlices, 0, st,
-                       static_cast<const float*>(partials), P, nfloats, dw, dw_layout<NetT>(rd));
+  return launch_reduce(static_cast<const float*>(partials), P, nfloats, L, dw, dw_layout<NetT>(rd), st);
 }
 
 // ------------------------------------------------------------------ dispatch

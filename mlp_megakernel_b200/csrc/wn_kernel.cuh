@@ -97,7 +97,10 @@ __global__ void __launch_bounds__(kWnCols * kWnRowGroups)
   if (!valid) return;
   const float inv = 1.0f / sqrtf(ss);
   const float scale = g_all[s.goff[l] + j] * inv;
-  __half* w = out.w[l];
+  __half* w = out.w[0];  // a constant-index pick: out.w[l] would copy out to the stack
+#pragma unroll
+  for (int k = 1; k < 8; ++k)
+    if (k == l) w = out.w[k];
 #pragma unroll
   for (int u = 0; u < kWnMaxPer; ++u) {
     const int i = r + u * kWnRowGroups;
