@@ -174,7 +174,17 @@ struct BwdCfg {
   static constexpr int OFF_MISC = OFF_BAR + 8 * NUM_BARS;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static constexpr int ACC_COL = dw_col(L);
-  static constexpr int TMEM_COLS_RAW = ACC_COL + NS * ACC_W;
+  // Data-gradient GEMMs with A from TMEM: the epilogue also packs dz_l
+  // (fp16, two per column) into a per-slot TMEM tile at ZT_COL that the next
+  // dgrad reads as its A operand (the TS form reads only W from shared
+  // memory: 2 of the 6 KB an SS 128x64x16 UMMA reads), where TMEM has room
+  // for it beside the dW and dgrad accumulators (the 64-wide networks and the
+  // 5-layer one; not 3L128, whose accumulators fill TMEM).  dz_L = g still
+  // comes from its ring slot (SS).
+  static constexpr int ZT_W = NetT::template D<1>() / 2;
+  static constexpr bool DG_TS = !H32 && L >= 2 && ACC_COL + NS * (ACC_W + ZT_W) <= 512;
+  static constexpr int ZT_COL = ACC_COL + NS * ACC_W;
+  static constexpr int TMEM_COLS_RAW = ACC_COL + NS * ACC_W + (DG_TS ? NS * ZT_W : 0);
   static constexpr int TMEM_COLS = TMEM_COLS_RAW <= 128 ? 128 : TMEM_COLS_RAW <= 256 ? 256 : 512;
   static constexpr int PARTIAL_FLOATS = [] {
     int n = 0;
@@ -243,6 +253,28 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[CW]) 
   else if constexpr (CW == 16) tmem_ld_wait_x16(taddr, r);
   else if constexpr (CW == 32) tmem_ld_wait_x32(taddr, r);
   else tmem_ld_wait_x64(taddr, r);
+}
+
+// N consecutive 32-bit TMEM columns of this warp's lanes from registers
+// (complete with tmem_wait_st()).
+template <int N>
+__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&r)[N]) {
+  if constexpr (N == 4) {
+    tmem_st_x4(taddr, r);
+  } else if constexpr (N == 8) {
+    tmem_st_x8(taddr, r);
+  } else if constexpr (N == 16) {
+    tmem_st_x16(taddr, r);
+  } else {
+    static_assert(N % 16 == 0, "TMEM store width");
+#pragma unroll
+    for (int c = 0; c < N; c += 16) {
+      uint32_t w[16];
+#pragma unroll
+      for (int v = 0; v < 16; ++v) w[v] = r[c + v];
+      tmem_st_x16(taddr + c, w);
+    }
+  }
 }
 
 // The layer index l = L - 1 - i of static_for iteration i, as a type.
@@ -439,17 +471,25 @@ __global__ void __launch_bounds__(BwdCfg<NetT, H32>::THREADS, 1)
     const bool issuer = (lane == 0);
     // dgrad: dh_l[128 x d_l] = dz_{l+1} W_l^T: A = dz (K-major, K = d_{l+1}),
     // B = W_l as stored ([d_l rows][d_{l+1}] = K-major W_l^T)
-    auto issue_dgrad = [&](auto lc, uint32_t acc, uint32_t zsrc) {
+    // (DG_TS, l < L-1: A = the packed dz_{l+1} in TMEM at zt, 16 K-elements
+    // per 8 columns)
+    auto issue_dgrad = [&](auto lc, uint32_t acc, uint32_t zsrc, uint32_t zt) {
       constexpr int l = decltype(lc)::value;
       constexpr int DI = NetT::template D<l>();
       constexpr int DO = NetT::template D<l + 1>();
       constexpr uint32_t idesc_d = make_idesc_f16(kTileM, DI, 0, 0);
-      const uint64_t ad0 = kmajor_base_desc<DO>(zsrc);
       const uint64_t bd0 = kmajor_base_desc<DO>(s_w + NetT::template w_off<l>());
+      if constexpr (Cfg::DG_TS && l < L - 1) {
 #pragma unroll
-      for (int k = 0; k < DO / 16; ++k)
-        umma_f16(acc, ad0 + (kmajor_koff<kTileM, DO>(k) >> 4), bd0 + (kmajor_koff<DI, DO>(k) >> 4), idesc_d,
-                 k > 0 ? 1u : 0u);
+        for (int k = 0; k < DO / 16; ++k)
+          umma_f16_ts(acc, zt + 8 * k, bd0 + (kmajor_koff<DI, DO>(k) >> 4), idesc_d, k > 0 ? 1u : 0u);
+      } else {
+        const uint64_t ad0 = kmajor_base_desc<DO>(zsrc);
+#pragma unroll
+        for (int k = 0; k < DO / 16; ++k)
+          umma_f16(acc, ad0 + (kmajor_koff<kTileM, DO>(k) >> 4), bd0 + (kmajor_koff<DI, DO>(k) >> 4), idesc_d,
+                   k > 0 ? 1u : 0u);
+      }
     };
     // wgrad over the 128 tile rows (K): dW_l += h_l^T dz (A = h_l, B = dz) or,
     // transposed, dW_l^T += dz^T h_l (A = dz, B = h_l); both operands
@@ -512,7 +552,7 @@ __global__ void __launch_bounds__(BwdCfg<NetT, H32>::THREADS, 1)
           if (!ok) return;
           tc_fence_after();
           if (issuer) {
-            issue_dgrad(std::integral_constant<int, l>{}, acc, zsrc);
+            issue_dgrad(std::integral_constant<int, l>{}, acc, zsrc, 0u);
             umma_commit(bar_acc_full(0));
             if constexpr (l < L - 1) {
               // weight gradient of layer l+1: A = fp16 h_{l+1} (low half-slot),
@@ -578,7 +618,7 @@ __global__ void __launch_bounds__(BwdCfg<NetT, H32>::THREADS, 1)
             tc_fence_after();
             const uint32_t a_h = slot_addr(na % R);
             if (issuer) {
-              issue_dgrad(lc_rev<L>(lc), acc, zsrc);
+              issue_dgrad(lc_rev<L>(lc), acc, zsrc, tmem_base + Cfg::ZT_COL + s * Cfg::ZT_W);
               umma_commit(bar_acc_full(s));
               issue_wgrad(lc_rev<L>(lc), i, a_h, zsrc);
               umma_commit(bar_wg_done(s));
@@ -697,6 +737,11 @@ __global__ void __launch_bounds__(BwdCfg<NetT, H32>::THREADS, 1)
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(bar_slot_empty(nh % R));  // h_l read
+          if constexpr (Cfg::DG_TS) {
+            // dz_l -> TMEM for dgrad(l-1); its previous contents, dz_{l+1},
+            // were read by dgrad(l), complete since its acc_full commit
+            tmem_st_cols<CW / 2>(tmem_base + lane_off + Cfg::ZT_COL + s * Cfg::ZT_W + c0 / 2, o);
+          }
           if constexpr (Cfg::G_TILES == 1) {
             // G still holds dz_{l+1} until this layer's wgrad has read it
             ok = __all_sync(0xffffffffu, mbar_wait(bar_wg_done(s), step & 1, abort_flag, kDevTimeoutEpi));
@@ -710,6 +755,7 @@ __global__ void __launch_bounds__(BwdCfg<NetT, H32>::THREADS, 1)
           for (int u = 0; u < CW / 8; ++u)
             st_tile_row8<DI>(sg, row, c0 + 8 * u, o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
           fence_proxy_async_smem();
+          if constexpr (Cfg::DG_TS) tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar_dz_full(s));
