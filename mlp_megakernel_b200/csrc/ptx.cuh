@@ -137,19 +137,42 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
                "r"(src), "r"(c0), "r"(c1)
                : "memory");
 }
+// L2 eviction-priority policies (createpolicy), for the accesses below that
+// carry one (.L2::cache_hint): evict_last lines are kept over normal ones,
+// evict_first lines are the first to go.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
 // L2 prefetch of one TMA box (the box a tma_load_2d at these coordinates
-// would load); no shared memory or barrier involved.
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+// would load) under an eviction policy; no shared memory or barrier involved.
+__device__ __forceinline__ void tma_prefetch_l2_2d_hint(const CUtensorMap* map, int c0, int c1, uint64_t pol) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile.L2::cache_hint [%0, {%1, %2}], %3;" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1)
+               "r"(c0), "r"(c1), "l"(pol)
                : "memory");
 }
+// tma_load_2d under an eviction policy.
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0,
+                                                 int c1, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "l"(pol)
+      : "memory");
+}
 // Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) of global
-// memory into L2.
-__device__ __forceinline__ void prefetch_l2_bulk(const void* gptr, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(gptr)),
-               "r"(bytes)
+// memory into L2 under an eviction policy.
+__device__ __forceinline__ void prefetch_l2_bulk_hint(const void* gptr, uint32_t bytes, uint64_t pol) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(gptr)),
+               "r"(bytes), "l"(pol)
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() {
