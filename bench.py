@@ -41,7 +41,6 @@ import json
 import os
 import statistics
 import sys
-import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -114,79 +113,127 @@ REASON_BITS = {
 }
 
 
-class ClockSampler:
-    """Samples SM clock and clock-event reasons through NVML in a thread.
+def _clock_sample_loop(bus: str, index: int, period: float, conn, stop) -> None:
+    """Body of ClockSampler's child process: NVML samples of the SM clock and
+    the clock-event reasons every `period` seconds until `stop` is set, then
+    the list goes back through `conn`.  A separate process, not a thread: the
+    main process holds the interpreter lock while it waits in a CUDA
+    synchronize, which starved a sampler thread of all samples in a ~10 ms
+    timed region."""
+    try:
+        import pynvml as nv
 
-    Samples are timestamped; ``mark_start`` / ``mark_stop`` bracket the timed
-    region and ``summary`` reports the samples inside it (plus the ones taken
-    under load in the warm-up just before it when the timed region is shorter
-    than a few sample periods)."""
+        nv.nvmlInit()
+        try:
+            h = nv.nvmlDeviceGetHandleByPciBusId_v2(bus) if bus else nv.nvmlDeviceGetHandleByIndex(index)
+        except Exception:
+            h = nv.nvmlDeviceGetHandleByIndex(index)
+        reasons = None
+        for fn in ("nvmlDeviceGetCurrentClocksEventReasons", "nvmlDeviceGetCurrentClocksThrottleReasons"):
+            if hasattr(nv, fn):
+                reasons = getattr(nv, fn)
+                break
+        max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+    except Exception as e:  # no NVML: the parent reports it
+        conn.send(("error", repr(e)[:200]))
+        return
+    conn.send(("ready", max_mhz))
+    samples = []
+    while not stop.is_set():
+        try:
+            samples.append((time.monotonic(), nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                            reasons(h) if reasons else 0))
+        except Exception:
+            pass
+        time.sleep(period)
+    conn.send(("samples", samples))
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML in a child
+    process (spawned, so it shares no CUDA state and no interpreter lock with
+    the timing loop).
+
+    Samples are timestamped on the system's monotonic clock; ``mark_start`` /
+    ``mark_stop`` bracket the timed region and ``summary`` reports the samples
+    inside it (plus the ones taken under load in the warm-up just before it
+    when the timed region is shorter than a few sample periods)."""
 
     def __init__(self, device_index: int, period_s: float = 0.001):
         self.samples = []
         self.period = period_s
-        self._stop = threading.Event()
+        self.index = device_index
         self.ok = False
+        self.note = None
         self.max_mhz = None
         self.t_start = self.t_stop = None
+        self.bus = ""
         try:
-            import pynvml as nv
-
-            nv.nvmlInit()
-            self.nv = nv
+            import pynvml  # noqa: F401  (present: the child can sample)
             import torch
 
             props = torch.cuda.get_device_properties(device_index)
             try:
-                bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
-                self.h = nv.nvmlDeviceGetHandleByPciBusId_v2(bus)
+                self.bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
             except Exception:
-                self.h = nv.nvmlDeviceGetHandleByIndex(device_index)
-            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+                self.bus = ""
             self.ok = True
-        except Exception:
-            self.ok = False
-
-    def _reasons(self):
-        nv = self.nv
-        for fn in ("nvmlDeviceGetCurrentClocksEventReasons", "nvmlDeviceGetCurrentClocksThrottleReasons"):
-            if hasattr(nv, fn):
-                return getattr(nv, fn)(self.h)
-        return 0
-
-    def _run(self):
-        nv = self.nv
-        while not self._stop.is_set():
-            try:
-                t = time.perf_counter()
-                self.samples.append((t, nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM), self._reasons()))
-            except Exception:
-                pass
-            time.sleep(self.period)
+        except Exception as e:
+            self.note = f"NVML unavailable: {type(e).__name__}"
 
     def mark_start(self):
-        self.t_start = time.perf_counter()
+        self.t_start = time.monotonic()
 
     def mark_stop(self):
-        self.t_stop = time.perf_counter()
+        self.t_stop = time.monotonic()
 
     def __enter__(self):
-        if self.ok:
-            self.t = threading.Thread(target=self._run, daemon=True)
-            self.t.start()
-            time.sleep(3 * self.period)  # first samples before the caller's work starts
+        if not self.ok:
+            return self
+        import multiprocessing as mp
+
+        ctx = mp.get_context("spawn")
+        self._conn, child = ctx.Pipe()
+        self._stop = ctx.Event()
+        self.proc = ctx.Process(target=_clock_sample_loop,
+                                args=(self.bus, self.index, self.period, child, self._stop), daemon=True)
+        self.proc.start()
+        deadline = time.monotonic() + 60
+        while not self._conn.poll(0.05) and self.proc.is_alive() and time.monotonic() < deadline:
+            pass
+        if self._conn.poll(0):
+            kind, val = self._conn.recv()
+            if kind == "ready":
+                self.max_mhz = val
+                time.sleep(5 * self.period)  # first samples before the caller's work starts
+                return self
+            self.note = f"sampler: {val}"
+        else:
+            self.note = "sampler process did not start"
+        self.ok = False
+        self._stop.set()
+        self.proc.join(5)
+        if self.proc.is_alive():
+            self.proc.terminate()
         return self
 
     def __exit__(self, *a):
-        if self.ok:
-            time.sleep(2 * self.period)
-            self._stop.set()
-            self.t.join()
+        if not self.ok:
+            return
+        time.sleep(2 * self.period)
+        self._stop.set()
+        if self._conn.poll(30):
+            kind, val = self._conn.recv()
+            if kind == "samples":
+                self.samples = val
+        self.proc.join(10)
+        if self.proc.is_alive():
+            self.proc.terminate()
 
     def summary(self):
         if not self.ok or not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
-                    "note": "NVML unavailable" if not self.ok else "no samples"}
+                    "note": self.note or "no samples"}
         t0 = self.t_start if self.t_start is not None else -1e30
         t1 = self.t_stop if self.t_stop is not None else 1e30
         inside = [s for s in self.samples if t0 <= s[0] <= t1]
@@ -877,9 +924,6 @@ def run_training(args, world, rank, dist, barrier, name, rows):
 
 def main():
     args = parse_args()
-    # the clock sampler is a Python thread: a short interpreter switch interval
-    # lets it run while the main thread launches a timed region of ~10 ms
-    sys.setswitchinterval(0.0002)
     if args.impl == "reference":
         run_reference(args)
     else:
