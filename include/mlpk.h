@@ -225,7 +225,10 @@ int mlpk_cast_f16_f32(const void* src_f16, float* dst, int64_t n, mlpk_stream_t 
  * order into dW_out (bitwise identical on all ranks).  Every rank must call it
  * once per step, in the same order; the step count lives in device memory, so
  * the call can be captured in a CUDA graph.  When it returns (on the stream),
- * every rank has finished reading this rank's buffer.  If a peer does not
+ * this rank's dW input (the first n floats) may be rewritten; the other ranks
+ * may still be reading the rest of this rank's buffer until they return from
+ * the same step, so free a buffer (mlpk_peer_free) only after every rank has
+ * synchronized its device and met a host barrier.  If a peer does not
  * arrive within the bounded wait (1 s), the kernel sets MLPK_DEVST_TIMEOUT_FLAG
  * (16) in the device status word (mlpk_device_status).  At most 8 ranks;
  * mlpk_peer_alloc and mlpk_peer_open allocate / map device memory (set-up

@@ -1189,8 +1189,8 @@ int mlpk_peer_alloc(int64_t n, void** buf_out, void* handle_out) {
   if (!buf_out || !handle_out) return MLPK_ERR_NULL;
   if (n <= 0 || n % 4 != 0) return MLPK_ERR_SHAPE;
   static_assert(sizeof(cudaIpcMemHandle_t) == MLPK_PEER_HANDLE_BYTES, "IPC handle size");
-  // the slot of n floats, then ready[8], done[8], count, epoch (32-bit words, padded)
-  const size_t bytes = (static_cast<size_t>(n) + 4 * mlpk::kPeerMaxRanks) * sizeof(float);
+  // `in`, slot 0 and slot 1 (n floats each), then the ready and epoch words
+  const size_t bytes = 3 * static_cast<size_t>(n) * sizeof(float) + mlpk::kPeerFlagWords * sizeof(uint32_t);
   void* p = nullptr;
   int rc = cuda_status(cudaMalloc(&p, bytes));
   if (rc) return rc;
@@ -1235,8 +1235,12 @@ int mlpk_peer_allreduce(void* const* bufs, int world, int rank, int64_t n, float
   DevInfo di;
   int rc = current_device_info(&di, nullptr);
   if (rc != MLPK_OK) return rc;
-  const int64_t blocks = (n / 4 + 255) / 256;
-  const int grid = static_cast<int>(blocks < di.sm_count ? blocks : di.sm_count);
+  // the same grid on every call and every rank (CTA c always owns the same
+  // elements and flags): at most one CTA per SM, all resident
+  int64_t blocks = (n / 4 + 255) / 256;
+  if (blocks > di.sm_count) blocks = di.sm_count;
+  if (blocks > mlpk::kPeerMaxCtas) blocks = mlpk::kPeerMaxCtas;
+  const int grid = static_cast<int>(blocks);
   return launch_kernel(mlpk::mlp_peer_allreduce_kernel, grid, 256, 0, static_cast<cudaStream_t>(stream),
                        peers, world, rank, static_cast<int>(n), dW_out);
 }

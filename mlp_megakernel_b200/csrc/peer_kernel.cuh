@@ -3,23 +3,28 @@
 // reference's DP recipe, done without NCCL).
 //
 // Every rank owns one exported ("peer") buffer of
-//   [slot: n floats][ready[8]][done[8]][count][epoch] (uint32 words)
-// opened by every other rank through CUDA IPC.  In each step:
-//   1. the backward's reduction writes this rank's dW into its slot;
-//   2. mlp_peer_allreduce_kernel: every CTA reads the step number
-//      e = epoch + 1 from its own buffer; thread 0 of CTA 0 stores e into
-//      ready[rank] of every rank's buffer (release, system scope); every CTA
-//      waits until its own ready[q] >= e for all q (acquire, bounded), then its
-//      threads sum the slots of ranks 0 .. W-1 in rank order and write the
-//      result.  Every rank adds the same values in the same order, so the sum
-//      is bitwise identical on all ranks (NCCL's ring / tree orders do not
+//   [in: n floats][slot 0: n floats][slot 1: n floats]
+//   [ready[kPeerMaxRanks][kPeerMaxCtas]][epoch[kPeerMaxCtas]] (uint32 words)
+// opened by every other rank through CUDA IPC.  Step e of CTA c (every call
+// launches the same grid; CTA c owns the same float4s every time):
+//   1. the backward's reduction has written this rank's dW into `in`;
+//   2. CTA c copies its float4s of `in` into slot e % 2, then stores e into
+//      ready[rank][c] of every rank's buffer (release, system scope), waits
+//      until its own ready[q][c] >= e for every rank q (acquire, bounded),
+//      and sums slot e % 2 of ranks 0 .. W-1 in rank order over its float4s.
+//      Every rank adds the same values in the same order, so the sum is
+//      bitwise identical on all ranks (NCCL's ring / tree orders do not
 //      promise that);
-//   3. completion: every CTA counts itself done in `count`; CTA 0 then stores
-//      e into done[rank] of every rank's buffer, waits for its own done[q] >= e
-//      and finally sets epoch = e.  So when the kernel returns on a rank, every
-//      rank has finished reading that rank's slot (it may be rewritten by the
-//      next backward, freed, or the process may exit) and no rank will write
-//      into that rank's buffer again in this step.
+//   3. CTA c records e in its epoch word (read by CTA c of the next call).
+// Why two slots and no closing barrier: rank r rewrites slot e % 2 in step
+// e + 2, after its CTA c passed the ready wait of step e + 1; rank q signals
+// that step only from its next kernel, i.e. after it finished reading rank
+// r's slot e % 2 in step e.  So one flag hand-off per step suffices (the
+// first version closed every step with a second, "done" hand-off and a count
+// of finished CTAs).  `in` is never read by the other ranks: the next
+// backward may rewrite it as soon as this kernel returns.  The other ranks
+// may still be reading this rank's slots then, so a buffer is freed only
+// after every rank synchronized its device and met a host barrier.
 // The step number lives in device memory, so the kernel can be replayed from
 // a CUDA graph.  Plain peer loads and stores only (no multicast objects, no
 // TMA).  Every wait is bounded: on expiry the kernel records kDevTimeoutFlag in
@@ -31,6 +36,9 @@
 namespace mlpk {
 
 constexpr int kPeerMaxRanks = 8;
+constexpr int kPeerMaxCtas = 256;  // CTAs of one call (the host caps the grid)
+// 32-bit words after the three float regions
+constexpr int kPeerFlagWords = kPeerMaxRanks * kPeerMaxCtas + kPeerMaxCtas;
 
 struct PeerPtrs {
   float* buf[kPeerMaxRanks];  // every rank's peer buffer (this rank's own included)
@@ -50,11 +58,12 @@ __device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
   return v;
 }
 
-// Bounded wait until every word flags[0 .. world-1] >= epoch (acquire).
-__device__ __forceinline__ bool peer_wait_all(const uint32_t* flags, int world, uint32_t epoch) {
+// Bounded wait until every word flags[q * stride], q < world, is >= epoch
+// (acquire).
+__device__ __forceinline__ bool peer_wait_all(const uint32_t* flags, int stride, int world, uint32_t epoch) {
   const uint64_t t0 = globaltimer_ns();
   for (int q = 0; q < world; ++q) {
-    while (static_cast<int32_t>(ld_relaxed_sys(flags + q) - epoch) < 0) {
+    while (static_cast<int32_t>(ld_relaxed_sys(flags + static_cast<size_t>(q) * stride) - epoch) < 0) {
       if (globaltimer_ns() - t0 > MLPK_WAIT_TIMEOUT_NS) {
         atomicOr(&g_device_status, kDevTimeoutFlag);
         return false;
@@ -65,45 +74,42 @@ __device__ __forceinline__ bool peer_wait_all(const uint32_t* flags, int world, 
   return true;
 }
 
-// Release: everything this thread (and, after a CTA barrier, its CTA) wrote
-// or read before is ordered before the flag stores.
-__device__ __forceinline__ void peer_signal_all(const PeerPtrs& peers, int world, int n, int word,
-                                                uint32_t epoch) {
-  fence_sys();
-  for (int q = 0; q < world; ++q)
-    st_relaxed_sys(reinterpret_cast<uint32_t*>(peers.buf[q] + static_cast<size_t>(n)) + word, epoch);
-}
-
 __global__ void __launch_bounds__(256)
     mlp_peer_allreduce_kernel(PeerPtrs peers, int world, int rank, int n, float* __restrict__ out) {
   pdl_enter();
-  auto words = [&](int q) { return reinterpret_cast<uint32_t*>(peers.buf[q] + static_cast<size_t>(n)); };
-  uint32_t* const ready = words(rank);                  // ready[kPeerMaxRanks]
-  uint32_t* const done = ready + kPeerMaxRanks;         // done[kPeerMaxRanks]
-  uint32_t* const count = ready + 2 * kPeerMaxRanks;    // CTAs finished, all steps
-  uint32_t* const epoch_word = count + 1;               // steps completed
+  const int c = blockIdx.x;
+  auto flags = [&](int q) { return reinterpret_cast<uint32_t*>(peers.buf[q] + 3 * static_cast<size_t>(n)); };
+  uint32_t* const epoch_word = flags(rank) + kPeerMaxRanks * kPeerMaxCtas + c;
   __shared__ int s_ok;
   __shared__ uint32_t s_epoch;
-  if (threadIdx.x == 0) {
-    // epoch only changes at the very end of CTA 0, after every CTA counted itself
-    const uint32_t e = *reinterpret_cast<volatile uint32_t*>(epoch_word) + 1u;
-    s_epoch = e;
-    // this rank's slot was completed by the previous kernel on this stream
-    if (blockIdx.x == 0) peer_signal_all(peers, world, n, rank, e);
-    s_ok = peer_wait_all(ready, world, e) ? 1 : 0;
-  }
+  if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile uint32_t*>(epoch_word) + 1u;
   __syncthreads();
   const uint32_t e = s_epoch;
+  const size_t slot = static_cast<size_t>(n) * (1 + (e & 1u));
+  // n is a multiple of 4 (checked by the host); CTA c's float4s: a grid stride
+  const int i0 = c * blockDim.x + threadIdx.x, stride = gridDim.x * blockDim.x;
+  {
+    const float4* in = reinterpret_cast<const float4*>(peers.buf[rank]);
+    float4* mine = reinterpret_cast<float4*>(peers.buf[rank] + slot);
+    for (int i4 = i0; 4 * i4 < n; i4 += stride) mine[i4] = in[i4];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // release this CTA's copy (the CTA barrier above orders every thread's
+    // stores before this fence), then acquire every rank's
+    fence_sys();
+    for (int q = 0; q < world; ++q) st_relaxed_sys(flags(q) + rank * kPeerMaxCtas + c, e);
+    s_ok = peer_wait_all(flags(rank) + c, kPeerMaxCtas, world, e) ? 1 : 0;
+  }
+  __syncthreads();
   if (s_ok) {
-    // n is a multiple of 4 (checked by the host); grid-stride over float4s
-    // (the host keeps the grid at most one CTA per SM: every CTA is resident)
-    for (int i4 = blockIdx.x * blockDim.x + threadIdx.x; 4 * i4 < n; i4 += gridDim.x * blockDim.x) {
+    for (int i4 = i0; 4 * i4 < n; i4 += stride) {
       // all ranks' loads in flight at once (one NVLink round trip), then the
       // adds in fixed rank order: identical sums on every rank
       float4 v[kPeerMaxRanks];
 #pragma unroll
       for (int q = 0; q < kPeerMaxRanks; ++q)
-        if (q < world) v[q] = __ldcv(reinterpret_cast<const float4*>(peers.buf[q]) + i4);
+        if (q < world) v[q] = __ldcv(reinterpret_cast<const float4*>(peers.buf[q] + slot) + i4);
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int q = 0; q < kPeerMaxRanks; ++q) {
@@ -117,29 +123,9 @@ __global__ void __launch_bounds__(256)
       reinterpret_cast<float4*>(out)[i4] = acc;
     }
   }
-  __syncthreads();  // this CTA's peer reads are complete
-  if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(count, 1u);
-    if (blockIdx.x == 0) {
-      // every CTA of this kernel (count is cumulative over steps) ...
-      const uint32_t target = e * gridDim.x;
-      const uint64_t t0 = globaltimer_ns();
-      bool ok = s_ok != 0;
-      while (ok && static_cast<int32_t>(ld_relaxed_sys(count) - target) < 0) {
-        if (globaltimer_ns() - t0 > MLPK_WAIT_TIMEOUT_NS) {
-          atomicOr(&g_device_status, kDevTimeoutFlag);
-          ok = false;
-        }
-      }
-      // ... then every rank is done with the others' buffers for this step
-      if (ok) {
-        peer_signal_all(peers, world, n, kPeerMaxRanks + rank, e);
-        peer_wait_all(done, world, e);
-      }
-      *reinterpret_cast<volatile uint32_t*>(epoch_word) = e;
-    }
-  }
+  // the step is done for this CTA index (also after a timeout, so that the
+  // step numbers of later calls stay in line with the other ranks')
+  if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(epoch_word) = e;
 }
 
 }  // namespace mlpk

@@ -110,6 +110,7 @@ class PeerGradReducer:
         if n % 4:
             raise ValueError("the gradient length must be a multiple of 4")
         self.n = n
+        self.process_group = process_group
         self.world = dist.get_world_size(process_group)
         self.rank = dist.get_rank(process_group)
         if self.world > _lib.PEER_MAX_RANKS:
@@ -169,11 +170,17 @@ class PeerGradReducer:
         return out
 
     def close(self, sync: bool = True):
-        """Unmap the peers' buffers and free this rank's.  Safe once this rank's
-        last reduction has completed: that kernel returns only after every rank
-        finished reading and writing this rank's buffer."""
+        """Unmap the peers' buffers and free this rank's.  Collective: a rank's
+        last reduction may return while the other ranks still read its buffer,
+        so every rank synchronizes its device and meets the others at a
+        barrier before anything is unmapped or freed (``sync=False``: set-up
+        failures only, before any reduction ran)."""
         if sync:
+            import torch.distributed as dist
+
             torch.cuda.synchronize()
+            if self.world > 1:
+                dist.barrier(group=self.process_group)
         self._local = None
         for p in self._opened:
             self._lib.mlpk_peer_close(ctypes.c_void_p(p))
