@@ -705,8 +705,9 @@ TRAIN_SPECS = {
     # global M = 1,048,576 split over the ranks
     "W256": {"dims": (256, 256, 256, 256), "x_dist": "normal", "x_seed": 4, "strong": True, "wn": False,
              "metric": "fused MLP fwd+bwd rows/s (wide 3L D=H=OUT=256)",
-             "workload": "BASELINE config 5: 3L D=H=OUT=256 training step (streamed weights), "
-                         "fp16 activation storage, global M={G} rows, {M} per GPU"},
+             "workload": "BASELINE config 5: 3L D=H=OUT=256 training step (streamed weights), plain "
+                         "weights (config 5 has no weight norm), fp16 activation storage, global M={G} rows, "
+                         "{M} per GPU"},
 }
 
 
